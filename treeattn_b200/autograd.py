@@ -1,0 +1,177 @@
+"""Autograd functions and the reference-facing entry points.
+
+* ``hierarchical_attention`` -- same signature, argument meaning and errors as the
+  reference op ``treeattn_cuda.hierarchical_attention``
+  (packages/treeattn-cuda/src/treeattn_cuda/_autograd.py:863-915).
+* ``tree_attention`` -- the attn-bench kernel contract ``fn(q, k, v, causal, softmax_scale)``
+  on bshd tensors, including the Haar tree build (attn_bench/baselines/treeattn_cuda.py:24-59)
+  fused into one autograd node.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Literal
+
+import torch
+
+from . import ops
+
+Mode = Literal["deterministic", "stochastic"]
+NUM_SAMPLES_ENV_VAR = "TREEATTN_NUM_SAMPLES"
+_DEFAULT_BLOCK_SIZE = 256
+
+
+class TreeAttentionFunction(torch.autograd.Function):
+    """Stochastic non-causal tree attention on (seq, B, H, D) views.
+
+    forward(q (L,B,H,D), k_int (N-1,B,H,D), v (N,B,H,D), num_samples, max_logit)
+      -> (out (L,B,H,D), weights (L,B,H,S) float32, non-differentiable)
+    Saves q, k_int, v and the sampled leaves / weights (8 bytes per path) for backward.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k_int, v, num_samples, max_logit):
+        res = ops.forward(q, k_int, v, num_samples, max_logit=max_logit)
+        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights)
+        ctx.num_samples = num_samples
+        ctx.max_logit = max_logit
+        ctx.mark_non_differentiable(res.weights)
+        return res.out, res.weights
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_weights):
+        del grad_weights
+        q, k_int, v, leaf, weights = ctx.saved_tensors
+        dq, dk, dv = ops.backward(q, k_int, v, grad_out, leaf, weights, ctx.num_samples,
+                                  max_logit=ctx.max_logit, dk_dtype=k_int.dtype)
+        return dq, dk, dv, None, None
+
+
+class TreeAttentionBshdFunction(torch.autograd.Function):
+    """Tree build + stochastic tree attention on bshd tensors, one autograd node.
+
+    The internal-node keys stay float32 in backward (dk_int is fed to the transposed tree
+    build directly), so dK is rounded to the input dtype once.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None):
+        qv, kv, vv = (t.transpose(0, 1) for t in (q, k, v))  # logical (S, B, H, D) views
+        k_int = ops.tree_build(kv)
+        out = torch.empty_like(q)
+        res = ops.forward(qv, k_int, vv, num_samples, max_logit=max_logit, out=out.transpose(0, 1),
+                          gumbels=gumbels)
+        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights)
+        ctx.num_samples = num_samples
+        ctx.max_logit = max_logit
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k_int, v, leaf, weights = ctx.saved_tensors
+        B, S, H, D = q.shape
+        dq = torch.empty_like(q)
+        dv = torch.empty_like(v)
+        dk_int = torch.empty((B, H, S - 1, D), device=q.device, dtype=torch.float32).permute(2, 0, 1, 3)
+        grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
+        ops.backward(q.transpose(0, 1), k_int, v.transpose(0, 1), grad_out.transpose(0, 1), leaf,
+                     weights, ctx.num_samples, max_logit=ctx.max_logit, dq=dq.transpose(0, 1),
+                     dk=dk_int, dv=dv.transpose(0, 1))
+        dk = torch.empty_like(q)
+        ops.tree_build_backward(dk_int, dk.transpose(0, 1))
+        return dq, dk, dv, None, None, None
+
+
+def hierarchical_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    num_heads: int,
+    is_causal: bool = False,
+    mode: Mode = "stochastic",
+    num_samples: int = 64,
+    *,
+    block_size: int = _DEFAULT_BLOCK_SIZE,
+    max_logit: float = ops.MAX_LOGIT,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Hierarchical (tree) attention: query (L,B,E), key (N-1,B,E), value (N,B,E).
+
+    Returns ``(output (L,B,E), weights (L,B,H,S) float32)``. ``block_size`` is accepted for
+    signature compatibility; the fused kernels have no host-side query blocking.
+    Mirrors treeattn_cuda/_autograd.py:863-915 (stochastic, non-causal).
+    """
+    del block_size
+    if mode != "stochastic":
+        raise NotImplementedError("treeattn_b200 implements mode='stochastic'")
+    if is_causal:
+        raise NotImplementedError("treeattn_b200 implements is_causal=False")
+    if query.dim() != 3 or value.dim() != 3:
+        raise ValueError("query and value must have shape (L, B, E) and (N, B, E)")
+    if num_samples is None or num_samples <= 0:
+        raise ValueError(f"num_samples must be > 0, got {num_samples}")
+    l_q, batch, embed = query.shape
+    num_leaves = value.shape[0]
+    if embed % num_heads != 0:
+        raise ValueError(f"embed_dim={embed} is not divisible by num_heads={num_heads}")
+    width = embed // num_heads
+    if num_leaves > 1 and key.shape[0] != num_leaves - 1:
+        raise ValueError(f"Key tensor length must be N-1 ({num_leaves - 1}), but got {key.shape[0]}.")
+
+    q = query.reshape(l_q, batch, num_heads, width)
+    v = value.reshape(num_leaves, batch, num_heads, width)
+    if num_leaves == 0:
+        out = torch.zeros_like(query)
+        return out, torch.empty((l_q, batch, num_heads, 0), device=query.device, dtype=query.dtype)
+    if num_leaves == 1:
+        # a single leaf: every path ends there (_autograd.py:668-683)
+        out = value.expand(l_q, -1, -1)
+        return out.contiguous(), torch.ones((l_q, batch, num_heads, 1), device=query.device,
+                                            dtype=query.dtype)
+    if not ops.is_power_of_two(num_leaves):
+        raise ValueError(f"treeattn_b200 requires a power-of-two number of leaves, got {num_leaves}")
+    k = key.reshape(num_leaves - 1, batch, num_heads, width)
+    out, weights = TreeAttentionFunction.apply(q, k, v, num_samples, max_logit)
+    return out.reshape(l_q, batch, embed), weights
+
+
+def resolve_num_samples() -> int | None:
+    """``TREEATTN_NUM_SAMPLES`` (attn_bench/baselines/_treeattn_common.py:30-47)."""
+    raw = os.environ.get(NUM_SAMPLES_ENV_VAR, "").strip()
+    if not raw or raw == "0":
+        return None
+    try:
+        n = int(raw)
+    except ValueError as e:
+        raise ValueError(f"{NUM_SAMPLES_ENV_VAR}={raw!r} is not an integer") from e
+    if n < 0:
+        raise ValueError(f"{NUM_SAMPLES_ENV_VAR}={n} must be >= 0")
+    return n or None
+
+
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                   softmax_scale: float | None = None, *, num_samples: int | None = None,
+                   max_logit: float = ops.MAX_LOGIT,
+                   gumbels: torch.Tensor | None = None) -> torch.Tensor:
+    """attn-bench kernel contract: bshd q/k/v (B,S,H,D) -> out (B,S,H,D).
+
+    ``k`` are leaf keys; the internal-node keys are their sequence-axis Haar transform in
+    the reference's layout. ``softmax_scale`` is ignored, as in the reference adapters
+    (baselines/treeattn_cuda.py:25). ``num_samples`` defaults to ``TREEATTN_NUM_SAMPLES``.
+    ``gumbels`` (float32 (log2 S, S, B, H, num_samples, 2)) replaces the generator's noise,
+    for replaying a recorded draw.
+    """
+    del softmax_scale
+    if causal:
+        raise ValueError("treeattn_b200 does not support causal attention yet")
+    if num_samples is None:
+        num_samples = resolve_num_samples()
+    if num_samples is None:
+        raise ValueError("num_samples is required (argument or TREEATTN_NUM_SAMPLES)")
+    if q.dim() != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must share one (B, S, H, D) shape")
+    B, S, H, D = q.shape
+    if not ops.is_power_of_two(S) or S < 2:
+        raise ValueError(f"treeattn_b200 requires power-of-two seqlen, got {S}")
+    q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
+    return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels)

@@ -1,0 +1,237 @@
+// Fused deterministic backward: host entry point and the per-head path sort.
+// The typed kernels live in ta_backward_kernels.cuh (instantiated per dtype in
+// ta_backward_{f32,f16,bf16}.cu so the heavy templates compile in parallel).
+
+#include "ta_backward_kernels.cuh"
+
+namespace ta {
+
+template <typename T> int run_backward_typed(BwdParams& p, cudaStream_t st);
+extern template int run_backward_typed<float>(BwdParams&, cudaStream_t);
+extern template int run_backward_typed<__half>(BwdParams&, cudaStream_t);
+extern template int run_backward_typed<__nv_bfloat16>(BwdParams&, cudaStream_t);
+
+// ---------------------------------------------------------------------------------------
+// 2. segmented stable LSD radix sort of (key, value) records, one segment per head
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSortThreads) sort_hist_kernel(const BwdParams p, int src, int shift) {
+  __shared__ uint32_t cnt[kRadix];
+  const int seg = blockIdx.x / p.tiles_per_seg;
+  const int tile = blockIdx.x - seg * p.tiles_per_seg;
+  for (int i = threadIdx.x; i < kRadix; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t base = (int64_t)seg * p.P + (int64_t)tile * kSortTile;
+  const int64_t end = min((int64_t)(tile + 1) * kSortTile, p.P) - (int64_t)tile * kSortTile;
+  for (int i = threadIdx.x; i < end; i += blockDim.x)
+    atomicAdd(&cnt[(p.keys[src][base + i] >> shift) & (kRadix - 1)], 1u);
+  __syncthreads();
+  for (int d = threadIdx.x; d < kRadix; d += blockDim.x)
+    p.hist[((int64_t)seg * kRadix + d) * p.tiles_per_seg + tile] = cnt[d];
+}
+
+// exclusive scan of one segment's histogram in (digit, tile) order
+__global__ void __launch_bounds__(1024) sort_scan_kernel(const BwdParams p) {
+  __shared__ uint32_t warp_tot[32];
+  __shared__ uint32_t carry;
+  const int seg = blockIdx.x;
+  uint32_t* hh = p.hist + (int64_t)seg * kRadix * p.tiles_per_seg;
+  const int64_t n = (int64_t)kRadix * p.tiles_per_seg;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t base = 0; base < n; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const uint32_t v = i < n ? hh[i] : 0u;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0u;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      warp_tot[lane] = t;  // inclusive
+    }
+    __syncthreads();
+    const uint32_t before = carry + (warp > 0 ? warp_tot[warp - 1] : 0u) + x - v;
+    if (i < n) hh[i] = before;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = before + v;
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kSortThreads) sort_scatter_kernel(const BwdParams p, int src, int shift) {
+  constexpr int kWarps = kSortThreads / 32;
+  constexpr int kPerWarp = kSortTile / kWarps;  // 256 records
+  __shared__ uint32_t wcnt[kWarps][kRadix];
+  const int seg = blockIdx.x / p.tiles_per_seg;
+  const int tile = blockIdx.x - seg * p.tiles_per_seg;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < kWarps * kRadix; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t tbase = (int64_t)tile * kSortTile;
+  const int64_t base = (int64_t)seg * p.P + tbase;
+  const int64_t nvalid = min((int64_t)kSortTile, p.P - tbase);
+  // per-warp digit counts
+  uint32_t key[kPerWarp / 32], val[kPerWarp / 32];
+  int dig[kPerWarp / 32];
+#pragma unroll
+  for (int r = 0; r < kPerWarp / 32; ++r) {
+    const int64_t i = (int64_t)warp * kPerWarp + r * 32 + lane;
+    if (i < nvalid) {
+      key[r] = p.keys[src][base + i];
+      val[r] = p.vals[src][base + i];
+      dig[r] = (key[r] >> shift) & (kRadix - 1);
+      atomicAdd(&wcnt[warp][dig[r]], 1u);
+    } else {
+      dig[r] = kRadix;  // sentinel: not written
+    }
+  }
+  __syncthreads();
+  // exclusive scan over warps per digit, plus the global (digit, tile) offset
+  for (int d = threadIdx.x; d < kRadix; d += blockDim.x) {
+    uint32_t run = p.hist[((int64_t)seg * kRadix + d) * p.tiles_per_seg + tile];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t c = wcnt[w][d];
+      wcnt[w][d] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  uint32_t* dk = p.keys[src ^ 1] + (int64_t)seg * p.P;
+  uint32_t* dv = p.vals[src ^ 1] + (int64_t)seg * p.P;
+#pragma unroll
+  for (int r = 0; r < kPerWarp / 32; ++r) {
+    const unsigned same = __match_any_sync(0xffffffffu, dig[r]);
+    const int leader = __ffs(same) - 1;
+    if (dig[r] < kRadix) {
+      const uint32_t pos = wcnt[warp][dig[r]] + __popc(same & lt_mask);
+      dk[pos] = key[r];
+      dv[pos] = val[r];
+    }
+    __syncwarp();
+    if (lane == leader && dig[r] < kRadix) wcnt[warp][dig[r]] += __popc(same);
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+struct BwdLayout {
+  size_t keys[2], vals[2], gl, hist, partial, flags, total;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static BwdLayout bwd_layout(const ta_shape* s) {
+  BwdLayout w{};
+  const int64_t HB = s->batch * s->num_heads;
+  const int64_t P = s->num_queries * s->num_samples;
+  const int ln = floor_log2(s->num_leaves);
+  const int64_t tiles = (P + kSortTile - 1) / kSortTile;
+  const int64_t chunks = HB * ((P + kChunk - 1) / kChunk);
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+  w.keys[0] = take(HB * P * 4);
+  w.keys[1] = take(HB * P * 4);
+  w.vals[0] = take(HB * P * 4);
+  w.vals[1] = take(HB * P * 4);
+  w.gl = take(HB * P * ln * 4);
+  w.hist = take(HB * kRadix * tiles * 4);
+  w.partial = take(chunks * (ln + 1) * 2 * s->head_dim * 4);
+  w.flags = take(chunks * (ln + 1) * 2);
+  w.total = off;
+  return w;
+}
+
+
+int run_sort(BwdParams& p, cudaStream_t st) {
+  const int passes = (p.log_n + kRadixBits - 1) / kRadixBits;
+  const unsigned tiles = (unsigned)(p.B * p.H * p.tiles_per_seg);
+  int src = 0;
+  for (int ps = 0; ps < passes; ++ps) {
+    sort_hist_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
+    sort_scan_kernel<<<p.B * p.H, 1024, 0, st>>>(p);
+    sort_scatter_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
+    src ^= 1;
+  }
+  p.sorted_buf = src;
+  return check_launch("backward path sort");
+}
+
+}  // namespace ta
+
+using namespace ta;
+
+extern "C" size_t ta_backward_workspace_size(const ta_shape* shape) {
+  if (check_shape(shape, true) != TA_OK) return 0;
+  return bwd_layout(shape).total;
+}
+
+extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                           ta_layout kl, const void* v, ta_layout vl, const void* gout,
+                           ta_layout gl, const int32_t* leaf, const float* weights, void* dq,
+                           ta_layout dql, void* dk, ta_layout dkl, int32_t dk_dtype, void* dv,
+                           ta_layout dvl, void* ws, size_t ws_bytes, ta_stream_t stream) {
+  int rc = check_shape(shape, true);
+  if (rc) return rc;
+  const int es = dtype_size(shape->dtype);
+  if (dk_dtype != TA_F32 && dk_dtype != shape->dtype)
+    return fail(TA_ERR_INVALID, "dk_dtype must be TA_F32 or the input dtype");
+  if ((rc = check_view("q", q, ql, es, false)) || (rc = check_view("k_int", k, kl, es, false)) ||
+      (rc = check_view("v", v, vl, es, false)) || (rc = check_view("grad_out", gout, gl, es, false)) ||
+      (rc = check_view("dq", dq, dql, es, false)) ||
+      (rc = check_view("dk", dk, dkl, dtype_size(dk_dtype), false)) ||
+      (rc = check_view("dv", dv, dvl, es, false)))
+    return rc;
+  if (!leaf || !weights) return fail(TA_ERR_INVALID, "leaf and weights must not be NULL");
+  if (shape->num_queries * shape->num_samples >= (1ll << 31))
+    return fail(TA_ERR_UNSUPPORTED, "L * S must be < 2^31");
+  const BwdLayout w = bwd_layout(shape);
+  if (ws == nullptr || ws_bytes < w.total)
+    return fail(TA_ERR_WORKSPACE, "backward workspace too small (%zu < %zu)", ws_bytes, w.total);
+  BwdParams p{};
+  p.q = (const char*)q; p.k = (const char*)k; p.v = (const char*)v; p.dout = (const char*)gout;
+  p.dq = (char*)dq; p.dk = (char*)dk; p.dv = (char*)dv;
+  p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
+  p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
+  p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
+  p.gs = gl.seq; p.gb = gl.batch; p.gh = gl.head;
+  p.dqs = dql.seq; p.dqb = dql.batch; p.dqh = dql.head;
+  p.dks = dkl.seq; p.dkb = dkl.batch; p.dkh = dkl.head;
+  p.dvs = dvl.seq; p.dvb = dvl.batch; p.dvh = dvl.head;
+  p.leaf = leaf; p.weights = weights;
+  char* base = (char*)ws;
+  p.keys[0] = (uint32_t*)(base + w.keys[0]); p.keys[1] = (uint32_t*)(base + w.keys[1]);
+  p.vals[0] = (uint32_t*)(base + w.vals[0]); p.vals[1] = (uint32_t*)(base + w.vals[1]);
+  p.gl = (float*)(base + w.gl); p.hist = (uint32_t*)(base + w.hist);
+  p.partial = (float*)(base + w.partial); p.flags = (uint8_t*)(base + w.flags);
+  p.B = (int32_t)shape->batch; p.L = (int32_t)shape->num_queries; p.H = (int32_t)shape->num_heads;
+  p.S = (int32_t)shape->num_samples; p.N = (int32_t)shape->num_leaves;
+  p.D = (int32_t)shape->head_dim; p.log_n = floor_log2(shape->num_leaves);
+  p.nchunks = (int32_t)(shape->head_dim * es / 16);
+  p.dk_f32 = dk_dtype == TA_F32 ? 1 : 0;
+  p.P = shape->num_queries * shape->num_samples;
+  p.tiles_per_seg = (int32_t)((p.P + kSortTile - 1) / kSortTile);
+  p.chunks_per_seg = (int32_t)((p.P + kChunk - 1) / kChunk);
+  p.max_logit = shape->max_logit;
+  if (p.log_n > 30) return fail(TA_ERR_UNSUPPORTED, "tree too deep");
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (shape->dtype) {
+    case TA_F32: rc = run_backward_typed<float>(p, st); break;
+    case TA_F16: rc = run_backward_typed<__half>(p, st); break;
+    default: rc = run_backward_typed<__nv_bfloat16>(p, st); break;
+  }
+  return rc;
+}

@@ -1,0 +1,126 @@
+// Shared device/host helpers for the treeattn_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/treeattn_b200.h"
+
+namespace ta {
+
+// ---------------------------------------------------------------------------------------
+// error reporting (host)
+// ---------------------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int check_view(const char* name, const void* ptr, ta_layout lay, int esize, bool allow_null);
+int check_shape(const ta_shape* s, bool need_pow2);
+int pick_cpl(int nchunks);
+
+// ---------------------------------------------------------------------------------------
+// element types
+// ---------------------------------------------------------------------------------------
+inline int dtype_size(int32_t dt) { return dt == TA_F32 ? 4 : 2; }
+
+// Rows are moved in 16-byte chunks; a chunk holds EPC elements.
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int EPC = 4;
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+  __device__ __forceinline__ static float round(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int EPC = 8;
+  __device__ __forceinline__ static void unpack2(uint32_t w, float* f) {
+    f[0] = __uint_as_float(w << 16);
+    f[1] = __uint_as_float(w & 0xffff0000u);
+  }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    unpack2(u.x, f); unpack2(u.y, f + 2); unpack2(u.z, f + 4); unpack2(u.w, f + 6);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+template <> struct Elem<__half> {
+  static constexpr int EPC = 8;
+  __device__ __forceinline__ static void unpack2(uint32_t w, float* f) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    float2 t = __half22float2(h);
+    f[0] = t.x; f[1] = t.y;
+  }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    unpack2(u.x, f); unpack2(u.y, f + 2); unpack2(u.z, f + 4); unpack2(u.w, f + 6);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float round(float x) {
+    return __half2float(__float2half_rn(x));
+  }
+};
+
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+// Streaming load that is not kept in L1 (rows read once).
+__device__ __forceinline__ uint4 ld16_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st16(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// ---------------------------------------------------------------------------------------
+// math shared by forward and backward (accurate libm calls; no fast-math anywhere)
+// ---------------------------------------------------------------------------------------
+// (logsigmoid(x), logsigmoid(-x)) = (min(0,x) - t, min(0,-x) - t), t = log1p(exp(-|x|)):
+// the same expression torch's log_sigmoid kernel evaluates.
+__device__ __forceinline__ void log_sigmoid_pair(float x, float& left, float& right) {
+  const float t = log1pf(expf(-fabsf(x)));
+  left = fminf(0.0f, x) - t;
+  right = fminf(0.0f, -x) - t;
+}
+
+__device__ __forceinline__ float clamp_logit(float x, float m) {
+  return x > m ? m : (x < -m ? -m : x);
+}
+
+// Path position of a leaf: heap node of the final step is (1 << log_n) - 1 + bits, with
+// the direction taken at depth d in bit (log_n - 1 - d) of `bits`.
+__device__ __forceinline__ int64_t heap_node(int depth, uint32_t bits, int log_n) {
+  return ((int64_t)1 << depth) - 1 + (int64_t)(bits >> (log_n - depth));
+}
+
+__host__ __device__ inline int floor_log2(int64_t n) {
+  int r = 0;
+  while (n > 1) { n >>= 1; ++r; }
+  return r;
+}
+
+}  // namespace ta

@@ -1,0 +1,502 @@
+// Fused stochastic tree-attention forward for sm_100a.
+//
+// Work decomposition: one 4-lane group per (query, batch, head); a CTA of 256 threads owns
+// 64 consecutive queries of one (batch, head), so concurrently resident CTAs walk the same
+// head's tree and its rows stay hot in L2. Each lane holds a quarter of q (in 16-byte
+// chunks, interleaved so the group reads 64 contiguous bytes per load), the group walks
+// four sampled paths at once (four independent row gathers in flight per depth), and lane
+// t draws the Gumbel pair of the t-th path of the four.
+//
+// Per depth (reference: _tree_mha.py:99-119, _autograd.py:187-217,
+// sample_non_causal_paths.cu:54-128):
+//   s = clamp(q . k[node], +-max_logit)            (float32 accumulation)
+//   lp = (logsigmoid(s), logsigmoid(-s))
+//   dir = 1 iff lp_R + G_R > lp_L + G_L             (argmax, ties to the left)
+//   acc += lp[dir]; node = 2 node + 1 + dir
+// then w = exp(lp - logsumexp(lp)) over the S paths of a query (_autograd.py:495-498) and
+// out = sum_s w_s v[leaf_s] (weighted_value_sum.cu:8-47) -- all in one launch.
+
+#include <stdio.h>
+
+#include "ta_common.cuh"
+#include "ta_rng.cuh"
+
+namespace ta {
+
+constexpr int kFwdThreads = 256;
+constexpr int kFwdGroups = kFwdThreads / 4;  // queries per CTA
+
+enum FwdMode { kFull = 0, kSampleOnly = 1, kReplay = 2, kReplaySoftmax = 3 };
+
+struct FwdParams {
+  const char* q;
+  const char* k;
+  const char* v;
+  char* out;
+  int64_t qs, qb, qh;  // element strides (seq, batch, head)
+  int64_t ks, kb, kh;
+  int64_t vs, vb, vh;
+  int64_t os, ob, oh;
+  int32_t* leaf;
+  float* weights;   // kFull / kReplaySoftmax: weights; kSampleOnly / kReplay: log-probs
+  uint8_t* packed;  // written (kFull, kSampleOnly) or read (kReplay*)
+  const float* gumbels;
+  uint64_t seed, offset, offset_step;
+  FastDiv stride;
+  int32_t B, L, H, S, N, log_n, nchunks, pbytes;
+  float max_logit;
+  int32_t mode;
+};
+
+template <typename T, int CPL>
+__global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
+  using E = Elem<T>;
+  constexpr int EPC = E::EPC;
+  constexpr int NE = CPL * EPC;  // elements of a row held by one lane
+  extern __shared__ float smem[];
+
+  const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
+  const int bh = blockIdx.x / ltiles;
+  const int lt = blockIdx.x - bh * ltiles;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int g = threadIdx.x >> 2;
+  const int t4 = threadIdx.x & 3;
+  const int l = lt * kFwdGroups + g;
+  if (l >= p.L) return;  // whole group leaves together
+  const unsigned gmask = 0xFu << (threadIdx.x & 28);
+
+  float* s_lp = smem + g * p.S;                                   // [S] log-prob then weight
+  int32_t* s_leaf = reinterpret_cast<int32_t*>(smem + kFwdGroups * p.S) + g * p.S;  // [S]
+
+  const int64_t K = (int64_t)p.N - 1;
+  const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
+
+  // q slice of this lane
+  float qf[NE];
+  {
+    const char* qrow = p.q + ((int64_t)l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = i * 4 + t4;
+      if (c < p.nchunks) {
+        E::unpack(ldg16(qrow + c * 16), qf + i * EPC);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) qf[i * EPC + e] = 0.0f;
+      }
+    }
+  }
+  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
+  const int64_t kstride = p.ks * (int64_t)sizeof(T);
+  const bool replay = p.mode >= kReplay;
+
+  for (int s0 = 0; s0 < p.S; s0 += 4) {
+    const int ns = min(4, p.S - s0);
+    int64_t node[4] = {0, 0, 0, 0};
+    float lp = 0.0f;  // path s0 + t4
+    const uint32_t jm = j0 + s0 + t4;
+    for (int depth = 0; depth < p.log_n; ++depth) {
+      float dot[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        dot[t] = 0.0f;
+        if (t < ns) {
+          const char* krow = kbase + node[t] * kstride;
+          uint4 raw[CPL];
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            const int c = i * 4 + t4;
+            raw[i] = (c < p.nchunks) ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            float kf[EPC];
+            E::unpack(raw[i], kf);
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) dot[t] = fmaf(qf[i * EPC + e], kf[e], dot[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        dot[t] += __shfl_xor_sync(gmask, dot[t], 1, 4);
+        dot[t] += __shfl_xor_sync(gmask, dot[t], 2, 4);
+      }
+      const float mine = t4 == 0 ? dot[0] : (t4 == 1 ? dot[1] : (t4 == 2 ? dot[2] : dot[3]));
+      float lpl, lpr;
+      log_sigmoid_pair(clamp_logit(mine, p.max_logit), lpl, lpr);
+      int dir = 0;
+      if (t4 < ns) {
+        if (replay) {
+          const uint8_t byte = p.packed[(int64_t)jm * p.pbytes + (depth >> 3)];
+          dir = (byte >> (depth & 7)) & 1;
+        } else {
+          float gl, gr;
+          if (p.gumbels != nullptr) {
+            const float* gp = p.gumbels + ((int64_t)depth * p.L * p.B * p.H * p.S + jm) * 2;
+            gl = gp[0];
+            gr = gp[1];
+          } else {
+            const uint64_t off = p.offset + (uint64_t)depth * p.offset_step;
+            gl = torch_gumbel(p.seed, off, 2u * jm, p.stride);
+            gr = torch_gumbel(p.seed, off, 2u * jm + 1u, p.stride);
+          }
+          dir = (lpr + gr > lpl + gl) ? 1 : 0;
+        }
+        lp += dir ? lpr : lpl;
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int d = __shfl_sync(gmask, dir, t, 4);
+        node[t] = 2 * node[t] + 1 + d;
+      }
+    }
+    if (t4 < ns) {
+      const int64_t nm = t4 == 0 ? node[0] : (t4 == 1 ? node[1] : (t4 == 2 ? node[2] : node[3]));
+      s_lp[s0 + t4] = lp;
+      s_leaf[s0 + t4] = (int32_t)(nm - K);
+    }
+  }
+  __syncwarp(gmask);
+
+  if (p.mode == kSampleOnly || p.mode == kReplay) {
+    for (int s = t4; s < p.S; s += 4) {
+      p.weights[j0 + s] = s_lp[s];
+      p.leaf[j0 + s] = s_leaf[s];
+    }
+  } else {
+    // softmax over the S paths: lp - logsumexp(lp), exp
+    float m = -INFINITY;
+    for (int s = t4; s < p.S; s += 4) m = fmaxf(m, s_lp[s]);
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 1, 4));
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 2, 4));
+    float sum = 0.0f;
+    for (int s = 0; s < p.S; ++s) sum += expf(s_lp[s] - m);  // same order on every lane
+    const float lse = m + logf(sum);
+    __syncwarp(gmask);
+    for (int s = t4; s < p.S; s += 4) {
+      const float w = expf(s_lp[s] - lse);
+      s_lp[s] = w;
+      if (p.weights) p.weights[j0 + s] = w;
+      if (p.leaf) p.leaf[j0 + s] = s_leaf[s];
+    }
+    __syncwarp(gmask);
+  }
+  if (p.packed != nullptr && !replay) {
+    const int64_t base_node = ((int64_t)1 << p.log_n) - 1;
+    for (int s = t4; s < p.S; s += 4) {
+      const uint32_t bits = (uint32_t)((int64_t)s_leaf[s] + K - base_node);
+      for (int pb = 0; pb < p.pbytes; ++pb) {
+        uint32_t byte = 0;
+        for (int d = pb * 8; d < min(p.log_n, pb * 8 + 8); ++d)
+          byte |= ((bits >> (p.log_n - 1 - d)) & 1u) << (d & 7);
+        p.packed[(int64_t)(j0 + s) * p.pbytes + pb] = (uint8_t)byte;
+      }
+    }
+  }
+  if (p.mode != kFull) return;
+
+  // out[l,b,h] = sum_s w_s v[leaf_s]
+  float acc[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
+  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
+  const int64_t vstride = p.vs * (int64_t)sizeof(T);
+  for (int s = 0; s < p.S; ++s) {
+    const float w = s_lp[s];
+    int64_t lf = s_leaf[s];
+    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+    const char* vrow = vbase + lf * vstride;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = i * 4 + t4;
+      if (c < p.nchunks) {
+        float vf[EPC];
+        E::unpack(ldg16(vrow + c * 16), vf);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w, vf[e], acc[i * EPC + e]);
+      }
+    }
+  }
+  char* orow = p.out + ((int64_t)l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = i * 4 + t4;
+    if (c < p.nchunks) st16(orow + c * 16, E::pack(acc + i * EPC));
+  }
+}
+
+// out = sum_s w_s v[clamp(leaf_s)] for externally supplied leaves / weights.
+template <typename T, int CPL>
+__global__ void __launch_bounds__(kFwdThreads) value_sum_kernel(const FwdParams p) {
+  using E = Elem<T>;
+  constexpr int EPC = E::EPC;
+  constexpr int NE = CPL * EPC;
+  const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
+  const int bh = blockIdx.x / ltiles;
+  const int lt = blockIdx.x - bh * ltiles;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int g = threadIdx.x >> 2;
+  const int t4 = threadIdx.x & 3;
+  const int l = lt * kFwdGroups + g;
+  if (l >= p.L) return;
+  const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
+  float acc[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
+  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
+  for (int s = 0; s < p.S; ++s) {
+    const float w = p.weights[j0 + s];
+    int64_t lf = p.leaf[j0 + s];
+    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+    const char* vrow = vbase + lf * p.vs * (int64_t)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = i * 4 + t4;
+      if (c < p.nchunks) {
+        float vf[EPC];
+        E::unpack(ldg16(vrow + c * 16), vf);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w, vf[e], acc[i * EPC + e]);
+      }
+    }
+  }
+  char* orow = p.out + ((int64_t)l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = i * 4 + t4;
+    if (c < p.nchunks) st16(orow + c * 16, E::pack(acc + i * EPC));
+  }
+}
+
+__global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t numel,
+                                                          uint64_t seed, uint64_t offset,
+                                                          FastDiv stride) {
+  const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e < numel) out[e] = torch_gumbel(seed, offset, e, stride);
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+
+int pick_cpl(int nchunks) {
+  const int need = (nchunks + 3) / 4;
+  const int opts[] = {1, 2, 3, 4, 6, 8};
+  for (int c : opts)
+    if (c >= need) return c;
+  return -1;
+}
+
+static bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
+
+int check_view(const char* name, const void* ptr, ta_layout lay, int esize, bool allow_null) {
+  if (ptr == nullptr) {
+    if (allow_null) return TA_OK;
+    return fail(TA_ERR_INVALID, "%s is NULL", name);
+  }
+  if (!aligned16(ptr)) return fail(TA_ERR_INVALID, "%s is not 16-byte aligned", name);
+  if ((lay.seq * esize) % 16 || (lay.batch * esize) % 16 || (lay.head * esize) % 16)
+    return fail(TA_ERR_INVALID, "%s strides (%lld,%lld,%lld) are not 16-byte multiples", name,
+                (long long)lay.seq, (long long)lay.batch, (long long)lay.head);
+  return TA_OK;
+}
+
+int check_shape(const ta_shape* s, bool need_pow2) {
+  if (s == nullptr) return fail(TA_ERR_INVALID, "shape is NULL");
+  if (s->dtype != TA_F32 && s->dtype != TA_F16 && s->dtype != TA_BF16)
+    return fail(TA_ERR_INVALID, "unknown dtype %d", s->dtype);
+  if (s->batch <= 0 || s->num_queries <= 0 || s->num_heads <= 0 || s->head_dim <= 0 ||
+      s->num_samples <= 0)
+    return fail(TA_ERR_INVALID, "batch, num_queries, num_heads, head_dim and num_samples must be > 0");
+  if (s->num_leaves < 2) return fail(TA_ERR_INVALID, "num_leaves must be >= 2 (got %lld)",
+                                     (long long)s->num_leaves);
+  if (need_pow2 && (s->num_leaves & (s->num_leaves - 1)))
+    return fail(TA_ERR_UNSUPPORTED, "num_leaves must be a power of two (got %lld)",
+                (long long)s->num_leaves);
+  if (s->num_leaves > (1ll << 30)) return fail(TA_ERR_UNSUPPORTED, "num_leaves > 2^30");
+  const int es = dtype_size(s->dtype);
+  if ((s->head_dim * es) % 16) return fail(TA_ERR_UNSUPPORTED,
+      "head_dim * element size must be a multiple of 16 bytes (head_dim=%lld)", (long long)s->head_dim);
+  if (pick_cpl((int)(s->head_dim * es / 16)) < 0)
+    return fail(TA_ERR_UNSUPPORTED, "head_dim %lld too large", (long long)s->head_dim);
+  if (s->num_samples > 256) return fail(TA_ERR_UNSUPPORTED, "num_samples > 256");
+  const int64_t draws = s->num_queries * s->batch * s->num_heads * s->num_samples * 2;
+  if (draws >= (1ll << 31)) return fail(TA_ERR_UNSUPPORTED, "L*B*H*S*2 must be < 2^31");
+  if (!(s->max_logit > 0.0f)) return fail(TA_ERR_INVALID, "max_logit must be > 0");
+  return TA_OK;
+}
+
+template <typename T, int CPL>
+static void launch_fwd(const FwdParams& p, cudaStream_t st, bool value_only) {
+  const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
+  const dim3 grid((unsigned)(ltiles * p.B * p.H));
+  if (value_only) {
+    value_sum_kernel<T, CPL><<<grid, kFwdThreads, 0, st>>>(p);
+    return;
+  }
+  const size_t smem = (size_t)kFwdGroups * p.S * 8;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(fwd_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  fwd_kernel<T, CPL><<<grid, kFwdThreads, smem, st>>>(p);
+}
+
+template <typename T>
+static int dispatch_cpl(const FwdParams& p, cudaStream_t st, bool value_only) {
+  switch (pick_cpl(p.nchunks)) {
+    case 1: launch_fwd<T, 1>(p, st, value_only); break;
+    case 2: launch_fwd<T, 2>(p, st, value_only); break;
+    case 3: launch_fwd<T, 3>(p, st, value_only); break;
+    case 4: launch_fwd<T, 4>(p, st, value_only); break;
+    case 6: launch_fwd<T, 6>(p, st, value_only); break;
+    case 8: launch_fwd<T, 8>(p, st, value_only); break;
+    default: return fail(TA_ERR_UNSUPPORTED, "head_dim too large");
+  }
+  return check_launch("tree-attention forward");
+}
+
+static int run_fwd(const FwdParams& p, int32_t dtype, cudaStream_t st, bool value_only) {
+  if (p.L == 0) return TA_OK;
+  switch (dtype) {
+    case TA_F32: return dispatch_cpl<float>(p, st, value_only);
+    case TA_F16: return dispatch_cpl<__half>(p, st, value_only);
+    case TA_BF16: return dispatch_cpl<__nv_bfloat16>(p, st, value_only);
+  }
+  return fail(TA_ERR_INVALID, "unknown dtype");
+}
+
+static void fill_common(FwdParams& p, const ta_shape* s) {
+  p.B = (int32_t)s->batch;
+  p.L = (int32_t)s->num_queries;
+  p.H = (int32_t)s->num_heads;
+  p.S = (int32_t)s->num_samples;
+  p.N = (int32_t)s->num_leaves;
+  p.log_n = floor_log2(s->num_leaves);
+  p.nchunks = (int32_t)(s->head_dim * dtype_size(s->dtype) / 16);
+  p.pbytes = (p.log_n + 7) / 8;
+  p.max_logit = s->max_logit;
+}
+
+static int fill_rng(FwdParams& p, const ta_rng* rng, const float* gumbels) {
+  p.gumbels = gumbels;
+  if (gumbels == nullptr) {
+    if (rng == nullptr) return fail(TA_ERR_INVALID, "rng is NULL and no gumbels were given");
+    if (rng->draw_stride <= 0 || rng->draw_stride >= (1ll << 31) || (rng->offset & 3) ||
+        (rng->offset_step & 3))
+      return fail(TA_ERR_INVALID, "invalid rng (draw_stride %lld, offset %llu, step %llu)",
+                  (long long)rng->draw_stride, (unsigned long long)rng->offset,
+                  (unsigned long long)rng->offset_step);
+    p.seed = rng->seed;
+    p.offset = rng->offset;
+    p.offset_step = rng->offset_step;
+    p.stride.init((uint32_t)rng->draw_stride);
+  } else {
+    p.stride.init(1);
+  }
+  return TA_OK;
+}
+
+}  // namespace ta
+
+using namespace ta;
+
+extern "C" int ta_forward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                          ta_layout kl, const void* v, ta_layout vl, void* out, ta_layout ol,
+                          const ta_rng* rng, const float* gumbels, int32_t* leaf, float* weights,
+                          uint8_t* packed, ta_stream_t stream) {
+  int rc = check_shape(shape, true);
+  if (rc) return rc;
+  const int es = dtype_size(shape->dtype);
+  if ((rc = check_view("q", q, ql, es, false)) || (rc = check_view("k_int", k, kl, es, false)) ||
+      (rc = check_view("v", v, vl, es, false)) || (rc = check_view("out", out, ol, es, false)))
+    return rc;
+  FwdParams p{};
+  fill_common(p, shape);
+  if ((rc = fill_rng(p, rng, gumbels))) return rc;
+  p.q = (const char*)q; p.k = (const char*)k; p.v = (const char*)v; p.out = (char*)out;
+  p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
+  p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
+  p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
+  p.os = ol.seq; p.ob = ol.batch; p.oh = ol.head;
+  p.leaf = leaf; p.weights = weights; p.packed = packed;
+  p.mode = kFull;
+  return run_fwd(p, shape->dtype, (cudaStream_t)stream, false);
+}
+
+extern "C" int ta_sample_paths(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                               ta_layout kl, const ta_rng* rng, const float* gumbels,
+                               int32_t* leaf, float* log_prob, uint8_t* packed,
+                               ta_stream_t stream) {
+  int rc = check_shape(shape, false);
+  if (rc) return rc;
+  const int es = dtype_size(shape->dtype);
+  if ((rc = check_view("q", q, ql, es, false)) || (rc = check_view("k_int", k, kl, es, false)))
+    return rc;
+  if (!leaf || !log_prob) return fail(TA_ERR_INVALID, "leaf and log_prob must not be NULL");
+  FwdParams p{};
+  fill_common(p, shape);
+  if ((rc = fill_rng(p, rng, gumbels))) return rc;
+  p.q = (const char*)q; p.k = (const char*)k;
+  p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
+  p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
+  p.leaf = leaf; p.weights = log_prob; p.packed = packed;
+  p.mode = kSampleOnly;
+  return run_fwd(p, shape->dtype, (cudaStream_t)stream, false);
+}
+
+extern "C" int ta_replay_paths(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                               ta_layout kl, const uint8_t* packed, int32_t softmax,
+                               int32_t* leaf, float* out_f, ta_stream_t stream) {
+  int rc = check_shape(shape, false);
+  if (rc) return rc;
+  const int es = dtype_size(shape->dtype);
+  if ((rc = check_view("q", q, ql, es, false)) || (rc = check_view("k_int", k, kl, es, false)))
+    return rc;
+  if (!leaf || !out_f || !packed)
+    return fail(TA_ERR_INVALID, "packed, leaf and output must not be NULL");
+  FwdParams p{};
+  fill_common(p, shape);
+  p.stride.init(1);
+  p.q = (const char*)q; p.k = (const char*)k;
+  p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
+  p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
+  p.leaf = leaf; p.weights = out_f; p.packed = const_cast<uint8_t*>(packed);
+  p.mode = softmax ? kReplaySoftmax : kReplay;
+  return run_fwd(p, shape->dtype, (cudaStream_t)stream, false);
+}
+
+extern "C" int ta_weighted_value_sum(const ta_shape* shape, const void* v, ta_layout vl,
+                                     const int32_t* leaf, const float* weights, void* out,
+                                     ta_layout ol, ta_stream_t stream) {
+  int rc = check_shape(shape, false);
+  if (rc) return rc;
+  const int es = dtype_size(shape->dtype);
+  if ((rc = check_view("v", v, vl, es, false)) || (rc = check_view("out", out, ol, es, false)))
+    return rc;
+  if (!leaf || !weights) return fail(TA_ERR_INVALID, "leaf and weights must not be NULL");
+  FwdParams p{};
+  fill_common(p, shape);
+  p.v = (const char*)v; p.out = (char*)out;
+  p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
+  p.os = ol.seq; p.ob = ol.batch; p.oh = ol.head;
+  p.leaf = const_cast<int32_t*>(leaf); p.weights = const_cast<float*>(weights);
+  return run_fwd(p, shape->dtype, (cudaStream_t)stream, true);
+}
+
+extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth,
+                              ta_stream_t stream) {
+  if (!out || !rng || numel < 0 || numel >= (1ll << 31) || depth < 0)
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill: invalid arguments");
+  if (rng->draw_stride <= 0 || rng->draw_stride >= (1ll << 31) || (rng->offset & 3) ||
+      (rng->offset_step & 3))
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill: invalid rng");
+  if (numel == 0) return TA_OK;
+  FastDiv fd;
+  fd.init((uint32_t)rng->draw_stride);
+  const unsigned grid = (unsigned)((numel + 255) / 256);
+  gumbel_fill_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      out, (uint32_t)numel, rng->seed, rng->offset + (uint64_t)depth * rng->offset_step, fd);
+  return check_launch("gumbel fill");
+}
