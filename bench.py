@@ -1,0 +1,398 @@
+#!/usr/bin/env python
+"""Benchmark: fwd+bwd tokens/s of stochastic tree attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward + backward pass of the attn-bench kernel contract
+``tree_attention(q, k, v)`` on bshd bf16 tensors: Haar tree build from k, fused Gumbel-max
+path sampling + softmax + value gather, deterministic backward (dq, dk, dv) and the
+transposed tree build. Workload (BASELINE.json metric "S=16k, d=128 bf16"): B=1 per GPU,
+S=16384, H=16, d=128, 8 sampled paths per query, reference tree semantics (binary tree, one
+token per leaf). Inputs q, k, v, grad_out ~ N(0, 1) from a seeded CUDA generator.
+
+N > 1 (torchrun, one process per GPU, NCCL): the (batch, head) trees are independent, so
+every rank runs its own batch element with no data-path collective (weak scaling); the
+timed region is bracketed by barriers and the max over ranks is reported.
+
+``--impl reference`` times the CPU oracle (numpy restatement of the reference, forked over
+all host cores by head) on a bounded sample of the same workload and extrapolates to a full
+step. Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "fwd+bwd tokens/s/GPU at S=16k,d=128 bf16; % of HBM/tensor roofline; vs FA2"
+WORKLOAD = dict(workload="stochastic tree attention fwd+bwd (attn-bench bshd contract), "
+                         "reference semantics: binary tree, 1 token per leaf",
+                batch_per_gpu=1, seq_len=16384, heads=16, head_dim=128, num_samples=8,
+                dtype="bf16")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seq-len", type=int, default=WORKLOAD["seq_len"])
+    p.add_argument("--heads", type=int, default=WORKLOAD["heads"])
+    p.add_argument("--head-dim", type=int, default=WORKLOAD["head_dim"])
+    p.add_argument("--num-samples", type=int, default=WORKLOAD["num_samples"])
+    p.add_argument("--batch", type=int, default=WORKLOAD["batch_per_gpu"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        load = [x for x in sm if mx and x > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# algorithmic bytes per launch (compulsory unique traffic of each kernel)
+# ---------------------------------------------------------------------------------------
+def algorithmic_bytes(kernel: str, B, S, H, D, P, elt, launches_per_step):
+    rows = B * S * H * D * elt          # one (B, S, H, D) tensor
+    paths = B * S * H * P
+    table = {
+        # read q, k_int, v; write out; write leaf + weight per path
+        "fwd_fused": 4 * rows + 8 * paths,
+        # read q, dO, k_int, v, leaf + weight; write dq
+        "bwd_query": 5 * rows + 8 * paths,
+        # read q, dO per path-sorted chunk; write dk (float32) and dv
+        "bwd_node": 2 * rows + B * S * H * D * 4 + rows,
+        # read k, write k_int (all passes of one step, split evenly over its launches)
+        "tree_build": 2 * rows / max(1, launches_per_step),
+        # read dk_int (float32), write dk
+        "tree_build_bwd": (B * S * H * D * 4 + rows) / max(1, launches_per_step),
+    }
+    return table.get(kernel)
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    import treeattn_b200 as ta
+    from treeattn_b200 import ops
+
+    B, S, H, D, P = args.batch, args.seq_len, args.heads, args.head_dim, args.num_samples
+    dtype = torch.bfloat16
+    gen = torch.Generator(device=dev).manual_seed(1000 * rank)
+    q, k, v, go = (torch.randn(B, S, H, D, device=dev, generator=gen).to(dtype) for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    torch.manual_seed(rank)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        out = ta.tree_attention(q, k, v, False, None, num_samples=P)
+        out.backward(go)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(dev.index)
+    ops.profile_enable(True)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    ms_step = ms / args.steps
+    tokens_step = world * B * S
+    value = tokens_step / (ms_step / 1e3)
+
+    # end to end through the public API with host buffers: H2D inputs, D2H output + grads
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hgo = (t.detach().cpu().pin_memory() for t in (q, k, v, go))
+        hout, hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(4))
+
+        def step_e2e():
+            dq_ = hq.to(dev, non_blocking=True).requires_grad_(True)
+            dk_ = hk.to(dev, non_blocking=True).requires_grad_(True)
+            dv_ = hv.to(dev, non_blocking=True).requires_grad_(True)
+            g_ = hgo.to(dev, non_blocking=True)
+            out = ta.tree_attention(dq_, dk_, dv_, False, None, num_samples=P)
+            out.backward(g_)
+            hout.copy_(out.detach(), non_blocking=True)
+            hdq.copy_(dq_.grad, non_blocking=True)
+            hdk.copy_(dk_.grad, non_blocking=True)
+            hdv.copy_(dv_.grad, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            step_e2e()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step_e2e()
+        e1.record(stream)
+        barrier()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            tm = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ems = float(tm.item())
+        nbytes = hq.numel() * hq.element_size()
+        e2e = {"value": tokens_step / (ems / args.steps / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
+               "ms_per_step": ems / args.steps}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # kernel shares and the dominant kernel's roofline
+    total = sum(v[1] for v in prof.values()) or 1.0
+    kernels = {n: {"launches_per_step": c / args.steps, "ms_per_step": t / args.steps,
+                   "share": t / total} for n, (c, t) in sorted(prof.items(), key=lambda x: -x[1][1])}
+    top = max(prof.items(), key=lambda x: x[1][1])[0] if prof else None
+    hbm, peak_kind = peaks()
+    roof = None
+    if top is not None:
+        cnt, tms = prof[top]
+        per_launch_s = tms / cnt / 1e3
+        lps = cnt / args.steps
+        alg = algorithmic_bytes(top, B, S, H, D, P, 2, lps)
+        achieved = alg / per_launch_s / 1e9 if alg else None
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic_per_launch.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                traffic = json.load(f).get(top)
+        roof = {"kernel": top, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "algorithmic_bytes_per_launch": alg, "launch_ms": tms / cnt}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1) q/k/v/grad_out from a seeded CUDA generator",
+        "config": {**WORKLOAD, "batch_per_gpu": B, "seq_len": S, "heads": H, "head_dim": D,
+                   "num_samples": P, "global_batch": world * B,
+                   "parallelism": f"head-sharded x{world} (independent (batch, head) trees, no collective)",
+                   "l2": "inputs larger than L2 (q, k, v, grad_out: 4 x %d MiB)" % (B * S * H * D * 2 >> 20)},
+        "value_per_gpu": value / world,
+        "gpu_launches": int(sum(c for c, _ in prof.values())),
+        "kernels": kernels,
+        "roofline": roof,
+        "clocks": clk,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference(args, budget_s=20.0)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------
+# CPU arm: the numpy oracle (a port of the reference; the reference itself is Python and
+# does not travel), forked over heads on every host core
+# ---------------------------------------------------------------------------------------
+_SHARED = {}
+
+
+def _cpu_heads(hs):
+    from oracle import tree_oracle as O
+
+    d = _SHARED
+    sl = slice(hs[0], hs[1])
+    k_int = O.haar_internal_node_keys(d["k"][:, :, sl], "bf16")
+    t_build = time.perf_counter()
+    q, v, go, g = d["q"][:, :, sl], d["v"][:, :, sl], d["go"][:, :, sl], d["g"][:, :, :, sl]
+    fw = O.forward(q, k_int, v, g, d["P"])
+    dq, dk, dv = O.backward(q, k_int, v, go, fw["leaf"], fw["weights"])
+    O.haar_internal_node_keys_backward(dk)
+    return t_build
+
+
+def cpu_reference(args, budget_s=20.0):
+    """Time the oracle on all S tree nodes but only Ls queries; extrapolate to a full step."""
+    import multiprocessing as mp
+
+    sys.path.insert(0, ROOT)
+    from oracle import tree_oracle as O
+
+    B, S, H, D, P = 1, args.seq_len, args.heads, args.head_dim, args.num_samples
+    rng = np.random.default_rng(0)
+    Ls = 64
+    rb = lambda *s: O.round_to_bf16(rng.standard_normal(s, dtype=np.float32))  # noqa: E731
+    _SHARED.update(q=rb(Ls, B, H, D), k=rb(S, B, H, D), v=rb(S, B, H, D), go=rb(Ls, B, H, D),
+                   g=-np.log(rng.exponential(size=(O.log_n_of(S), Ls, B, H, P, 2)).astype(np.float32)),
+                   P=P)
+    cores = min(os.cpu_count() or 1, H)
+    chunks = [(i * H // cores, (i + 1) * H // cores) for i in range(cores)]
+    ctx = mp.get_context("fork")
+    # time the tree build alone and build + Ls queries, over the same pool
+    times = []
+    with ctx.Pool(cores) as pool:
+        deadline = time.perf_counter() + budget_s
+        while True:
+            t0 = time.perf_counter()
+            pool.map(_cpu_heads, chunks)
+            t_all = time.perf_counter() - t0
+            times.append(t_all)
+            if time.perf_counter() > deadline or len(times) >= 3:
+                break
+    t_sample = min(times)
+    # separate the full-tree build from the per-query work
+    with ctx.Pool(cores) as pool:
+        t0 = time.perf_counter()
+        pool.map(_build_only, chunks)
+        t_build = time.perf_counter() - t0
+    t_query = max(t_sample - t_build, 1e-9)
+    t_step = t_build + t_query * (S / Ls)
+    return {"value": B * S / t_step, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"numpy oracle (oracle/tree_oracle.py), Haar build of all {S} keys + fwd/bwd "
+                      f"of {Ls} of {S} queries x {H} heads, {cores} processes over heads; "
+                      f"full step extrapolated = build + query part x {S // Ls}",
+            "sample_s": t_sample, "extrapolated_step_s": t_step}
+
+
+def _build_only(hs):
+    from oracle import tree_oracle as O
+
+    sl = slice(hs[0], hs[1])
+    k_int = O.haar_internal_node_keys(_SHARED["k"][:, :, sl], "bf16")
+    dk = np.zeros_like(k_int)
+    O.haar_internal_node_keys_backward(dk)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    r = cpu_reference(args, budget_s=30.0)
+    vals = [r["value"]]
+    value = r["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": len(vals), "warmup": args.warmup,
+            "ms_per_step": args.seq_len / value * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1), bf16-rounded", "config": {**WORKLOAD, "batch_per_gpu": 1},
+            "cpu_baseline": {**r, "value": value},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    sys.path.insert(0, ROOT)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

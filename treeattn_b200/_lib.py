@@ -68,6 +68,8 @@ SIGNATURES = {
     "ta_last_error": (ctypes.c_char_p, []),
     "ta_abi_version": (_I32, []),
     "ta_device_rng_geometry": (ctypes.c_int, [_I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
+    "ta_profile_enable": (ctypes.c_int, [_I32]),
+    "ta_profile_collect": (_I64, [ctypes.c_char_p, _SZ]),
     "ta_philox_plan": (ctypes.c_int, [_I64, _I32, _I32, ctypes.POINTER(ctypes.c_uint64),
                                       ctypes.POINTER(_I64)]),
     "ta_gumbel_fill": (ctypes.c_int, [_P, _I64, ctypes.POINTER(Rng), _I32, _P]),

@@ -161,9 +161,18 @@ int run_sort(BwdParams& p, cudaStream_t st) {
   const unsigned tiles = (unsigned)(p.B * p.H * p.tiles_per_seg);
   int src = 0;
   for (int ps = 0; ps < passes; ++ps) {
-    sort_hist_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
-    sort_scan_kernel<<<p.B * p.H, 1024, 0, st>>>(p);
-    sort_scatter_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
+    {
+      TA_PROFILE("sort_hist", st);
+      sort_hist_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
+    }
+    {
+      TA_PROFILE("sort_scan", st);
+      sort_scan_kernel<<<p.B * p.H, 1024, 0, st>>>(p);
+    }
+    {
+      TA_PROFILE("sort_scatter", st);
+      sort_scatter_kernel<<<tiles, kSortThreads, 0, st>>>(p, src, ps * kRadixBits);
+    }
     src ^= 1;
   }
   p.sorted_buf = src;

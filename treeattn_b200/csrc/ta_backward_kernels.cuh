@@ -454,6 +454,7 @@ void launch_query(const BwdParams& p, cudaStream_t st) {
   const size_t smem = (size_t)kBwdGroups * p.S * 4;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(bwd_query_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  TA_PROFILE("bwd_query", st);
   bwd_query_kernel<T, CPL><<<ltiles * p.B * p.H, kBwdThreads, smem, st>>>(p);
 }
 
@@ -473,6 +474,7 @@ int run_query(const BwdParams& p, cudaStream_t st) {
 
 template <typename T, int EL>
 void launch_node_el(const BwdParams& p, cudaStream_t st, unsigned grid) {
+  TA_PROFILE("bwd_node", st);
   if (p.log_n <= 16) bwd_node_kernel<T, EL, 16><<<grid, kNodeWarps * 32, 0, st>>>(p);
   else bwd_node_kernel<T, EL, 30><<<grid, kNodeWarps * 32, 0, st>>>(p);
 }
@@ -494,6 +496,7 @@ int run_rest(BwdParams& p, cudaStream_t st) {
   }
   if ((rc = check_launch("backward node pass"))) return rc;
   const int64_t items = nchunks_total * (p.log_n + 1);
+  TA_PROFILE("bwd_fixup", st);
   bwd_fixup_kernel<T><<<(unsigned)((items + 7) / 8), 256, 0, st>>>(p);
   return check_launch("backward fix-up");
 }

@@ -3,6 +3,11 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
 #include "ta_common.cuh"
 
 namespace ta {
@@ -30,7 +35,79 @@ int check_launch(const char* what) {
   return TA_OK;
 }
 
+// ---- per-launch profiling -------------------------------------------------------------
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+static std::mutex g_prof_mu;
+static bool g_prof_on = false;
+static std::vector<ProfRecord> g_prof;
+static std::vector<cudaEvent_t> g_prof_pool;
+
+static cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+ProfScope::ProfScope(const char* name, cudaStream_t st) : slot(-1), stream(st) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof_on) return;
+  ProfRecord r{name, prof_event(), prof_event()};
+  cudaEventRecord(r.start, st);
+  slot = (int)g_prof.size();
+  g_prof.push_back(r);
+}
+
+ProfScope::~ProfScope() {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  cudaEventRecord(g_prof[slot].stop, stream);
+}
+
 }  // namespace ta
+
+extern "C" int ta_profile_enable(int32_t on) {
+  std::lock_guard<std::mutex> lk(ta::g_prof_mu);
+  ta::g_prof_on = on != 0;
+  return TA_OK;
+}
+
+// Waits for every recorded launch, writes "name count total_ms" lines (sorted by name) and
+// clears the records. Returns the bytes needed (excluding the terminator); truncates to len.
+extern "C" int64_t ta_profile_collect(char* buf, size_t len) {
+  std::lock_guard<std::mutex> lk(ta::g_prof_mu);
+  std::map<std::string, std::pair<int64_t, double>> agg;
+  for (auto& r : ta::g_prof) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(r.stop) == cudaSuccess) cudaEventElapsedTime(&ms, r.start, r.stop);
+    auto& a = agg[r.name];
+    a.first += 1;
+    a.second += ms;
+    ta::g_prof_pool.push_back(r.start);
+    ta::g_prof_pool.push_back(r.stop);
+  }
+  ta::g_prof.clear();
+  std::string out;
+  char line[256];
+  for (auto& kv : agg) {
+    snprintf(line, sizeof(line), "%s %lld %.6f\n", kv.first.c_str(), (long long)kv.second.first,
+             kv.second.second);
+    out += line;
+  }
+  if (buf && len) {
+    const size_t n = out.size() < len - 1 ? out.size() : len - 1;
+    memcpy(buf, out.data(), n);
+    buf[n] = 0;
+  }
+  return (int64_t)out.size();
+}
 
 extern "C" const char* ta_last_error(void) { return ta::g_err; }
 

@@ -20,6 +20,16 @@ int check_view(const char* name, const void* ptr, ta_layout lay, int esize, bool
 int check_shape(const ta_shape* s, bool need_pow2);
 int pick_cpl(int nchunks);
 
+// Per-launch CUDA-event timing, enabled by ta_profile_enable(1): a scope records an event
+// pair around the launches it encloses on `stream`; ta_profile_collect() aggregates them.
+struct ProfScope {
+  ProfScope(const char* name, cudaStream_t stream);
+  ~ProfScope();
+  int slot;
+  cudaStream_t stream;
+};
+#define TA_PROFILE(name, stream) ::ta::ProfScope _ta_prof_##__LINE__(name, stream)
+
 // ---------------------------------------------------------------------------------------
 // element types
 // ---------------------------------------------------------------------------------------

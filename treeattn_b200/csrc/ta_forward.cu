@@ -334,12 +334,14 @@ static void launch_fwd(const FwdParams& p, cudaStream_t st, bool value_only) {
   const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
   const dim3 grid((unsigned)(ltiles * p.B * p.H));
   if (value_only) {
+    TA_PROFILE("value_sum", st);
     value_sum_kernel<T, CPL><<<grid, kFwdThreads, 0, st>>>(p);
     return;
   }
   const size_t smem = (size_t)kFwdGroups * p.S * 8;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(fwd_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  TA_PROFILE(p.mode == kFull ? "fwd_fused" : (p.mode == kSampleOnly ? "sample_paths" : "replay_paths"), st);
   fwd_kernel<T, CPL><<<grid, kFwdThreads, smem, st>>>(p);
 }
 
@@ -496,6 +498,7 @@ extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int3
   FastDiv fd;
   fd.init((uint32_t)rng->draw_stride);
   const unsigned grid = (unsigned)((numel + 255) / 256);
+  TA_PROFILE("gumbel_fill", (cudaStream_t)stream);
   gumbel_fill_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
       out, (uint32_t)numel, rng->seed, rng->offset + (uint64_t)depth * rng->offset_step, fd);
   return check_launch("gumbel fill");

@@ -47,7 +47,7 @@ __device__ __forceinline__ float torch_uniform(uint64_t seed, uint64_t offset, u
 
 __device__ __forceinline__ float gumbel_from_uniform(float u) {
   const float half_eps = FLT_EPSILON * 0.5f;
-  const float lg = (u >= 1.0f - half_eps) ? -half_eps : logf(u);
+  const float lg = (u >= 1.0f - half_eps) ? -half_eps : __logf(u);
   const float e = -1.0f / 1.0f * lg;
   return -logf(e);
 }

@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(kTreeThreads) haar_bwd_kernel(const TreeParams
 
 template <typename T>
 static void launch_haar_fwd(int lv, const TreeParams& p, cudaStream_t st) {
+  TA_PROFILE("tree_build", st);
   const int64_t total = (int64_t)p.B * (p.count >> lv) * p.H * p.vecs;
   const unsigned grid = (unsigned)((total + kTreeThreads - 1) / kTreeThreads);
   switch (lv) {
@@ -164,6 +165,7 @@ static void launch_haar_fwd(int lv, const TreeParams& p, cudaStream_t st) {
 
 template <typename OUT_T>
 static void launch_haar_bwd(int lv, const TreeParams& p, cudaStream_t st) {
+  TA_PROFILE("tree_build_bwd", st);
   const int64_t total = (int64_t)p.B * (p.count >> lv) * p.H * p.vecs;
   const unsigned grid = (unsigned)((total + kTreeThreads - 1) / kTreeThreads);
   switch (lv) {

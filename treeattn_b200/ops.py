@@ -317,3 +317,25 @@ def weighted_value_sum(v, leaf, weights, *, out=None):
            layout(out), _stream(dev))
     _note("value_sum")
     return out
+
+
+# ---------------------------------------------------------------------------------------
+# per-launch profiling (CUDA events recorded by the library on each launch's stream)
+# ---------------------------------------------------------------------------------------
+
+def profile_enable(on: bool = True) -> None:
+    L.call("ta_profile_enable", 1 if on else 0)
+
+
+def profile_collect() -> dict[str, tuple[int, float]]:
+    """{kernel: (launches, total_ms)} of every launch since the last collect (synchronises)."""
+    lib = L.load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    n = lib.ta_profile_collect(buf, len(buf))
+    if n >= len(buf):
+        raise RuntimeError("profile text truncated")
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, cnt, ms = line.split()
+        out[name] = (int(cnt), float(ms))
+    return out
