@@ -109,14 +109,15 @@ int ta_philox_plan(int64_t numel, int32_t sm_count, int32_t max_threads_per_sm,
                    uint64_t* offset_step, int64_t* draw_stride);
 
 /*
- * The Gumbel noise of tree depth `depth`: out[e] for e < numel is bit-identical to
- * torch.empty(numel, dtype=float32, device=cuda).exponential_().log_().neg_() drawn at
- * generator state (rng->seed, rng->offset + depth * rng->offset_step) -- the per-depth draw
- * of the reference (_autograd.py:188-195) -- generated by the same device code the fused
- * sampler uses.
+ * The Gumbel noise of tree depths depth0 .. depth0+depths-1: out[d * numel + e] is
+ * bit-identical to torch.empty(numel, dtype=float32, device=cuda).exponential_().log_().neg_()
+ * drawn at generator state (rng->seed, rng->offset + (depth0 + d) * rng->offset_step) -- the
+ * per-depth draws of the reference (_autograd.py:188-195). Each philox 4-vector is computed
+ * once and feeds the four elements torch's grid-stride loop assigns to it. The result is the
+ * `gumbels` input of ta_forward / ta_sample_paths.
  */
-int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth,
-                   ta_stream_t stream);
+int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth0,
+                   int32_t depths, ta_stream_t stream);
 
 /* ---- tree build (A1) ---------------------------------------------------------------- */
 
@@ -151,10 +152,13 @@ int ta_tree_build_backward(int32_t dtype, int64_t batch, int64_t seq_len, int64_
 /*
  * Stochastic non-causal tree attention forward, one launch: per (query, sample) walk the
  * tree drawing the Gumbel noise in-kernel (or reading `gumbels` when it is not NULL:
- * float32 (log2 N, L, B, H, S, 2)), softmax the path log-probabilities over the S samples,
- * and write out[l,b,h] = sum_s w_s v[leaf_s]. Writes leaf (int32, may be NULL), weights
- * (float32, may be NULL) and packed path bits (may be NULL). num_leaves must be a power of
- * two >= 2.
+ * float32 (log2 N, L, B, H, S, 2), e.g. from ta_gumbel_fill), softmax the path
+ * log-probabilities over the S samples, and write out[l,b,h] = sum_s w_s v[leaf_s]. Writes
+ * leaf (int32, may be NULL), weights (float32, may be NULL), packed path bits (may be NULL)
+ * and, when branch_prob is not NULL, the probability of the branch NOT taken at every
+ * depth of every path, sigmoid(-sgn s) (float32, 16-byte aligned,
+ * [B*H][L*S][ta_branch_prob_stride(N)], head-major), which ta_backward consumes so it never
+ * recomputes a node logit. num_leaves must be a power of two >= 2.
  * Replaces _StochasticNonCausalTreeAttention.forward (_autograd.py:647-704), i.e.
  * sample_non_causal_paths_forward + softmax + weighted_value_sum_forward
  * (treeattn_cuda.cpp:479-488).
@@ -162,12 +166,15 @@ int ta_tree_build_backward(int32_t dtype, int64_t batch, int64_t seq_len, int64_
 int ta_forward(const ta_shape* shape, const void* q, ta_layout q_layout, const void* k_int,
                ta_layout k_layout, const void* v, ta_layout v_layout, void* out,
                ta_layout out_layout, const ta_rng* rng, const float* gumbels, int32_t* leaf,
-               float* weights, uint8_t* packed_paths, ta_stream_t stream);
+               float* weights, uint8_t* packed_paths, float* branch_prob, ta_stream_t stream);
+
+/* Floats per path row of branch_prob: log2(N) rounded up to a multiple of 4. */
+int32_t ta_branch_prob_stride(int64_t num_leaves);
 
 /* ---- fused deterministic backward (A8) -------------------------------------------- */
 
 /*
- * Gradients of ta_forward given its leaf and weights outputs. dq and dv are written in
+ * Gradients of ta_forward given its leaf, weights and branch_prob outputs. dq and dv are written in
  * shape->dtype; dk in `dk_dtype` (TA_F32 for a float32 accumulation buffer, or
  * shape->dtype). No float atomics: dK/dV are reduced by sorting paths by leaf and summing
  * each node's contributions in a fixed order, so results are bitwise repeatable.
@@ -179,9 +186,9 @@ size_t ta_backward_workspace_size(const ta_shape* shape);
 int ta_backward(const ta_shape* shape, const void* q, ta_layout q_layout, const void* k_int,
                 ta_layout k_layout, const void* v, ta_layout v_layout, const void* grad_out,
                 ta_layout grad_out_layout, const int32_t* leaf, const float* weights,
-                void* dq, ta_layout dq_layout, void* dk, ta_layout dk_layout, int32_t dk_dtype,
-                void* dv, ta_layout dv_layout, void* workspace, size_t workspace_bytes,
-                ta_stream_t stream);
+                const float* branch_prob, void* dq, ta_layout dq_layout, void* dk,
+                ta_layout dk_layout, int32_t dk_dtype, void* dv, ta_layout dv_layout,
+                void* workspace, size_t workspace_bytes, ta_stream_t stream);
 
 /* ---- reference-granularity entry points (treeattn_cuda.cpp:479-488) ---------------- */
 

@@ -46,12 +46,12 @@ def test_invalid_arguments_report_errors_without_a_gpu():
     shape = _lib.Shape(1, 8, 7, 1, 16, 4, _lib.TA_F32, 1e3)  # N=7: not a power of two
     lay = _lib.Layout(16, 16, 16)
     rc = lib.ta_forward(ctypes.byref(shape), None, lay, None, lay, None, lay, None, lay, None,
-                        None, None, None, None, None)
+                        None, None, None, None, None, None)
     assert rc == _lib.TA_ERR_UNSUPPORTED
     assert b"power of two" in lib.ta_last_error()
     shape.num_leaves = 8
     rc = lib.ta_forward(ctypes.byref(shape), None, lay, None, lay, None, lay, None, lay, None,
-                        None, None, None, None, None)
+                        None, None, None, None, None, None)
     assert rc == _lib.TA_ERR_INVALID and b"q is NULL" in lib.ta_last_error()
     shape.head_dim = 6  # 24 bytes: not a 16-byte multiple
     assert lib.ta_backward_workspace_size(ctypes.byref(shape)) == 0
@@ -67,7 +67,7 @@ def test_workspace_sizes():
     shape = _lib.Shape(1, 16384, 16384, 16, 128, 8, _lib.TA_BF16, 1e3)
     ws = lib.ta_backward_workspace_size(ctypes.byref(shape))
     P = 16384 * 8 * 16
-    assert ws >= P * 4 * 4 + P * 14 * 4  # records (2 buffers x key/val) + per-depth logit grads
+    assert ws >= P * 4 * 4 + P * 4  # records (2 buffers x key/val) + per-path dlp
     assert lib.ta_tree_build_workspace_size(1, 16384, 16, 128, _lib.TA_BF16) > 0
     assert lib.ta_tree_build_workspace_size(1, 32, 16, 128, _lib.TA_BF16) == 0
 

@@ -77,6 +77,8 @@ def test_gumbel_stream_bit_exact_with_torch(numel):
     for d in range(3):
         got = ops.gumbel_fill(torch.empty(numel, device=DEV), rng, d)
         assert torch.equal(got, ref[d]), f"depth {d}: {(got != ref[d]).sum().item()} differ"
+    allg = ops.gumbel_fill(torch.empty(3, numel, device=DEV), rng)
+    assert torch.equal(allg, ref)
 
 
 # ---------------------------------------------------------------------------------------
@@ -116,6 +118,19 @@ def test_sampler_matches_oracle_and_reference_stream(dtype, L, B, H, D, S):
                        packed.cpu())
 
 
+def test_fused_and_prefilled_noise_agree():
+    torch.manual_seed(0)
+    q = torch.randn(300, 2, 3, 64, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(511, 2, 3, 64, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(512, 2, 3, 64, device=DEV, dtype=torch.bfloat16)
+    torch.manual_seed(9)
+    a = ops.forward(q, k, v, 8)
+    torch.manual_seed(9)
+    b = ops.forward(q, k, v, 8, fused_rng=True)
+    assert torch.equal(a.leaf, b.leaf) and torch.equal(a.out, b.out)
+    assert torch.equal(a.branch_prob, b.branch_prob)
+
+
 def test_sampler_deterministic_and_seed_sensitive():
     torch.manual_seed(0)
     q = torch.randn(32, 1, 2, 16, device=DEV)
@@ -147,7 +162,7 @@ def test_forward_backward_match_reference_fixtures(path):
     # the reference test's tolerances (test_harness_smoke.py:887-891)
     np.testing.assert_allclose(res.out.reshape(L, B, -1).cpu().numpy(), f["out"], atol=5e-5, rtol=5e-5)
     np.testing.assert_allclose(res.weights.cpu().numpy(), f["weights"], atol=5e-5, rtol=5e-5)
-    dq, dk, dv = ops.backward(q, k, v, g, res.leaf, res.weights, S)
+    dq, dk, dv = ops.backward(q, k, v, g, res.leaf, res.weights, res.branch_prob, S)
     np.testing.assert_allclose(dq.reshape(L, B, -1).cpu().numpy(), f["dq"], atol=2e-4, rtol=2e-4)
     np.testing.assert_allclose(dk.reshape(L - 1, B, -1).cpu().numpy(), f["dk"], atol=4e-4, rtol=4e-4)
     np.testing.assert_allclose(dv.reshape(L, B, -1).cpu().numpy(), f["dv"], atol=2e-4, rtol=2e-4)
@@ -287,7 +302,7 @@ def test_edge_shapes_and_layouts():
         fw = O.forward(*(t.cpu().numpy() for t in (q, k, v, g)), S)
         assert_leaves_match(res.leaf.cpu().numpy(), fw["leaf"], q.cpu().numpy(), k.cpu().numpy(), g.cpu().numpy())
         np.testing.assert_allclose(res.out.cpu().numpy(), fw["out"], atol=5e-5, rtol=5e-5)
-        dq, dk, dv = ops.backward(q, k, v, go, res.leaf, res.weights, S)
+        dq, dk, dv = ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S)
         rq, rk, rv = O.backward(*(t.cpu().numpy() for t in (q, k, v, go)), res.leaf.cpu().numpy().astype(np.int64),
                                 res.weights.cpu().numpy())
         np.testing.assert_allclose(dq.cpu().numpy(), rq, atol=2e-4, rtol=2e-4)
@@ -305,7 +320,7 @@ def test_collapsed_paths_all_queries_one_leaf():
     torch.manual_seed(0)
     res = ops.forward(q, k, v, S)
     assert int(res.leaf.max()) == 0
-    dq, dk, dv = ops.backward(q, k, v, go, res.leaf, res.weights, S)
+    dq, dk, dv = ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S)
     rq, rk, rv = O.backward(*(t.cpu().numpy() for t in (q, k, v, go)), res.leaf.cpu().numpy().astype(np.int64),
                             res.weights.cpu().numpy())
     np.testing.assert_allclose(dv.cpu().numpy(), rv, atol=1e-3, rtol=1e-4)

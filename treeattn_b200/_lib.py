@@ -72,17 +72,18 @@ SIGNATURES = {
     "ta_profile_collect": (_I64, [ctypes.c_char_p, _SZ]),
     "ta_philox_plan": (ctypes.c_int, [_I64, _I32, _I32, ctypes.POINTER(ctypes.c_uint64),
                                       ctypes.POINTER(_I64)]),
-    "ta_gumbel_fill": (ctypes.c_int, [_P, _I64, ctypes.POINTER(Rng), _I32, _P]),
+    "ta_gumbel_fill": (ctypes.c_int, [_P, _I64, ctypes.POINTER(Rng), _I32, _I32, _P]),
+    "ta_branch_prob_stride": (_I32, [_I64]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_backward_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "ta_tree_build_backward": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P,
                                               _SZ, _P]),
     "ta_forward": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _L,
-                                  ctypes.POINTER(Rng), _P, _P, _P, _P, _P]),
+                                  ctypes.POINTER(Rng), _P, _P, _P, _P, _P, _P]),
     "ta_backward_workspace_size": (_SZ, [ctypes.POINTER(Shape)]),
     "ta_backward": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _L, _P, _P,
-                                   _P, _L, _P, _L, _I32, _P, _L, _P, _SZ, _P]),
+                                   _P, _P, _L, _P, _L, _I32, _P, _L, _P, _SZ, _P]),
     "ta_sample_paths": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L,
                                        ctypes.POINTER(Rng), _P, _P, _P, _P, _P]),
     "ta_replay_paths": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _I32, _P, _P,
@@ -104,7 +105,9 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        path = _build.LIB
+        path = os.environ.get("TREEATTN_B200_LIB") or _build.LIB
+        if os.environ.get("TREEATTN_B200_LIB"):
+            build_if_missing = False  # an explicitly chosen library is used as is
         if build_if_missing:
             _build.build()  # no-op when the library matches the sources
         elif not os.path.exists(path):

@@ -33,7 +33,7 @@ class TreeAttentionFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k_int, v, num_samples, max_logit):
         res = ops.forward(q, k_int, v, num_samples, max_logit=max_logit)
-        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights)
+        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights, res.branch_prob)
         ctx.num_samples = num_samples
         ctx.max_logit = max_logit
         ctx.mark_non_differentiable(res.weights)
@@ -42,8 +42,8 @@ class TreeAttentionFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out, grad_weights):
         del grad_weights
-        q, k_int, v, leaf, weights = ctx.saved_tensors
-        dq, dk, dv = ops.backward(q, k_int, v, grad_out, leaf, weights, ctx.num_samples,
+        q, k_int, v, leaf, weights, bp = ctx.saved_tensors
+        dq, dk, dv = ops.backward(q, k_int, v, grad_out, leaf, weights, bp, ctx.num_samples,
                                   max_logit=ctx.max_logit, dk_dtype=k_int.dtype)
         return dq, dk, dv, None, None
 
@@ -62,21 +62,21 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
         out = torch.empty_like(q)
         res = ops.forward(qv, k_int, vv, num_samples, max_logit=max_logit, out=out.transpose(0, 1),
                           gumbels=gumbels)
-        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights)
+        ctx.save_for_backward(q, k_int, v, res.leaf, res.weights, res.branch_prob)
         ctx.num_samples = num_samples
         ctx.max_logit = max_logit
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, k_int, v, leaf, weights = ctx.saved_tensors
+        q, k_int, v, leaf, weights, bp = ctx.saved_tensors
         B, S, H, D = q.shape
         dq = torch.empty_like(q)
         dv = torch.empty_like(v)
         dk_int = torch.empty((B, H, S - 1, D), device=q.device, dtype=torch.float32).permute(2, 0, 1, 3)
         grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
         ops.backward(q.transpose(0, 1), k_int, v.transpose(0, 1), grad_out.transpose(0, 1), leaf,
-                     weights, ctx.num_samples, max_logit=ctx.max_logit, dq=dq.transpose(0, 1),
+                     weights, bp, ctx.num_samples, max_logit=ctx.max_logit, dq=dq.transpose(0, 1),
                      dk=dk_int, dv=dv.transpose(0, 1))
         dk = torch.empty_like(q)
         ops.tree_build_backward(dk_int, dk.transpose(0, 1))

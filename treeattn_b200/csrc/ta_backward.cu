@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kSortThreads) sort_scatter_kernel(const BwdPar
 // host side
 // ---------------------------------------------------------------------------------------
 struct BwdLayout {
-  size_t keys[2], vals[2], gl, hist, partial, flags, total;
+  size_t keys[2], vals[2], dlp, hist, partial, flags, total;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -147,7 +147,7 @@ static BwdLayout bwd_layout(const ta_shape* s) {
   w.keys[1] = take(HB * P * 4);
   w.vals[0] = take(HB * P * 4);
   w.vals[1] = take(HB * P * 4);
-  w.gl = take(HB * P * ln * 4);
+  w.dlp = take(HB * P * 4);
   w.hist = take(HB * kRadix * tiles * 4);
   w.partial = take(chunks * (ln + 1) * 2 * s->head_dim * 4);
   w.flags = take(chunks * (ln + 1) * 2);
@@ -190,9 +190,10 @@ extern "C" size_t ta_backward_workspace_size(const ta_shape* shape) {
 
 extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
                            ta_layout kl, const void* v, ta_layout vl, const void* gout,
-                           ta_layout gl, const int32_t* leaf, const float* weights, void* dq,
-                           ta_layout dql, void* dk, ta_layout dkl, int32_t dk_dtype, void* dv,
-                           ta_layout dvl, void* ws, size_t ws_bytes, ta_stream_t stream) {
+                           ta_layout gl, const int32_t* leaf, const float* weights,
+                           const float* branch_prob, void* dq, ta_layout dql, void* dk,
+                           ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl, void* ws,
+                           size_t ws_bytes, ta_stream_t stream) {
   int rc = check_shape(shape, true);
   if (rc) return rc;
   const int es = dtype_size(shape->dtype);
@@ -204,7 +205,8 @@ extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, c
       (rc = check_view("dk", dk, dkl, dtype_size(dk_dtype), false)) ||
       (rc = check_view("dv", dv, dvl, es, false)))
     return rc;
-  if (!leaf || !weights) return fail(TA_ERR_INVALID, "leaf and weights must not be NULL");
+  if (!leaf || !weights || !branch_prob)
+    return fail(TA_ERR_INVALID, "leaf, weights and branch_prob must not be NULL");
   if (shape->num_queries * shape->num_samples >= (1ll << 31))
     return fail(TA_ERR_UNSUPPORTED, "L * S must be < 2^31");
   const BwdLayout w = bwd_layout(shape);
@@ -224,12 +226,14 @@ extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, c
   char* base = (char*)ws;
   p.keys[0] = (uint32_t*)(base + w.keys[0]); p.keys[1] = (uint32_t*)(base + w.keys[1]);
   p.vals[0] = (uint32_t*)(base + w.vals[0]); p.vals[1] = (uint32_t*)(base + w.vals[1]);
-  p.gl = (float*)(base + w.gl); p.hist = (uint32_t*)(base + w.hist);
+  p.dlp = (float*)(base + w.dlp); p.sig = branch_prob; p.hist = (uint32_t*)(base + w.hist);
   p.partial = (float*)(base + w.partial); p.flags = (uint8_t*)(base + w.flags);
   p.B = (int32_t)shape->batch; p.L = (int32_t)shape->num_queries; p.H = (int32_t)shape->num_heads;
   p.S = (int32_t)shape->num_samples; p.N = (int32_t)shape->num_leaves;
   p.D = (int32_t)shape->head_dim; p.log_n = floor_log2(shape->num_leaves);
   p.nchunks = (int32_t)(shape->head_dim * es / 16);
+  p.sig_stride = (p.log_n + 3) & ~3;
+  p.top_levels = smem_tree_levels(p.log_n, p.nchunks * 16, kTreeSmemBudget);
   p.dk_f32 = dk_dtype == TA_F32 ? 1 : 0;
   p.P = shape->num_queries * shape->num_samples;
   p.tiles_per_seg = (int32_t)((p.P + kSortTile - 1) / kSortTile);

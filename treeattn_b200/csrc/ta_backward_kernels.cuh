@@ -1,4 +1,4 @@
-// Fused deterministic backward of stochastic tree attention, sm_100a.
+// Fused deterministic backward of stochastic tree attention, sm_100a (typed kernels).
 //
 // Math (reference: _autograd.py:707-860, accumulate_qk_non_causal_all_depths_prepared.cu,
 // scatter_weighted_grad_v.cu):
@@ -8,21 +8,22 @@
 //   dq    = sum_s sum_d gl_sd k[node_sd]
 //   dk[n] = sum_{(s,d) through n} gl_sd q
 //   dv[l] = sum_{s ending at l} w_s dO
+// sigmoid(-sgn s_sd) comes from the forward (branch_prob), so no node logit is recomputed.
 //
 // The reference scatters dK/dV with float atomics (order-dependent results). Here the
 // scatter becomes a gather over paths sorted by leaf, so every node's sum has a fixed
 // order and the result is bitwise repeatable:
-//   1. query pass (one 4-lane group per query): g, dlp, per-depth gl (stored), dq (written);
-//      emits (path bits, path id) records in head-major path order.
+//   1. query pass (one 4-lane group per query): g, dlp (stored), dq (written); emits
+//      (path bits, path id) records in head-major path order.
 //   2. stable LSD radix sort of the records of each head by path bits (8-bit digits).
 //   3. node pass: each warp owns a chunk of consecutive sorted paths. Paths through a node
 //      are contiguous in this order, so the warp keeps one accumulator per depth in
 //      registers and writes a node's total when the node closes. Nodes cut by a chunk
 //      boundary leave a partial per side; nodes no path reaches are written as zeros.
-//   4. fix-up: the chunk where a cut node starts adds the partials of the following chunks
-//      in chunk order and writes the node.
-
+//   4. fix-up: the chunk where a cut node starts sums the partials of the chunks it spans
+//      (a fixed split over the CTA's warps, combined in warp order) and writes the node.
 #pragma once
+
 #include "ta_common.cuh"
 
 namespace ta {
@@ -35,7 +36,8 @@ constexpr int kSortTile = kSortThreads * kSortItems;  // 2048 records per tile
 constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
 constexpr int kChunk = 512;  // sorted paths per node-pass warp
-constexpr int kNodeWarps = 8;
+constexpr int kNodeWarps = 4;
+constexpr int kFixThreads = 256;
 
 struct BwdParams {
   const char* q; const char* k; const char* v; const char* dout;
@@ -44,18 +46,20 @@ struct BwdParams {
   int64_t dqs, dqb, dqh, dks, dkb, dkh, dvs, dvb, dvh;
   const int32_t* leaf;
   const float* weights;
-  float* gl;           // [HB][P][log_n]
+  const float* sig;    // [HB][P][sig_stride]  sigmoid(-sgn s) from the forward
+  float* dlp;          // [HB][P]
   uint32_t* keys[2];   // [HB][P]
   uint32_t* vals[2];
   uint32_t* hist;      // [HB][256][tiles_per_seg]
   float* partial;      // [chunks][log_n + 1][2][D]
   uint8_t* flags;      // [chunks][log_n + 1][2]: head kind (0 none, 1 ends here, 2 through), tail
-  int32_t B, L, H, S, N, D, log_n, nchunks;
+  int32_t B, L, H, S, N, D, log_n, nchunks, sig_stride;
   int32_t dk_f32;      // dk written as float32 (else input dtype)
   int64_t P;           // paths per head = L * S
   int32_t tiles_per_seg, chunks_per_seg;
   int32_t sorted_buf;  // which keys/vals buffer holds the sorted records
   float max_logit;
+  int32_t top_levels;  // tree levels staged in shared memory by the query pass
 };
 
 // radix-sort kernels (ta_backward.cu)
@@ -68,11 +72,11 @@ int run_sort(BwdParams& p, cudaStream_t st);
 // 1. query pass
 // ---------------------------------------------------------------------------------------
 template <typename T, int CPL>
-__global__ void __launch_bounds__(kBwdThreads) bwd_query_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdParams p) {
   using E = Elem<T>;
   constexpr int EPC = E::EPC;
   constexpr int NE = CPL * EPC;
-  constexpr int ILP = 2;
+  constexpr int DU = 4;  // depths whose rows are in flight together
   extern __shared__ float smem[];
 
   const int ltiles = (p.L + kBwdGroups - 1) / kBwdGroups;
@@ -83,54 +87,62 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_query_kernel(const BwdParams 
   const int g = threadIdx.x >> 2;
   const int t4 = threadIdx.x & 3;
   const int l = lt * kBwdGroups + g;
-  if (l >= p.L) return;
   const unsigned gmask = 0xFu << (threadIdx.x & 28);
-  float* s_dlp = smem + g * p.S;
+  const int row_bytes = p.nchunks * 16;
+  const int top_rows = (1 << p.top_levels) - 1;
+  char* s_tree = reinterpret_cast<char*>(smem);
+  float* s_dlp = reinterpret_cast<float*>(s_tree + (size_t)top_rows * row_bytes) + g * p.S;
 
-  const int64_t K = (int64_t)p.N - 1;
-  const int64_t base_node = ((int64_t)1 << p.log_n) - 1;
+  const uint32_t K = (uint32_t)p.N - 1u;
+  const uint32_t base_node = (1u << p.log_n) - 1u;
   const int64_t j0 = (((int64_t)l * p.B + b) * p.H + h) * p.S;
   const int64_t hb = (int64_t)b * p.H + h;
   const int64_t path0 = hb * p.P + (int64_t)l * p.S;  // head-major path index of sample 0
 
-  float qf[NE], acc[NE];
+  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
+  const uint32_t vstride = (uint32_t)(p.vs * (int64_t)sizeof(T));
+  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
+  const uint32_t kstride = (uint32_t)(p.ks * (int64_t)sizeof(T));
+  if (top_rows > 0) {
+    stage_tree_rows(s_tree, kbase, kstride, top_rows, row_bytes);
+    cp_async_wait_0();
+    __syncthreads();
+  }
+  if (l >= p.L) return;  // whole group leaves together (no block barrier follows)
+
+  // g_s = dO . v[leaf_s]
   {
-    const char* qrow = p.q + ((int64_t)l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
+    uint4 graw[CPL];
     const char* grow = p.dout + ((int64_t)l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
       const int c = i * 4 + t4;
-      if (c < p.nchunks) {
-        E::unpack(ldg16(qrow + c * 16), qf + i * EPC);
-        E::unpack(ldg16(grow + c * 16), acc + i * EPC);  // dO, reused as dq accumulator later
-      } else {
+      graw[i] = c < p.nchunks ? ldg16(grow + c * 16) : make_uint4(0, 0, 0, 0);
+    }
+    for (int s0 = 0; s0 < p.S; s0 += 4) {
+      uint4 raw[4][CPL];
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) { qf[i * EPC + e] = 0.0f; acc[i * EPC + e] = 0.0f; }
+      for (int t = 0; t < 4; ++t) {
+        const int s = min(s0 + t, p.S - 1);
+        int32_t lf = p.leaf[j0 + s];
+        lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+        const char* vrow = vbase + (uint64_t)(uint32_t)lf * vstride;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const int c = i * 4 + t4;
+          raw[t][i] = c < p.nchunks ? ldg16(vrow + c * 16) : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) d = Dot<T>::chunk(graw[i], raw[t][i], d);
+        d += __shfl_xor_sync(gmask, d, 1, 4);
+        d += __shfl_xor_sync(gmask, d, 2, 4);
+        if (t4 == t && s0 + t < p.S) s_dlp[s0 + t] = d;
       }
     }
-  }
-  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
-
-  // g_s = dO . v[leaf_s]
-  for (int s = 0; s < p.S; ++s) {
-    int64_t lf = p.leaf[j0 + s];
-    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-    const char* vrow = vbase + lf * p.vs * (int64_t)sizeof(T);
-    float d = 0.0f;
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      const int c = i * 4 + t4;
-      if (c < p.nchunks) {
-        float vf[EPC];
-        E::unpack(ldg16(vrow + c * 16), vf);
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) d = fmaf(acc[i * EPC + e], vf[e], d);
-      }
-    }
-    d += __shfl_xor_sync(gmask, d, 1, 4);
-    d += __shfl_xor_sync(gmask, d, 2, 4);
-    if (t4 == 0) s_dlp[s] = d;
   }
   __syncwarp(gmask);
   // dlp_s = w_s (g_s - sum_t w_t g_t)
@@ -138,76 +150,56 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_query_kernel(const BwdParams 
   for (int s = 0; s < p.S; ++s) wg = fmaf(p.weights[j0 + s], s_dlp[s], wg);
   __syncwarp(gmask);
   for (int s = t4; s < p.S; s += 4) {
-    const float w = p.weights[j0 + s];
-    s_dlp[s] = w * (s_dlp[s] - wg);
+    const float d = p.weights[j0 + s] * (s_dlp[s] - wg);
+    s_dlp[s] = d;
+    p.dlp[path0 + s] = d;
+    // sort record of path s: (path bits, path id within its head)
+    p.keys[0][path0 + s] = (uint32_t)p.leaf[j0 + s] + K - base_node;
+    p.vals[0][path0 + s] = (uint32_t)(l * p.S + s);
   }
   __syncwarp(gmask);
 
+  // dq = sum_s sum_d sgn sig dlp k[node]
+  float acc[NE];
 #pragma unroll
   for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
-  const int64_t kstride = p.ks * (int64_t)sizeof(T);
-
-  for (int s0 = 0; s0 < p.S; s0 += ILP) {
-    const int ns = min(ILP, p.S - s0);
-    uint32_t bits[ILP];
-    float dlp[ILP];
+  for (int s = 0; s < p.S; ++s) {
+    const uint32_t bits = (uint32_t)p.leaf[j0 + s] + K - base_node;
+    const float dlp = s_dlp[s];
+    const float* sig = p.sig + (path0 + s) * p.sig_stride;
+    for (int d0 = 0; d0 < p.log_n; d0 += DU) {
+      uint4 raw[DU][CPL];
+      float gl[DU];
 #pragma unroll
-    for (int t = 0; t < ILP; ++t) {
-      const int s = s0 + (t < ns ? t : 0);
-      bits[t] = (uint32_t)((int64_t)p.leaf[j0 + s] + K - base_node);
-      dlp[t] = t < ns ? s_dlp[s] : 0.0f;
-    }
-    if (t4 < ns) {  // sort record of path s0 + t4: (path bits, path id within its head)
-      const int s = s0 + t4;
-      uint32_t bt = bits[0];
+      for (int u = 0; u < DU; ++u) {
+        const int d = min(d0 + u, p.log_n - 1);
+        const uint32_t node = (1u << d) - 1u + (bits >> (p.log_n - d));
+        if (d < p.top_levels) {
+          const char* krow = s_tree + node * (uint32_t)row_bytes;
 #pragma unroll
-      for (int t = 1; t < ILP; ++t) bt = t == t4 ? bits[t] : bt;
-      p.keys[0][path0 + s] = bt;
-      p.vals[0][path0 + s] = (uint32_t)((int64_t)l * p.S + s);
-    }
-    for (int depth = 0; depth < p.log_n; ++depth) {
-      uint4 raw[ILP][CPL];
-      float dot[ILP];
+          for (int i = 0; i < CPL; ++i) {
+            const int c = i * 4 + t4;
+            raw[u][i] = c < p.nchunks ? lds16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          }
+        } else {
+          const char* krow = kbase + (uint64_t)node * kstride;
 #pragma unroll
-      for (int t = 0; t < ILP; ++t) {
-        const int64_t node = heap_node(depth, bits[t], p.log_n);
-        const char* krow = kbase + node * kstride;
-        dot[t] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-          const int c = i * 4 + t4;
-          raw[t][i] = (c < p.nchunks && t < ns) ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < CPL; ++i) {
+            const int c = i * 4 + t4;
+            raw[u][i] = c < p.nchunks ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          }
         }
+        const float sgn = ((bits >> (p.log_n - 1 - d)) & 1u) ? -1.0f : 1.0f;
+        gl[u] = d0 + u < p.log_n ? sgn * __ldg(sig + d) * dlp : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < DU; ++u) {
 #pragma unroll
         for (int i = 0; i < CPL; ++i) {
           float kf[EPC];
-          E::unpack(raw[t][i], kf);
+          E::unpack(raw[u][i], kf);
 #pragma unroll
-          for (int e = 0; e < EPC; ++e) dot[t] = fmaf(qf[i * EPC + e], kf[e], dot[t]);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < ILP; ++t) {
-        dot[t] += __shfl_xor_sync(gmask, dot[t], 1, 4);
-        dot[t] += __shfl_xor_sync(gmask, dot[t], 2, 4);
-      }
-      float gl[ILP];
-#pragma unroll
-      for (int t = 0; t < ILP; ++t) {
-        const float x = clamp_logit(dot[t], p.max_logit);
-        const int bit = (bits[t] >> (p.log_n - 1 - depth)) & 1;
-        const float sgn = bit ? -1.0f : 1.0f;
-        gl[t] = sgn * dlp[t] / (1.0f + expf(sgn * x));
-        if (t == t4 && t < ns) p.gl[(path0 + s0 + t) * p.log_n + depth] = gl[t];
-      }
-#pragma unroll
-      for (int t = 0; t < ILP; ++t) {
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-          float kf[EPC];
-          E::unpack(raw[t][i], kf);
-#pragma unroll
-          for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(gl[t], kf[e], acc[i * EPC + e]);
+          for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(gl[u], kf[e], acc[i * EPC + e]);
         }
       }
     }
@@ -223,36 +215,117 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_query_kernel(const BwdParams 
 // ---------------------------------------------------------------------------------------
 // 3. node pass over leaf-sorted paths
 // ---------------------------------------------------------------------------------------
-template <int EL>
-struct LaneRow {  // EL consecutive row elements per lane, lanes cover the row
-  template <typename T>
-  __device__ __forceinline__ static void load(const char* row, int lane, int D, float* f) {
+__device__ __forceinline__ void ffma2(float2& acc, float2 a, float2 b) {
+  uint64_t c, x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(acc.x), "f"(acc.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc.x), "=f"(acc.y) : "l"(c));
+}
+
+// A lane's slice of a row: EP element pairs (2*EP consecutive elements), packed on load.
+template <typename T, int EP>
+struct Slice {
+  uint32_t w[sizeof(T) == 2 ? EP : 2 * EP];
+  __device__ __forceinline__ void load(const char* row, int lane, int D) {
+    const bool ok = lane * 2 * EP < D;
+    if constexpr (sizeof(T) == 2) {
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(row) + lane * EP;
+      if constexpr (EP == 2) {
+        const uint2 u = ok ? __ldg(reinterpret_cast<const uint2*>(r)) : make_uint2(0, 0);
+        w[0] = u.x; w[1] = u.y;
+      } else {
 #pragma unroll
-    for (int e = 0; e < EL; ++e) {
-      const int c = lane * EL + e;
-      f[e] = c < D ? static_cast<float>(reinterpret_cast<const T*>(row)[c]) : 0.0f;
+        for (int i = 0; i < EP; ++i) w[i] = ok ? __ldg(r + i) : 0u;
+      }
+    } else if constexpr (EP == 2) {
+      const uint4 u = ok ? __ldg(reinterpret_cast<const uint4*>(row) + lane) : make_uint4(0, 0, 0, 0);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    } else {
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(row) + lane * 2 * EP;
+#pragma unroll
+      for (int i = 0; i < 2 * EP; ++i) w[i] = ok ? __ldg(r + i) : 0u;
+    }
+  }
+  // plain (generic) loads, for rows staged in shared memory
+  __device__ __forceinline__ void load_plain(const char* row, int lane, int D) {
+    const bool ok = lane * 2 * EP < D;
+    if constexpr (sizeof(T) == 2 && EP == 2) {
+      const uint2 u = ok ? *reinterpret_cast<const uint2*>(reinterpret_cast<const uint32_t*>(row) + lane * EP)
+                         : make_uint2(0, 0);
+      w[0] = u.x; w[1] = u.y;
+    } else if constexpr (sizeof(T) == 4 && EP == 2) {
+      const uint4 u = ok ? *(reinterpret_cast<const uint4*>(row) + lane) : make_uint4(0, 0, 0, 0);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    } else {
+      constexpr int NW = sizeof(T) == 2 ? EP : 2 * EP;
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(row) + lane * NW;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) w[i] = ok ? r[i] : 0u;
+    }
+  }
+  __device__ __forceinline__ float2 pair(int i) const {
+    if constexpr (sizeof(T) == 2) {
+      float f[2];
+      Elem<T>::unpack2(w[i], f);
+      return make_float2(f[0], f[1]);
+    } else {
+      return make_float2(__uint_as_float(w[2 * i]), __uint_as_float(w[2 * i + 1]));
     }
   }
 };
 
 template <typename T>
-__device__ __forceinline__ void store_row_elems(char* row, int lane, int EL, int D, const float* f,
-                                                bool f32) {
-  for (int e = 0; e < EL; ++e) {
-    const int c = lane * EL + e;
+__device__ __forceinline__ void store_pairs(char* row, int lane, int EP, int D, const float2* f,
+                                            bool f32) {
+  for (int i = 0; i < EP; ++i) {
+    const int c = (lane * EP + i) * 2;
     if (c < D) {
-      if (f32) reinterpret_cast<float*>(row)[c] = f[e];
-      else reinterpret_cast<T*>(row)[c] = static_cast<T>(f[e]);
+      if (f32) {
+        *reinterpret_cast<float2*>(reinterpret_cast<float*>(row) + c) = f[i];
+      } else {
+        reinterpret_cast<T*>(row)[c] = static_cast<T>(f[i].x);
+        reinterpret_cast<T*>(row)[c + 1] = static_cast<T>(f[i].y);
+      }
     }
   }
 }
 
-template <typename T, int EL, int MAXD>
+constexpr int kNodeBatch = 8;  // paths staged per batch
+constexpr int kMaxLevels = 31;  // tree depths + 1 (leaf level)
+
+// Per-warp shared memory of the node pass (bytes): two staging buffers of one batch (q rows,
+// dO rows, per-depth coefficients, weight, key) plus the open-node accumulators of every
+// level and the prefix of each open node.
+__host__ __device__ inline int node_stage_bytes(int row_bytes) {
+  return kNodeBatch * (2 * row_bytes + 32 * 4 + 4 + 4 + 4) + 33 * kNodeBatch * 4;
+}
+__host__ __device__ inline int node_warp_bytes(int row_bytes, int D, int levels) {
+  return 2 * node_stage_bytes(row_bytes) + levels * D * 4 + 32 * 4;
+}
+
+// One warp walks a chunk of kChunk consecutive leaf-sorted paths of one head. Lanes own
+// 2*EP consecutive elements of D. Batches of kNodeBatch paths are staged into shared
+// memory with cp.async (double-buffered); then, level by level (depth d in [0, log_n) for
+// dK, d == log_n for dV), the warp adds the batch's contributions gl_{p,d} q_p (or w_p dO_p)
+// into the accumulator of the open node of that level, writing a node out whenever the
+// run of paths through it ends. Paths through one node are consecutive, so each node's sum
+// is formed in sorted-path order: deterministic.
+template <typename T, int EP>
 __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdParams p) {
+  extern __shared__ __align__(16) unsigned char s_node[];
   const int lane = threadIdx.x & 31;
-  const int64_t chunk = (int64_t)blockIdx.x * kNodeWarps + (threadIdx.x >> 5);
+  const int wid = threadIdx.x >> 5;
+  const int64_t chunk = (int64_t)blockIdx.x * kNodeWarps + wid;
   const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
   if (chunk >= nchunks_total) return;
+  const int row_bytes = p.D * (int)sizeof(T);
+  const int stage_bytes = node_stage_bytes(row_bytes);
+  unsigned char* wmem = s_node + (size_t)wid * node_warp_bytes(row_bytes, p.D, p.log_n + 1);
+  float* s_acc = reinterpret_cast<float*>(wmem + 2 * stage_bytes);  // [log_n + 1][D]
+  uint32_t* s_pre = reinterpret_cast<uint32_t*>(s_acc + (p.log_n + 1) * p.D);  // open node prefix
+
   const int seg = (int)(chunk / p.chunks_per_seg);
   const int cis = (int)(chunk - (int64_t)seg * p.chunks_per_seg);
   const int b = seg / p.H, h = seg - (seg / p.H) * p.H;
@@ -261,197 +334,348 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
   const int64_t i1 = min(i0 + kChunk, p.P);
   const uint32_t* keys = p.keys[p.sorted_buf] + (int64_t)seg * p.P;
   const uint32_t* vals = p.vals[p.sorted_buf] + (int64_t)seg * p.P;
+  const float* sig = p.sig + (int64_t)seg * p.P * p.sig_stride;
+  const float* dlp = p.dlp + (int64_t)seg * p.P;
 
   const int64_t base_node = ((int64_t)1 << ln) - 1;
   const int64_t K = (int64_t)p.N - 1;
-  char* dkb = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh) * (p.dk_f32 ? 4 : (int64_t)sizeof(T));
-  const int64_t dk_row = p.dks * (p.dk_f32 ? 4 : (int64_t)sizeof(T));
+  const int64_t dk_es = p.dk_f32 ? 4 : (int64_t)sizeof(T);
+  char* dkb = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh) * dk_es;
+  const int64_t dk_row = p.dks * dk_es;
   char* dvb = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh) * (int64_t)sizeof(T);
   const int64_t dv_row = p.dvs * (int64_t)sizeof(T);
+  const char* qbase = p.q + ((int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
+  const int64_t q_row = p.qs * (int64_t)sizeof(T);
+  const char* gbase = p.dout + ((int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
+  const int64_t g_row = p.gs * (int64_t)sizeof(T);
   float* part = p.partial + chunk * (int64_t)(ln + 1) * 2 * p.D;
   uint8_t* flg = p.flags + chunk * (int64_t)(ln + 1) * 2;
-  const float zeros[EL] = {};
 
-  // depth levels d in [0, ln) are internal nodes, d == ln is the leaf (dv)
-  auto node_of = [&](int d, uint32_t key) -> int64_t {
-    return d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - K;
+  // node of level d with prefix `pre` (d == ln: the leaf)
+  auto node_index = [&](int d, uint32_t pre) -> int64_t {
+    return d < ln ? ((int64_t)1 << d) - 1 + pre : (int64_t)pre + base_node - K;
   };
-  auto write_node = [&](int d, int64_t node, const float* f) {
-    if (d < ln) store_row_elems<T>(dkb + node * dk_row, lane, EL, p.D, f, p.dk_f32);
-    else store_row_elems<T>(dvb + node * dv_row, lane, EL, p.D, f, false);
+  auto write_row = [&](int d, int64_t node, const float2* f) {
+    if (d < ln) store_pairs<T>(dkb + node * dk_row, lane, EP, p.D, f, p.dk_f32);
+    else store_pairs<T>(dvb + node * dv_row, lane, EP, p.D, f, false);
   };
-  // number of depths (of ln + 1) whose node two keys share
+  auto put_partial = [&](int slot, const float2* f) {
+    float* dst = part + (int64_t)slot * p.D;
+    for (int i = 0; i < EP; ++i) {
+      const int c = (lane * EP + i) * 2;
+      if (c < p.D) *reinterpret_cast<float2*>(dst + c) = f[i];
+    }
+  };
+  const float2 zero2[EP] = {};
+  // zero the nodes of level d with prefixes in [lo, hi]
+  auto zero_range = [&](int d, int64_t lo, int64_t hi) {
+    for (int64_t pf = lo; pf <= hi; ++pf) write_row(d, node_index(d, (uint32_t)pf), zero2);
+  };
   auto shared_depths = [&](uint32_t a, uint32_t c) -> int {
     const uint32_t x = a ^ c;
     return x == 0 ? ln + 1 : ln - (32 - __clz(x)) + 1;
   };
-  // zero every node strictly between key a and key c (a < c) at depths >= d0
-  auto zero_gap = [&](uint32_t a, uint32_t c, int d0, bool incl_a, bool incl_c) {
-    for (int d = d0; d <= ln; ++d) {
-      const int sh = ln - d;
-      int64_t lo = (int64_t)(a >> sh) + (incl_a ? 0 : 1);
-      int64_t hi = (int64_t)(c >> sh) - (incl_c ? 0 : 1);
-      for (int64_t pf = lo; pf <= hi; ++pf) {
-        const int64_t node = d < ln ? ((int64_t)1 << d) - 1 + pf : pf + base_node - K;
-        write_node(d, node, zeros);
-      }
+  // stage the batch starting at sorted index ib into buffer `buf` (asynchronous)
+  auto stage = [&](int buf, int64_t ib) {
+    unsigned char* st = wmem + (size_t)buf * stage_bytes;
+    char* sq = reinterpret_cast<char*>(st);
+    char* sg = sq + kNodeBatch * row_bytes;
+    float* sco = reinterpret_cast<float*>(sg + kNodeBatch * row_bytes);
+    float* sdl = sco + kNodeBatch * 32;
+    float* sw = sdl + kNodeBatch;
+    uint32_t* skey = reinterpret_cast<uint32_t*>(sw + kNodeBatch);
+    const int nb = (int)min((int64_t)kNodeBatch, i1 - ib);
+    uint32_t pl = 0, l = 0;
+    if (lane < nb) {
+      const uint32_t key = keys[ib + lane];
+      pl = vals[ib + lane];
+      l = pl / (uint32_t)p.S;
+      const uint32_t s = pl - l * (uint32_t)p.S;
+      skey[lane] = key;
+      cp_async4(sdl + lane, dlp + pl);
+      cp_async4(sw + lane, p.weights + (((int64_t)l * p.B + b) * p.H + h) * p.S + s);
     }
+    const int cpr = row_bytes / 16;
+    const int q4 = p.sig_stride >> 2;
+    for (int r = 0; r < nb; ++r) {
+      const uint32_t lr = __shfl_sync(0xffffffffu, l, r);
+      const uint32_t pr = __shfl_sync(0xffffffffu, pl, r);
+      for (int c = lane; c < cpr; c += 32) {
+        cp_async16(sq + r * row_bytes + c * 16, qbase + (int64_t)lr * q_row + c * 16);
+        cp_async16(sg + r * row_bytes + c * 16, gbase + (int64_t)lr * g_row + c * 16);
+      }
+      if (lane < q4) cp_async16(sco + r * 32 + 4 * lane, sig + (int64_t)pr * p.sig_stride + 4 * lane);
+    }
+    cp_async_commit();
   };
 
-  float acc[MAXD + 1][EL];
-#pragma unroll
-  for (int d = 0; d <= MAXD; ++d)
-#pragma unroll
-    for (int e = 0; e < EL; ++e) acc[d][e] = 0.0f;
-
-  uint32_t first = keys[i0];
-  uint32_t open_before = 0;  // depths whose current node started before this chunk
+  // chunk start: open nodes, accumulators, flags
+  const uint32_t first = keys[i0];
+  uint32_t open_before = 0;  // levels whose open node started before this chunk
   if (i0 > 0) {
     const int sd = shared_depths(keys[i0 - 1], first);
     open_before = sd >= 32 ? 0xffffffffu : ((1u << sd) - 1u);
-  } else {
-    // nodes left of the segment's first path are unreached
-    const uint32_t lo_key = 0;
-    if (first > 0) zero_gap(lo_key, first, 0, true, false);
   }
-  for (int d = 0; d <= ln; ++d) {
+  for (int i = lane; i < (ln + 1) * p.D; i += 32) s_acc[i] = 0.0f;
+  for (int d = lane; d <= ln; d += 32) {
+    s_pre[d] = first >> (ln - d);
     flg[2 * d] = 0;
     flg[2 * d + 1] = 0;
   }
+  if (i0 == 0) {  // nodes left of the head's first path are unreached
+    for (int d = 0; d <= ln; ++d) {
+      const int64_t hi = (int64_t)(first >> (ln - d)) - 1;
+      if (hi >= 0) zero_range(d, 0, hi);
+    }
+  }
+  __syncwarp();
 
-  uint32_t prev = first;
-  for (int64_t i = i0; i < i1; ++i) {
-    const uint32_t key = keys[i];
-    const uint32_t pl = vals[i];
-    if (i > i0 && key != prev) {
-      const int sd = shared_depths(prev, key);
-      // close nodes at depths >= sd
+  stage(0, i0);
+  int buf = 0;
+  uint32_t prev = first;  // key of the path before the current batch (chunk start: itself)
+  for (int64_t ib = i0; ib < i1; ib += kNodeBatch, buf ^= 1) {
+    if (ib + kNodeBatch < i1) {
+      stage(buf ^ 1, ib + kNodeBatch);
+      cp_async_wait_1();
+    } else {
+      cp_async_wait_0();
+    }
+    __syncwarp();
+    unsigned char* st = wmem + (size_t)buf * stage_bytes;
+    const char* sq = reinterpret_cast<const char*>(st);
+    const char* sg = sq + kNodeBatch * row_bytes;
+    float* sco = reinterpret_cast<float*>(const_cast<char*>(sg) + kNodeBatch * row_bytes);
+    const float* sdl = sco + kNodeBatch * 32;
+    const float* sw = sdl + kNodeBatch;
+    const uint32_t* skey = reinterpret_cast<const uint32_t*>(sw + kNodeBatch);
+    const int nb = (int)min((int64_t)kNodeBatch, i1 - ib);
+    // coefficients gl = sgn * sigmoid(-sgn s) * dlp, transposed to [level][path] (level ln:
+    // the weights, for dV) so one level's coefficients of the batch are two float4 loads
+    float* sct = reinterpret_cast<float*>(const_cast<uint32_t*>(skey) + kNodeBatch);  // [33][8]
+    for (int idx = lane; idx < nb * 32; idx += 32) {
+      const int r = idx >> 5, d = idx & 31;
+      float co = 0.0f;
+      if (d < ln) {
+        const float sv = sco[r * 32 + d];
+        co = (((skey[r] >> (ln - 1 - d)) & 1u) ? -sv : sv) * sdl[r];
+      } else if (d == ln) {
+        co = sw[r];
+      }
+      if (d <= ln) sct[d * kNodeBatch + r] = co;
+    }
+    if (nb < kNodeBatch)
+      for (int idx = lane; idx < (ln + 1) * kNodeBatch; idx += 32)
+        if ((idx % kNodeBatch) >= nb) sct[idx] = 0.0f;
+    // run boundaries: lane d holds the bitmask of batch paths that start a new node at level d
+    uint32_t bmask = 0;
+    {
+      uint32_t pk = prev;
+      for (int r = 0; r < nb; ++r) {
+        const uint32_t kk = skey[r];
+        const int sd = shared_depths(pk, kk);
+        if (sd <= lane) bmask |= 1u << r;
+        pk = kk;
+      }
+    }
+    __syncwarp();
+    // this batch's q slices, unpacked
+    float2 qv[kNodeBatch][EP];
 #pragma unroll
-      for (int d = 0; d <= MAXD; ++d) {
-        if (d >= sd && d <= ln) {
-          const int64_t node = node_of(d, prev);
-          if ((open_before >> d) & 1u) {  // started in an earlier chunk: head partial
-            float* dst = part + (int64_t)(2 * d) * p.D;
-            for (int e = 0; e < EL; ++e)
-              if (lane * EL + e < p.D) dst[lane * EL + e] = acc[d][e];
-            flg[2 * d] = 1;
+    for (int r = 0; r < kNodeBatch; ++r) {
+      if (r < nb) {  // staged rows past the batch end are stale: keep them out of the sums
+        Slice<T, EP> row;
+        row.load_plain(sq + r * row_bytes, lane, p.D);
+#pragma unroll
+        for (int i = 0; i < EP; ++i) qv[r][i] = row.pair(i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < EP; ++i) qv[r][i] = make_float2(0.0f, 0.0f);
+      }
+    }
+    for (int d = 0; d <= ln; ++d) {
+      const bool leaf = d == ln;
+      float2 a[EP];
+      float* ad = s_acc + d * p.D;
+#pragma unroll
+      for (int i = 0; i < EP; ++i) {
+        const int c = (lane * EP + i) * 2;
+        a[i] = c < p.D ? *reinterpret_cast<const float2*>(ad + c) : make_float2(0.0f, 0.0f);
+      }
+      const float4 c0 = reinterpret_cast<const float4*>(sct + d * kNodeBatch)[0];
+      const float4 c1 = reinterpret_cast<const float4*>(sct + d * kNodeBatch)[1];
+      const float co[kNodeBatch] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const uint32_t m = __shfl_sync(0xffffffffu, bmask, d & 31);
+      if (!leaf && m == 0) {
+        // no node of this level ends inside the batch
+#pragma unroll
+        for (int r = 0; r < kNodeBatch; ++r)
+#pragma unroll
+          for (int i = 0; i < EP; ++i) {
+            a[i].x = fmaf(co[r], qv[r][i].x, a[i].x);
+            a[i].y = fmaf(co[r], qv[r][i].y, a[i].y);
+          }
+      } else {
+        uint32_t pre = s_pre[d];
+#pragma unroll
+        for (int r = 0; r < kNodeBatch; ++r) {
+          if ((m >> r) & 1u) {  // the run of node `pre` ends before path r
+            if ((open_before >> d) & 1u) {
+              put_partial(2 * d, a);
+              if (lane == 0) flg[2 * d] = 1;
+              open_before &= ~(1u << d);
+            } else {
+              write_row(d, node_index(d, pre), a);
+            }
+#pragma unroll
+            for (int i = 0; i < EP; ++i) a[i] = make_float2(0.0f, 0.0f);
+            const uint32_t npre = skey[r] >> (ln - d);
+            if (npre > pre + 1u) zero_range(d, (int64_t)pre + 1, (int64_t)npre - 1);
+            pre = npre;
+          }
+          float2 v[EP];
+          if (leaf && r < nb) {
+            Slice<T, EP> row;
+            row.load_plain(sg + r * row_bytes, lane, p.D);
+#pragma unroll
+            for (int i = 0; i < EP; ++i) v[i] = row.pair(i);
           } else {
-            write_node(d, node, acc[d]);
+#pragma unroll
+            for (int i = 0; i < EP; ++i) v[i] = qv[r][i];
           }
 #pragma unroll
-          for (int e = 0; e < EL; ++e) acc[d][e] = 0.0f;
+          for (int i = 0; i < EP; ++i) {
+            a[i].x = fmaf(co[r], v[i].x, a[i].x);
+            a[i].y = fmaf(co[r], v[i].y, a[i].y);
+          }
         }
+        if (lane == 0) s_pre[d] = pre;
       }
-      open_before &= (sd >= 32 ? 0xffffffffu : ((1u << sd) - 1u));
-      zero_gap(prev, key, sd, false, false);
-    }
-    prev = key;
-    // accumulate this path
-    const int l = (int)(pl / (uint32_t)p.S);
-    const int s = (int)(pl - (uint32_t)l * (uint32_t)p.S);
-    const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
-    const float glv = lane < ln ? p.gl[((int64_t)seg * p.P + pl) * ln + lane] : 0.0f;
-    float qf[EL], of[EL];
-    LaneRow<EL>::template load<T>(p.q + ((int64_t)l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T), lane, p.D, qf);
-    LaneRow<EL>::template load<T>(p.dout + ((int64_t)l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T), lane, p.D, of);
 #pragma unroll
-    for (int d = 0; d < MAXD; ++d) {
-      const float gd = __shfl_sync(0xffffffffu, glv, d & 31);
-      if (d < ln) {
-#pragma unroll
-        for (int e = 0; e < EL; ++e) acc[d][e] = fmaf(gd, qf[e], acc[d][e]);
+      for (int i = 0; i < EP; ++i) {
+        const int c = (lane * EP + i) * 2;
+        if (c < p.D) *reinterpret_cast<float2*>(ad + c) = a[i];
       }
     }
-    // leaf accumulator lives at index ln; MAXD >= ln so index it statically
-#pragma unroll
-    for (int d = 0; d <= MAXD; ++d) {
-      if (d == ln) {
-#pragma unroll
-        for (int e = 0; e < EL; ++e) acc[d][e] = fmaf(w, of[e], acc[d][e]);
-      }
-    }
+    prev = skey[nb - 1];
+    __syncwarp();
   }
 
   // chunk end: close or hand over every open node
   const bool has_next = i1 < p.P;
   const uint32_t nxt = has_next ? keys[i1] : 0u;
   const int sd_next = has_next ? shared_depths(prev, nxt) : 0;
+  for (int d = 0; d <= ln; ++d) {
+    float2 a[EP];
+    const float* ad = s_acc + d * p.D;
 #pragma unroll
-  for (int d = 0; d <= MAXD; ++d) {
-    if (d <= ln) {
-      const bool cont = d < sd_next;  // node continues into the next chunk
-      const bool before = (open_before >> d) & 1u;
-      if (cont) {
-        float* dst = part + (int64_t)(2 * d + (before ? 0 : 1)) * p.D;
-        for (int e = 0; e < EL; ++e)
-          if (lane * EL + e < p.D) dst[lane * EL + e] = acc[d][e];
+    for (int i = 0; i < EP; ++i) {
+      const int c = (lane * EP + i) * 2;
+      a[i] = c < p.D ? *reinterpret_cast<const float2*>(ad + c) : make_float2(0.0f, 0.0f);
+    }
+    const uint32_t pre = s_pre[d];
+    const bool cont = d < sd_next;  // node continues into the next chunk
+    const bool before = (open_before >> d) & 1u;
+    if (cont) {
+      put_partial(2 * d + (before ? 0 : 1), a);
+      if (lane == 0) {
         if (before) flg[2 * d] = 2;      // passes through this chunk
         else flg[2 * d + 1] = 1;         // starts here: this chunk owns the fix-up
-      } else if (before) {
-        float* dst = part + (int64_t)(2 * d) * p.D;
-        for (int e = 0; e < EL; ++e)
-          if (lane * EL + e < p.D) dst[lane * EL + e] = acc[d][e];
-        flg[2 * d] = 1;
-      } else {
-        write_node(d, node_of(d, prev), acc[d]);
       }
+    } else {
+      if (before) {
+        put_partial(2 * d, a);
+        if (lane == 0) flg[2 * d] = 1;
+      } else {
+        write_row(d, node_index(d, pre), a);
+      }
+      // unreached nodes up to the next path (or to the end of the level)
+      const int64_t hi = has_next ? (int64_t)(nxt >> (ln - d)) - 1 : ((int64_t)1 << d) - 1;
+      if (hi > (int64_t)pre) zero_range(d, (int64_t)pre + 1, hi);
     }
-  }
-  if (has_next) {
-    zero_gap(prev, nxt, sd_next, false, false);
-  } else {
-    // nodes right of the segment's last path are unreached
-    const uint32_t hi_key = (uint32_t)(((uint64_t)1 << ln) - 1);
-    if (prev < hi_key) zero_gap(prev, hi_key, 0, false, true);
   }
 }
 
 // ---------------------------------------------------------------------------------------
-// 4. fix-up of nodes cut by chunk boundaries
+// 4. fix-up of nodes cut by chunk boundaries: one warp per chunk, for every depth at which
+// the chunk owns a cut node; partials are added in chunk order
 // ---------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) bwd_fixup_kernel(const BwdParams p) {
   const int lane = threadIdx.x & 31;
-  const int ln = p.log_n;
-  const int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t chunk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
-  if (item >= nchunks_total * (ln + 1)) return;
-  const int64_t chunk = item / (ln + 1);
-  const int d = (int)(item - chunk * (ln + 1));
-  const uint8_t* flg = p.flags;
-  const int64_t stride = (int64_t)(ln + 1) * 2;
-  if (flg[chunk * stride + 2 * d + 1] == 0) return;  // not the owner of a cut node
+  if (chunk >= nchunks_total) return;
+  const int ln = p.log_n;
   const int seg = (int)(chunk / p.chunks_per_seg);
-  const int b = seg / p.H, h = seg - (seg / p.H) * p.H;
   const int64_t cis = chunk - (int64_t)seg * p.chunks_per_seg;
-  const int64_t i_last = min((cis + 1) * (int64_t)kChunk, p.P) - 1;
-  const uint32_t key = p.keys[p.sorted_buf][(int64_t)seg * p.P + i_last];
+  const int64_t seg_end = (int64_t)(seg + 1) * p.chunks_per_seg;  // first chunk of the next head
+  const int b = seg / p.H, h = seg - (seg / p.H) * p.H;
+  const int64_t stride = (int64_t)(ln + 1) * 2;
+  const uint8_t* flg = p.flags;
   const int64_t base_node = ((int64_t)1 << ln) - 1;
-  const int64_t node = d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - (p.N - 1);
-  for (int c0 = lane; c0 < p.D; c0 += 32) {
-    float tot = p.partial[(chunk * (ln + 1) * 2 + 2 * d + 1) * p.D + c0];
-    int64_t c = chunk + 1;
-    while (true) {
-      tot += p.partial[(c * (ln + 1) * 2 + 2 * d) * p.D + c0];
-      if (flg[c * stride + 2 * d] != 2) break;
-      ++c;
+  uint32_t key = 0;
+  bool have_key = false;
+  for (int d = 0; d <= ln; ++d) {
+    if (flg[chunk * stride + 2 * d + 1] == 0) continue;  // not the owner of a cut node
+    if (!have_key) {
+      const int64_t i_last = min((cis + 1) * (int64_t)kChunk, p.P) - 1;
+      key = p.keys[p.sorted_buf][(int64_t)seg * p.P + i_last];
+      have_key = true;
     }
-    if (d < ln) {
-      char* row = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh + node * p.dks) *
-                             (p.dk_f32 ? 4 : (int64_t)sizeof(T));
-      if (p.dk_f32) reinterpret_cast<float*>(row)[c0] = tot;
-      else reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot);
-    } else {
-      char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
-      reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot);
+    // the node spans chunk+1 .. c_end: chunks flagged "through" followed by one "ends here"
+    int64_t c_end = chunk + 1;
+    for (int64_t c0 = chunk + 1; c0 < seg_end; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const bool ends = c < seg_end && flg[c * stride + 2 * d] != 2;
+      const unsigned m = __ballot_sync(0xffffffffu, ends);
+      if (m) {
+        c_end = c0 + __ffs(m) - 1;
+        break;
+      }
+    }
+    const int64_t node = d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - (p.N - 1);
+    for (int c0 = lane * 2; c0 < p.D; c0 += 64) {
+      float2 tot = *reinterpret_cast<const float2*>(p.partial + (chunk * stride + 2 * d + 1) * p.D + c0);
+      int64_t c = chunk + 1;
+      for (; c + 4 <= c_end + 1; c += 4) {
+        float2 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = *reinterpret_cast<const float2*>(p.partial + ((c + u) * stride + 2 * d) * p.D + c0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { tot.x += v[u].x; tot.y += v[u].y; }
+      }
+      for (; c <= c_end; ++c) {
+        const float2 v = *reinterpret_cast<const float2*>(p.partial + (c * stride + 2 * d) * p.D + c0);
+        tot.x += v.x;
+        tot.y += v.y;
+      }
+      if (d < ln) {
+        char* row = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh + node * p.dks) *
+                               (p.dk_f32 ? 4 : (int64_t)sizeof(T));
+        if (p.dk_f32) {
+          *reinterpret_cast<float2*>(reinterpret_cast<float*>(row) + c0) = tot;
+        } else {
+          reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
+          reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
+        }
+      } else {
+        char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
+        reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
+        reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
+      }
     }
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// typed launchers
+// ---------------------------------------------------------------------------------------
 template <typename T, int CPL>
 void launch_query(const BwdParams& p, cudaStream_t st) {
   const int ltiles = (p.L + kBwdGroups - 1) / kBwdGroups;
-  const size_t smem = (size_t)kBwdGroups * p.S * 4;
+  const size_t smem = (size_t)kBwdGroups * p.S * 4 +
+                      (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(bwd_query_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   TA_PROFILE("bwd_query", st);
@@ -472,11 +696,13 @@ int run_query(const BwdParams& p, cudaStream_t st) {
   return check_launch("backward query pass");
 }
 
-template <typename T, int EL>
+template <typename T, int EP>
 void launch_node_el(const BwdParams& p, cudaStream_t st, unsigned grid) {
   TA_PROFILE("bwd_node", st);
-  if (p.log_n <= 16) bwd_node_kernel<T, EL, 16><<<grid, kNodeWarps * 32, 0, st>>>(p);
-  else bwd_node_kernel<T, EL, 30><<<grid, kNodeWarps * 32, 0, st>>>(p);
+  const int smem = kNodeWarps * node_warp_bytes(p.D * (int)sizeof(T), p.D, p.log_n + 1);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(bwd_node_kernel<T, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  bwd_node_kernel<T, EP><<<grid, kNodeWarps * 32, smem, st>>>(p);
 }
 
 template <typename T>
@@ -485,22 +711,20 @@ int run_rest(BwdParams& p, cudaStream_t st) {
   if (rc) return rc;
   const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
   const unsigned grid = (unsigned)((nchunks_total + kNodeWarps - 1) / kNodeWarps);
-  const int el = (p.D + 31) / 32;
-  switch (el) {
+  const int ep = (p.D + 63) / 64;  // element pairs per lane
+  switch (ep) {
     case 1: launch_node_el<T, 1>(p, st, grid); break;
     case 2: launch_node_el<T, 2>(p, st, grid); break;
-    case 3: launch_node_el<T, 3>(p, st, grid); break;
-    case 4: launch_node_el<T, 4>(p, st, grid); break;
-    case 5: case 6: case 7: case 8: launch_node_el<T, 8>(p, st, grid); break;
+    case 3: case 4: launch_node_el<T, 4>(p, st, grid); break;
     default: return fail(TA_ERR_UNSUPPORTED, "head_dim too large for the node pass");
   }
   if ((rc = check_launch("backward node pass"))) return rc;
-  const int64_t items = nchunks_total * (p.log_n + 1);
-  TA_PROFILE("bwd_fixup", st);
-  bwd_fixup_kernel<T><<<(unsigned)((items + 7) / 8), 256, 0, st>>>(p);
+  {
+    TA_PROFILE("bwd_fixup", st);
+    bwd_fixup_kernel<T><<<(unsigned)((nchunks_total + 7) / 8), 256, 0, st>>>(p);
+  }
   return check_launch("backward fix-up");
 }
-
 
 // the typed half of ta_backward: query pass, then sort + node pass + fix-up
 template <typename T>
@@ -509,4 +733,5 @@ int run_backward_typed(BwdParams& p, cudaStream_t st) {
   if (rc) return rc;
   return run_rest<T>(p, st);
 }
+
 }  // namespace ta

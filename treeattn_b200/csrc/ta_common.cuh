@@ -91,6 +91,37 @@ template <> struct Elem<__half> {
   }
 };
 
+// Dot-product step over one 16-byte chunk: acc += sum_e a[e] * b[e] in element order, with
+// float32 accumulation. 16-bit types use the sm_100 mixed-precision FMA (bf16/f16 operands,
+// f32 accumulate), which is exactly the f32 FMA of the widened operands.
+template <typename T> struct Dot;
+template <> struct Dot<float> {
+  __device__ __forceinline__ static float chunk(const uint4& a, const uint4& b, float acc) {
+    acc = fmaf(__uint_as_float(a.x), __uint_as_float(b.x), acc);
+    acc = fmaf(__uint_as_float(a.y), __uint_as_float(b.y), acc);
+    acc = fmaf(__uint_as_float(a.z), __uint_as_float(b.z), acc);
+    acc = fmaf(__uint_as_float(a.w), __uint_as_float(b.w), acc);
+    return acc;
+  }
+};
+#define TA_MIXED_FMA2(TYPE)                                                              \
+  __device__ __forceinline__ static float fma2(uint32_t a, uint32_t b, float acc) {    \
+    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n" \
+        " fma.rn.f32." TYPE " %0, al, bl, %0;\n fma.rn.f32." TYPE " %0, ah, bh, %0;\n}"  \
+        : "+f"(acc) : "r"(a), "r"(b));                                                     \
+    return acc;                                                                            \
+  }                                                                                        \
+  __device__ __forceinline__ static float chunk(const uint4& a, const uint4& b, float acc) { \
+    acc = fma2(a.x, b.x, acc);                                                             \
+    acc = fma2(a.y, b.y, acc);                                                             \
+    acc = fma2(a.z, b.z, acc);                                                             \
+    acc = fma2(a.w, b.w, acc);                                                             \
+    return acc;                                                                            \
+  }
+template <> struct Dot<__nv_bfloat16> { TA_MIXED_FMA2("bf16") };
+template <> struct Dot<__half> { TA_MIXED_FMA2("f16") };
+#undef TA_MIXED_FMA2
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
@@ -102,6 +133,43 @@ __device__ __forceinline__ uint4 ld16_stream(const void* p) {
                : "l"(p));
   return r;
 }
+__device__ __forceinline__ uint4 lds16(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Levels of a head's tree kept in shared memory by the path-walking kernels: the largest
+// T <= log_n whose 2^T - 1 node rows fit in `budget` bytes.
+__host__ __device__ inline int smem_tree_levels(int log_n, int row_bytes, int budget) {
+  int t = 0;
+  while (t < log_n && (((1ll << (t + 1)) - 1) * row_bytes) <= budget) ++t;
+  return t;
+}
+constexpr int kTreeSmemBudget = 64 * 1024;
+
+// Cooperative copy of tree rows [0, rows) of one head into shared memory (all threads of
+// the block; completes with the caller's cp_async_wait_0 + __syncthreads).
+__device__ __forceinline__ void stage_tree_rows(char* dst, const char* kbase, uint32_t kstride,
+                                                int rows, int row_bytes) {
+  const int pieces_per_row = row_bytes >> 4;
+  const int total = rows * pieces_per_row;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = i / pieces_per_row, c = i - r * pieces_per_row;
+    cp_async16(dst + (size_t)r * row_bytes + c * 16, kbase + (uint64_t)r * kstride + c * 16);
+  }
+  cp_async_commit();
+}
+
 __device__ __forceinline__ void st16(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;
 }

@@ -40,12 +40,16 @@ struct FwdParams {
   int32_t* leaf;
   float* weights;   // kFull / kReplaySoftmax: weights; kSampleOnly / kReplay: log-probs
   uint8_t* packed;  // written (kFull, kSampleOnly) or read (kReplay*)
+  float* sig;       // optional per (path, depth) σ(-sgn s) for the backward
+  int64_t P;        // paths per head (L * S)
+  int32_t sig_stride;
   const float* gumbels;
   uint64_t seed, offset, offset_step;
   FastDiv stride;
   int32_t B, L, H, S, N, log_n, nchunks, pbytes;
   float max_logit;
   int32_t mode;
+  int32_t top_levels;  // tree levels staged in shared memory
 };
 
 template <typename T, int CPL>
@@ -63,60 +67,75 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
   const int g = threadIdx.x >> 2;
   const int t4 = threadIdx.x & 3;
   const int l = lt * kFwdGroups + g;
-  if (l >= p.L) return;  // whole group leaves together
   const unsigned gmask = 0xFu << (threadIdx.x & 28);
+  const int row_bytes = p.nchunks * 16;
+  const int top_rows = (1 << p.top_levels) - 1;
+  char* s_tree = reinterpret_cast<char*>(smem);  // top tree levels of this head
+  float* s_lp = reinterpret_cast<float*>(s_tree + (size_t)top_rows * row_bytes) + g * p.S;
+  int32_t* s_leaf = reinterpret_cast<int32_t*>(s_lp - g * p.S + kFwdGroups * p.S) + g * p.S;
+  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
+  const uint32_t kstride = (uint32_t)(p.ks * (int64_t)sizeof(T));
+  if (top_rows > 0) {
+    stage_tree_rows(s_tree, kbase, kstride, top_rows, row_bytes);
+    cp_async_wait_0();
+    __syncthreads();
+  }
+  if (l >= p.L) return;  // whole group leaves together
 
-  float* s_lp = smem + g * p.S;                                   // [S] log-prob then weight
-  int32_t* s_leaf = reinterpret_cast<int32_t*>(smem + kFwdGroups * p.S) + g * p.S;  // [S]
-
-  const int64_t K = (int64_t)p.N - 1;
+  const uint32_t K = (uint32_t)p.N - 1u;
   const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
+  // per-path σ(-sgn s) rows for the backward: [b*H + h][l*S + s][sig_stride]
+  float* sig_row0 = p.sig ? p.sig + (((int64_t)b * p.H + h) * p.P + (int64_t)l * p.S) * p.sig_stride
+                          : nullptr;
 
-  // q slice of this lane
-  float qf[NE];
+  // q slice of this lane, kept in its storage format (16-byte chunks)
+  uint4 qraw[CPL];
   {
     const char* qrow = p.q + ((int64_t)l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
       const int c = i * 4 + t4;
-      if (c < p.nchunks) {
-        E::unpack(ldg16(qrow + c * 16), qf + i * EPC);
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) qf[i * EPC + e] = 0.0f;
-      }
+      qraw[i] = c < p.nchunks ? ldg16(qrow + c * 16) : make_uint4(0, 0, 0, 0);
     }
   }
-  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
-  const int64_t kstride = p.ks * (int64_t)sizeof(T);
   const bool replay = p.mode >= kReplay;
+  const uint32_t M = 2u * (uint32_t)p.L * (uint32_t)p.B * (uint32_t)p.H * (uint32_t)p.S;
 
   for (int s0 = 0; s0 < p.S; s0 += 4) {
     const int ns = min(4, p.S - s0);
-    int64_t node[4] = {0, 0, 0, 0};
+    uint32_t node[4] = {0u, 0u, 0u, 0u};
     float lp = 0.0f;  // path s0 + t4
     const uint32_t jm = j0 + s0 + t4;
+    float sig4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int depth = 0; depth < p.log_n; ++depth) {
+      uint4 raw[4][CPL];
+      if (depth < p.top_levels) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const char* krow = s_tree + node[t] * (uint32_t)row_bytes;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            const int c = i * 4 + t4;
+            raw[t][i] = (t < ns && c < p.nchunks) ? lds16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const char* krow = kbase + (uint64_t)node[t] * kstride;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            const int c = i * 4 + t4;
+            raw[t][i] = (t < ns && c < p.nchunks) ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
       float dot[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         dot[t] = 0.0f;
-        if (t < ns) {
-          const char* krow = kbase + node[t] * kstride;
-          uint4 raw[CPL];
 #pragma unroll
-          for (int i = 0; i < CPL; ++i) {
-            const int c = i * 4 + t4;
-            raw[i] = (c < p.nchunks) ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int i = 0; i < CPL; ++i) {
-            float kf[EPC];
-            E::unpack(raw[i], kf);
-#pragma unroll
-            for (int e = 0; e < EPC; ++e) dot[t] = fmaf(qf[i * EPC + e], kf[e], dot[t]);
-          }
-        }
+        for (int i = 0; i < CPL; ++i) dot[t] = Dot<T>::chunk(qraw[i], raw[t][i], dot[t]);
       }
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
@@ -134,9 +153,9 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
         } else {
           float gl, gr;
           if (p.gumbels != nullptr) {
-            const float* gp = p.gumbels + ((int64_t)depth * p.L * p.B * p.H * p.S + jm) * 2;
-            gl = gp[0];
-            gr = gp[1];
+            const float2 gg = *reinterpret_cast<const float2*>(p.gumbels + (uint64_t)depth * M + 2u * jm);
+            gl = gg.x;
+            gr = gg.y;
           } else {
             const uint64_t off = p.offset + (uint64_t)depth * p.offset_step;
             gl = torch_gumbel(p.seed, off, 2u * jm, p.stride);
@@ -145,15 +164,28 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
           dir = (lpr + gr > lpl + gl) ? 1 : 0;
         }
         lp += dir ? lpr : lpl;
+        if (sig_row0 != nullptr) {
+          // σ(-sgn s) = exp(log-prob of the branch not taken)
+          const float sv = expf(dir ? lpl : lpr);
+          const int slot = depth & 3;
+          sig4[0] = slot == 0 ? sv : sig4[0];
+          sig4[1] = slot == 1 ? sv : sig4[1];
+          sig4[2] = slot == 2 ? sv : sig4[2];
+          sig4[3] = slot == 3 ? sv : sig4[3];
+          if (slot == 3 || depth == p.log_n - 1) {
+            float* dst = sig_row0 + (int64_t)(s0 + t4) * p.sig_stride + (depth & ~3);
+            *reinterpret_cast<float4*>(dst) = make_float4(sig4[0], sig4[1], sig4[2], sig4[3]);
+          }
+        }
       }
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const int d = __shfl_sync(gmask, dir, t, 4);
-        node[t] = 2 * node[t] + 1 + d;
+        node[t] = 2u * node[t] + 1u + (uint32_t)d;
       }
     }
     if (t4 < ns) {
-      const int64_t nm = t4 == 0 ? node[0] : (t4 == 1 ? node[1] : (t4 == 2 ? node[2] : node[3]));
+      const uint32_t nm = t4 == 0 ? node[0] : (t4 == 1 ? node[1] : (t4 == 2 ? node[2] : node[3]));
       s_lp[s0 + t4] = lp;
       s_leaf[s0 + t4] = (int32_t)(nm - K);
     }
@@ -202,12 +234,12 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
 #pragma unroll
   for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
   const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-  const int64_t vstride = p.vs * (int64_t)sizeof(T);
+  const uint32_t vstride = (uint32_t)(p.vs * (int64_t)sizeof(T));
   for (int s = 0; s < p.S; ++s) {
     const float w = s_lp[s];
-    int64_t lf = s_leaf[s];
+    int32_t lf = s_leaf[s];
     lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-    const char* vrow = vbase + lf * vstride;
+    const char* vrow = vbase + (uint64_t)(uint32_t)lf * vstride;
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
       const int c = i * 4 + t4;
@@ -271,11 +303,30 @@ __global__ void __launch_bounds__(kFwdThreads) value_sum_kernel(const FwdParams 
   }
 }
 
+// Gumbel noise of `depths` draws of `numel` elements: one thread per (depth, call, subsequence)
+// computes one philox 4-vector and writes the (up to) four elements torch's grid-stride
+// loop would fill from it: e = tid + stride * (4 * call + c), c = 0..3.
 __global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t numel,
+                                                          uint32_t stride, uint32_t calls,
                                                           uint64_t seed, uint64_t offset,
-                                                          FastDiv stride) {
-  const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e < numel) out[e] = torch_gumbel(seed, offset, e, stride);
+                                                          uint64_t offset_step, int depths) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t per_depth = (uint64_t)stride * calls;
+  if (t >= per_depth * depths) return;
+  const int depth = (int)(t / per_depth);
+  const uint32_t r = (uint32_t)(t - (uint64_t)depth * per_depth);
+  const uint32_t call = r / stride;
+  const uint32_t tid = r - call * stride;
+  const uint32_t e0 = tid + stride * 4u * call;
+  if (e0 >= numel) return;
+  curandStatePhilox4_32_10_t st;
+  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * call, &st);
+  const float4 u4 = _curand_uniform4(st.output);
+  float* o = out + (uint64_t)depth * numel;
+  o[e0] = gumbel_from_uniform(u4.x);
+  if (e0 + stride < numel) o[e0 + stride] = gumbel_from_uniform(u4.y);
+  if (e0 + 2u * stride < numel) o[e0 + 2u * stride] = gumbel_from_uniform(u4.z);
+  if (e0 + 3u * stride < numel) o[e0 + 3u * stride] = gumbel_from_uniform(u4.w);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -338,7 +389,8 @@ static void launch_fwd(const FwdParams& p, cudaStream_t st, bool value_only) {
     value_sum_kernel<T, CPL><<<grid, kFwdThreads, 0, st>>>(p);
     return;
   }
-  const size_t smem = (size_t)kFwdGroups * p.S * 8;
+  const size_t smem = (size_t)kFwdGroups * p.S * 8 +
+                      (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(fwd_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   TA_PROFILE(p.mode == kFull ? "fwd_fused" : (p.mode == kSampleOnly ? "sample_paths" : "replay_paths"), st);
@@ -378,6 +430,7 @@ static void fill_common(FwdParams& p, const ta_shape* s) {
   p.log_n = floor_log2(s->num_leaves);
   p.nchunks = (int32_t)(s->head_dim * dtype_size(s->dtype) / 16);
   p.pbytes = (p.log_n + 7) / 8;
+  p.top_levels = smem_tree_levels(p.log_n, p.nchunks * 16, kTreeSmemBudget);
   p.max_logit = s->max_logit;
 }
 
@@ -407,7 +460,7 @@ using namespace ta;
 extern "C" int ta_forward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
                           ta_layout kl, const void* v, ta_layout vl, void* out, ta_layout ol,
                           const ta_rng* rng, const float* gumbels, int32_t* leaf, float* weights,
-                          uint8_t* packed, ta_stream_t stream) {
+                          uint8_t* packed, float* branch_prob, ta_stream_t stream) {
   int rc = check_shape(shape, true);
   if (rc) return rc;
   const int es = dtype_size(shape->dtype);
@@ -423,6 +476,11 @@ extern "C" int ta_forward(const ta_shape* shape, const void* q, ta_layout ql, co
   p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
   p.os = ol.seq; p.ob = ol.batch; p.oh = ol.head;
   p.leaf = leaf; p.weights = weights; p.packed = packed;
+  p.sig = branch_prob;
+  p.P = shape->num_queries * shape->num_samples;
+  p.sig_stride = (p.log_n + 3) & ~3;
+  if (branch_prob && ((uintptr_t)branch_prob & 15))
+    return fail(TA_ERR_INVALID, "branch_prob must be 16-byte aligned");
   p.mode = kFull;
   return run_fwd(p, shape->dtype, (cudaStream_t)stream, false);
 }
@@ -487,19 +545,26 @@ extern "C" int ta_weighted_value_sum(const ta_shape* shape, const void* v, ta_la
   return run_fwd(p, shape->dtype, (cudaStream_t)stream, true);
 }
 
-extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth,
-                              ta_stream_t stream) {
-  if (!out || !rng || numel < 0 || numel >= (1ll << 31) || depth < 0)
+extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth0,
+                              int32_t depths, ta_stream_t stream) {
+  if (!out || !rng || numel < 0 || numel >= (1ll << 31) || depth0 < 0 || depths < 0)
     return fail(TA_ERR_INVALID, "ta_gumbel_fill: invalid arguments");
   if (rng->draw_stride <= 0 || rng->draw_stride >= (1ll << 31) || (rng->offset & 3) ||
       (rng->offset_step & 3))
     return fail(TA_ERR_INVALID, "ta_gumbel_fill: invalid rng");
-  if (numel == 0) return TA_OK;
-  FastDiv fd;
-  fd.init((uint32_t)rng->draw_stride);
-  const unsigned grid = (unsigned)((numel + 255) / 256);
+  if (numel == 0 || depths == 0) return TA_OK;
+  const uint32_t stride = (uint32_t)rng->draw_stride;
+  const uint64_t bundles = ((uint64_t)numel + stride - 1) / stride;
+  const uint32_t calls = (uint32_t)((bundles + 3) / 4);
+  const uint64_t threads = (uint64_t)stride * calls * depths;
+  const unsigned grid = (unsigned)((threads + 255) / 256);
   TA_PROFILE("gumbel_fill", (cudaStream_t)stream);
   gumbel_fill_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      out, (uint32_t)numel, rng->seed, rng->offset + (uint64_t)depth * rng->offset_step, fd);
+      out, (uint32_t)numel, stride, calls, rng->seed,
+      rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step, depths);
   return check_launch("gumbel fill");
+}
+
+extern "C" int32_t ta_branch_prob_stride(int64_t num_leaves) {
+  return (floor_log2(num_leaves) + 3) & ~3;
 }

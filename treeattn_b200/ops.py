@@ -127,13 +127,21 @@ def reserve_gumbel_stream(device: torch.device, numel: int, depths: int) -> L.Rn
     return L.Rng(seed, offset, step, stride)
 
 
-def gumbel_fill(out: torch.Tensor, rng: L.Rng, depth: int) -> torch.Tensor:
-    """Fill float32 ``out`` with depth ``depth``'s Gumbel noise of the stream ``rng``."""
+def gumbel_fill(out: torch.Tensor, rng: L.Rng, depth0: int = 0) -> torch.Tensor:
+    """Fill float32 ``out`` (depths, numel) -- or (numel,) for one depth -- with the Gumbel
+    noise of depths depth0.. of the stream ``rng`` (bit-identical to torch's draws)."""
     _require_cuda(out)
     if out.dtype != torch.float32 or not out.is_contiguous():
         raise ValueError("out must be a contiguous float32 tensor")
-    L.call("ta_gumbel_fill", _ptr(out), out.numel(), ctypes.byref(rng), depth, _stream(out.device))
+    depths = out.shape[0] if out.dim() > 1 else 1
+    numel = out.numel() // depths
+    L.call("ta_gumbel_fill", _ptr(out), numel, ctypes.byref(rng), depth0, depths,
+           _stream(out.device))
     return out
+
+
+def branch_prob_stride(num_leaves: int) -> int:
+    return (log_n_of(num_leaves) + 3) & ~3
 
 
 # ---------------------------------------------------------------------------------------
@@ -193,17 +201,22 @@ class ForwardResult:
     leaf: torch.Tensor      # (L, B, H, S) int32
     weights: torch.Tensor   # (L, B, H, S) float32
     packed: torch.Tensor | None
+    branch_prob: torch.Tensor | None  # (B*H, L*S, stride) float32, for the backward
 
 
 def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: int, *,
             max_logit: float = MAX_LOGIT, out: torch.Tensor | None = None,
             gumbels: torch.Tensor | None = None, want_packed: bool = False,
-            rng: L.Rng | None = None) -> ForwardResult:
+            rng: L.Rng | None = None, for_backward: bool = True,
+            fused_rng: bool = False) -> ForwardResult:
     """Fused sampler + softmax + value gather. q (L,B,H,D), k_int (N-1,B,H,D), v (N,B,H,D).
 
     The Gumbel noise comes from torch's default CUDA generator (reserved here, exactly as
     the reference's per-depth draws consume it) unless ``gumbels`` (float32
-    (log2 N, L, B, H, S, 2)) or an explicit ``rng`` is given.
+    (log2 N, L, B, H, S, 2)) or an explicit ``rng`` is given. By default all depths' noise is
+    drawn first by ``ta_gumbel_fill`` (each philox 4-vector used four times);
+    ``fused_rng=True`` draws it inside the sampler instead. ``for_backward`` also returns the
+    per-path branch probabilities ``ta_backward`` needs.
     """
     _require_cuda(q, k_int, v)
     Lq, B, H, D = q.shape
@@ -220,24 +233,32 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
     if want_packed:
         packed = torch.empty((Lq, B, H, num_samples, (log_n_of(N) + 7) // 8), device=dev,
                              dtype=torch.uint8)
+    numel = Lq * B * H * num_samples * 2
+    rng_p = None
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
-        rng_p = None
     else:
         if rng is None:
-            rng = reserve_gumbel_stream(dev, Lq * B * H * num_samples * 2, log_n_of(N))
-        rng_p = ctypes.byref(rng)
+            rng = reserve_gumbel_stream(dev, numel, log_n_of(N))
+        if fused_rng:
+            rng_p = ctypes.byref(rng)
+        else:
+            gumbels = gumbel_fill(torch.empty((log_n_of(N), numel), device=dev, dtype=torch.float32), rng)
+    bp = None
+    if for_backward:
+        bp = torch.empty((B * H, Lq * num_samples, branch_prob_stride(N)), device=dev,
+                         dtype=torch.float32)
     L.call("ta_forward", ctypes.byref(shape), _ptr(q), layout(q), _ptr(k_int), layout(k_int),
            _ptr(v), layout(v), _ptr(out), layout(out), rng_p, _ptr(gumbels), _ptr(leaf),
-           _ptr(weights), _ptr(packed), _stream(dev))
+           _ptr(weights), _ptr(packed), _ptr(bp), _stream(dev))
     _note("forward")
-    return ForwardResult(out, leaf, weights, packed)
+    return ForwardResult(out, leaf, weights, packed, bp)
 
 
-def backward(q, k_int, v, grad_out, leaf, weights, num_samples, *, max_logit=MAX_LOGIT,
-             dq=None, dk=None, dv=None, dk_dtype: torch.dtype | None = None):
+def backward(q, k_int, v, grad_out, leaf, weights, branch_prob, num_samples, *,
+             max_logit=MAX_LOGIT, dq=None, dk=None, dv=None, dk_dtype: torch.dtype | None = None):
     """Deterministic gradients (dq, dk, dv) of ``forward``. All (seq, B, H, D) views."""
-    _require_cuda(q, k_int, v, grad_out, leaf, weights)
+    _require_cuda(q, k_int, v, grad_out, leaf, weights, branch_prob)
     Lq, B, H, D = q.shape
     N = v.shape[0]
     dev = q.device
@@ -257,7 +278,7 @@ def backward(q, k_int, v, grad_out, leaf, weights, num_samples, *, max_logit=MAX
     grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
     L.call("ta_backward", ctypes.byref(shape), _ptr(q), layout(q), _ptr(k_int), layout(k_int),
            _ptr(v), layout(v), _ptr(grad_out), layout(grad_out), _ptr(leaf.contiguous()),
-           _ptr(weights.contiguous()), _ptr(dq), layout(dq), _ptr(dk), layout(dk),
+           _ptr(weights.contiguous()), _ptr(branch_prob), _ptr(dq), layout(dq), _ptr(dk), layout(dk),
            dtype_code(dk.dtype), _ptr(dv), layout(dv), _ptr(ws), ws_bytes, _stream(dev))
     _note("backward")
     return dq, dk, dv
