@@ -326,3 +326,30 @@ def test_collapsed_paths_all_queries_one_leaf():
     np.testing.assert_allclose(dv.cpu().numpy(), rv, atol=1e-3, rtol=1e-4)
     np.testing.assert_allclose(dk.cpu().numpy(), rk, atol=1e-3, rtol=1e-4)
     np.testing.assert_allclose(dq.cpu().numpy(), rq, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("L,N,B,H,D,S", [(512, 512, 1, 2, 128, 8), (4, 4096, 1, 1, 64, 8),
+                                         (300, 1024, 2, 3, 32, 5), (1024, 256, 1, 2, 96, 16),
+                                         (64, 128, 1, 1, 256, 4)])
+def test_backward_bf16_tensor_core_node_pass(L, N, B, H, D, S):
+    """bf16 head_dim % 32 == 0 takes the mma.sync node pass: dense, sparse (many rows per
+    chunk and unreached nodes), odd sample counts, D up to 256."""
+    torch.manual_seed(L + N + D)
+    q = torch.randn(L, B, H, D, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(N - 1, B, H, D, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(N, B, H, D, device=DEV, dtype=torch.bfloat16)
+    go = torch.randn(L, B, H, D, device=DEV, dtype=torch.bfloat16)
+    torch.manual_seed(2)
+    res = ops.forward(q, k, v, S)
+    dq, dk, dv = ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S,
+                              dk_dtype=torch.float32)
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    rq, rk, rv = O.backward(f(q), f(k), f(v), f(go), res.leaf.cpu().numpy().astype(np.int64),
+                            res.weights.cpu().numpy())
+    np.testing.assert_allclose(f(dk), rk, atol=2e-4, rtol=2e-4)  # float32 output
+    np.testing.assert_allclose(f(dv), rv, atol=2e-2, rtol=1e-2)  # bf16 outputs
+    np.testing.assert_allclose(f(dq), rq, atol=2e-2, rtol=1e-2)
+    # deterministic
+    dq2, dk2, dv2 = ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S,
+                                 dk_dtype=torch.float32)
+    assert torch.equal(dk, dk2) and torch.equal(dv, dv2) and torch.equal(dq, dq2)

@@ -134,13 +134,17 @@ struct BwdLayout {
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+static int chunk_of(const ta_shape* s) {
+  return use_mma_node_pass(s->dtype, s->head_dim) ? kChunkMma : kChunk;
+}
+
 static BwdLayout bwd_layout(const ta_shape* s) {
   BwdLayout w{};
   const int64_t HB = s->batch * s->num_heads;
   const int64_t P = s->num_queries * s->num_samples;
   const int ln = floor_log2(s->num_leaves);
   const int64_t tiles = (P + kSortTile - 1) / kSortTile;
-  const int64_t chunks = HB * ((P + kChunk - 1) / kChunk);
+  const int64_t chunks = HB * ((P + chunk_of(s) - 1) / chunk_of(s));
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   w.keys[0] = take(HB * P * 4);
@@ -237,7 +241,8 @@ extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, c
   p.dk_f32 = dk_dtype == TA_F32 ? 1 : 0;
   p.P = shape->num_queries * shape->num_samples;
   p.tiles_per_seg = (int32_t)((p.P + kSortTile - 1) / kSortTile);
-  p.chunks_per_seg = (int32_t)((p.P + kChunk - 1) / kChunk);
+  p.chunk = chunk_of(shape);
+  p.chunks_per_seg = (int32_t)((p.P + p.chunk - 1) / p.chunk);
   p.max_logit = shape->max_logit;
   if (p.log_n > 30) return fail(TA_ERR_UNSUPPORTED, "tree too deep");
   cudaStream_t st = (cudaStream_t)stream;

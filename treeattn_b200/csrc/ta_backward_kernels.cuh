@@ -24,6 +24,8 @@
 //      (a fixed split over the CTA's warps, combined in warp order) and writes the node.
 #pragma once
 
+#include <type_traits>
+
 #include "ta_common.cuh"
 
 namespace ta {
@@ -60,7 +62,14 @@ struct BwdParams {
   int32_t sorted_buf;  // which keys/vals buffer holds the sorted records
   float max_logit;
   int32_t top_levels;  // tree levels staged in shared memory by the query pass
+  int32_t chunk;       // sorted paths per node-pass chunk
 };
+
+// The tensor-core node pass serves bf16 inputs whose head_dim is a multiple of 32 (<= 256).
+inline bool use_mma_node_pass(int32_t dtype, int64_t D) {
+  return dtype == TA_BF16 && D % 32 == 0 && D <= 256 && D / 32 != 5 && D / 32 != 6 && D / 32 != 7;
+}
+constexpr int kChunkMma = 128;
 
 // radix-sort kernels (ta_backward.cu)
 __global__ void sort_hist_kernel(const BwdParams p, int src, int shift);
@@ -330,8 +339,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
   const int cis = (int)(chunk - (int64_t)seg * p.chunks_per_seg);
   const int b = seg / p.H, h = seg - (seg / p.H) * p.H;
   const int ln = p.log_n;
-  const int64_t i0 = (int64_t)cis * kChunk;
-  const int64_t i1 = min(i0 + kChunk, p.P);
+  const int64_t i0 = (int64_t)cis * p.chunk;
+  const int64_t i1 = min(i0 + p.chunk, p.P);
   const uint32_t* keys = p.keys[p.sorted_buf] + (int64_t)seg * p.P;
   const uint32_t* vals = p.vals[p.sorted_buf] + (int64_t)seg * p.P;
   const float* sig = p.sig + (int64_t)seg * p.P * p.sig_stride;
@@ -596,15 +605,18 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
 }
 
 // ---------------------------------------------------------------------------------------
-// 4. fix-up of nodes cut by chunk boundaries: one warp per chunk, for every depth at which
-// the chunk owns a cut node; partials are added in chunk order
+// 4. fix-up of nodes cut by chunk boundaries: one CTA per chunk, for every level at which
+// the chunk owns a cut node. The chunks the node spans are split into contiguous ranges,
+// one per warp (each summed in chunk order), and the warp sums are added in warp order.
 // ---------------------------------------------------------------------------------------
+constexpr int kFixWarps = 4;
+
 template <typename T>
-__global__ void __launch_bounds__(256) bwd_fixup_kernel(const BwdParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t chunk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
-  if (chunk >= nchunks_total) return;
+__global__ void __launch_bounds__(kFixWarps * 32) bwd_fixup_kernel(const BwdParams p) {
+  __shared__ float s_part[kFixWarps][256];
+  __shared__ int64_t s_cend;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t chunk = blockIdx.x;
   const int ln = p.log_n;
   const int seg = (int)(chunk / p.chunks_per_seg);
   const int64_t cis = chunk - (int64_t)seg * p.chunks_per_seg;
@@ -618,55 +630,81 @@ __global__ void __launch_bounds__(256) bwd_fixup_kernel(const BwdParams p) {
   for (int d = 0; d <= ln; ++d) {
     if (flg[chunk * stride + 2 * d + 1] == 0) continue;  // not the owner of a cut node
     if (!have_key) {
-      const int64_t i_last = min((cis + 1) * (int64_t)kChunk, p.P) - 1;
+      const int64_t i_last = min((cis + 1) * (int64_t)p.chunk, p.P) - 1;
       key = p.keys[p.sorted_buf][(int64_t)seg * p.P + i_last];
       have_key = true;
     }
     // the node spans chunk+1 .. c_end: chunks flagged "through" followed by one "ends here"
-    int64_t c_end = chunk + 1;
-    for (int64_t c0 = chunk + 1; c0 < seg_end; c0 += 32) {
-      const int64_t c = c0 + lane;
-      const bool ends = c < seg_end && flg[c * stride + 2 * d] != 2;
-      const unsigned m = __ballot_sync(0xffffffffu, ends);
-      if (m) {
-        c_end = c0 + __ffs(m) - 1;
-        break;
+    if (warp == 0) {
+      int64_t c_end = chunk + 1;
+      for (int64_t c0 = chunk + 1; c0 < seg_end; c0 += 32) {
+        const int64_t c = c0 + lane;
+        const bool ends = c < seg_end && flg[c * stride + 2 * d] != 2;
+        const unsigned m = __ballot_sync(0xffffffffu, ends);
+        if (m) {
+          c_end = c0 + __ffs(m) - 1;
+          break;
+        }
       }
+      if (lane == 0) s_cend = c_end;
     }
-    const int64_t node = d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - (p.N - 1);
+    __syncthreads();
+    const int64_t c_end = s_cend;
+    const int64_t span = c_end - chunk;  // chunks after this one
+    const int64_t per = (span + kFixWarps - 1) / kFixWarps;
+    const int64_t c_lo = chunk + 1 + warp * per;
+    const int64_t c_hi = min(chunk + 1 + (warp + 1) * per, c_end + 1);
     for (int c0 = lane * 2; c0 < p.D; c0 += 64) {
-      float2 tot = *reinterpret_cast<const float2*>(p.partial + (chunk * stride + 2 * d + 1) * p.D + c0);
-      int64_t c = chunk + 1;
-      for (; c + 4 <= c_end + 1; c += 4) {
-        float2 v[4];
+      float2 tot = make_float2(0.0f, 0.0f);
+      int64_t c = c_lo;
+      for (; c + 8 <= c_hi; c += 8) {
+        float2 v[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 8; ++u)
           v[u] = *reinterpret_cast<const float2*>(p.partial + ((c + u) * stride + 2 * d) * p.D + c0);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) { tot.x += v[u].x; tot.y += v[u].y; }
+        for (int u = 0; u < 8; ++u) { tot.x += v[u].x; tot.y += v[u].y; }
       }
-      for (; c <= c_end; ++c) {
+      for (; c < c_hi; ++c) {
         const float2 v = *reinterpret_cast<const float2*>(p.partial + (c * stride + 2 * d) * p.D + c0);
         tot.x += v.x;
         tot.y += v.y;
       }
-      if (d < ln) {
-        char* row = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh + node * p.dks) *
-                               (p.dk_f32 ? 4 : (int64_t)sizeof(T));
-        if (p.dk_f32) {
-          *reinterpret_cast<float2*>(reinterpret_cast<float*>(row) + c0) = tot;
+      s_part[warp][c0] = tot.x;
+      s_part[warp][c0 + 1] = tot.y;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int64_t node = d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - (p.N - 1);
+      for (int c0 = lane * 2; c0 < p.D; c0 += 64) {
+        float2 tot = *reinterpret_cast<const float2*>(p.partial + (chunk * stride + 2 * d + 1) * p.D + c0);
+        for (int w = 0; w < kFixWarps; ++w) {
+          tot.x += s_part[w][c0];
+          tot.y += s_part[w][c0 + 1];
+        }
+        if (d < ln) {
+          char* row = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh + node * p.dks) *
+                                 (p.dk_f32 ? 4 : (int64_t)sizeof(T));
+          if (p.dk_f32) {
+            *reinterpret_cast<float2*>(reinterpret_cast<float*>(row) + c0) = tot;
+          } else {
+            reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
+            reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
+          }
         } else {
+          char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
           reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
           reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
         }
-      } else {
-        char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
-        reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
-        reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
       }
     }
+    __syncthreads();
   }
 }
+
+}  // namespace ta
+#include "ta_backward_mma.cuh"
+namespace ta {
 
 // ---------------------------------------------------------------------------------------
 // typed launchers
@@ -709,6 +747,27 @@ template <typename T>
 int run_rest(BwdParams& p, cudaStream_t st) {
   int rc = run_sort(p, st);
   if (rc) return rc;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (p.chunk == kChunkMma) {
+      {
+        TA_PROFILE("bwd_node", st);
+        switch (p.D / 32) {
+          case 1: launch_node_mma<1>(p, st); break;
+          case 2: launch_node_mma<2>(p, st); break;
+          case 3: launch_node_mma<3>(p, st); break;
+          case 4: launch_node_mma<4>(p, st); break;
+          default: launch_node_mma<8>(p, st); break;
+        }
+      }
+      if ((rc = check_launch("backward node pass"))) return rc;
+      const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
+      {
+        TA_PROFILE("bwd_fixup", st);
+        bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
+      }
+      return check_launch("backward fix-up");
+    }
+  }
   const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
   const unsigned grid = (unsigned)((nchunks_total + kNodeWarps - 1) / kNodeWarps);
   const int ep = (p.D + 63) / 64;  // element pairs per lane
@@ -721,7 +780,7 @@ int run_rest(BwdParams& p, cudaStream_t st) {
   if ((rc = check_launch("backward node pass"))) return rc;
   {
     TA_PROFILE("bwd_fixup", st);
-    bwd_fixup_kernel<T><<<(unsigned)((nchunks_total + 7) / 8), 256, 0, st>>>(p);
+    bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
   }
   return check_launch("backward fix-up");
 }
