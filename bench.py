@@ -301,21 +301,29 @@ _SHARED = {}
 
 
 def _cpu_heads(hs):
+    """Oracle work for heads [hs[0], hs[1]): (tree-build seconds, query seconds)."""
     from oracle import tree_oracle as O
 
     d = _SHARED
     sl = slice(hs[0], hs[1])
+    t0 = time.perf_counter()
     k_int = O.haar_internal_node_keys(d["k"][:, :, sl], "bf16")
-    t_build = time.perf_counter()
+    O.haar_internal_node_keys_backward(np.zeros_like(k_int))
+    t1 = time.perf_counter()
     q, v, go, g = d["q"][:, :, sl], d["v"][:, :, sl], d["go"][:, :, sl], d["g"][:, :, :, sl]
     fw = O.forward(q, k_int, v, g, d["P"])
-    dq, dk, dv = O.backward(q, k_int, v, go, fw["leaf"], fw["weights"])
-    O.haar_internal_node_keys_backward(dk)
-    return t_build
+    O.backward(q, k_int, v, go, fw["leaf"], fw["weights"])
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
 
 
 def cpu_reference(args, budget_s=20.0):
-    """Time the oracle on all S tree nodes but only Ls queries; extrapolate to a full step."""
+    """Time the oracle on all S tree nodes but only Ls queries; extrapolate to a full step.
+
+    Each worker process owns a slice of the heads and times the tree build (all S keys) and
+    the fwd+bwd of the Ls sampled queries separately; a full step is
+    max(build) + max(query) * S / Ls.
+    """
     import multiprocessing as mp
 
     sys.path.insert(0, ROOT)
@@ -331,39 +339,22 @@ def cpu_reference(args, budget_s=20.0):
     cores = min(os.cpu_count() or 1, H)
     chunks = [(i * H // cores, (i + 1) * H // cores) for i in range(cores)]
     ctx = mp.get_context("fork")
-    # time the tree build alone and build + Ls queries, over the same pool
-    times = []
+    samples = []
     with ctx.Pool(cores) as pool:
         deadline = time.perf_counter() + budget_s
         while True:
-            t0 = time.perf_counter()
-            pool.map(_cpu_heads, chunks)
-            t_all = time.perf_counter() - t0
-            times.append(t_all)
-            if time.perf_counter() > deadline or len(times) >= 3:
+            res = pool.map(_cpu_heads, chunks)
+            samples.append((max(r[0] for r in res), max(r[1] for r in res)))
+            if time.perf_counter() > deadline or len(samples) >= 3:
                 break
-    t_sample = min(times)
-    # separate the full-tree build from the per-query work
-    with ctx.Pool(cores) as pool:
-        t0 = time.perf_counter()
-        pool.map(_build_only, chunks)
-        t_build = time.perf_counter() - t0
-    t_query = max(t_sample - t_build, 1e-9)
+    t_build = min(s[0] for s in samples)
+    t_query = min(s[1] for s in samples)
     t_step = t_build + t_query * (S / Ls)
     return {"value": B * S / t_step, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"numpy oracle (oracle/tree_oracle.py), Haar build of all {S} keys + fwd/bwd "
-                      f"of {Ls} of {S} queries x {H} heads, {cores} processes over heads; "
-                      f"full step extrapolated = build + query part x {S // Ls}",
-            "sample_s": t_sample, "extrapolated_step_s": t_step}
-
-
-def _build_only(hs):
-    from oracle import tree_oracle as O
-
-    sl = slice(hs[0], hs[1])
-    k_int = O.haar_internal_node_keys(_SHARED["k"][:, :, sl], "bf16")
-    dk = np.zeros_like(k_int)
-    O.haar_internal_node_keys_backward(dk)
+            "sample": f"numpy oracle (oracle/tree_oracle.py), Haar build + transpose of all {S} keys "
+                      f"and fwd+bwd of {Ls} of {S} queries x {H} heads, {cores} processes over heads; "
+                      f"step = build + query part x {S // Ls}",
+            "build_s": t_build, "query_sample_s": t_query, "extrapolated_step_s": t_step}
 
 
 def run_reference(args):
@@ -375,7 +366,7 @@ def run_reference(args):
     vals = [r["value"]]
     value = r["value"]
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": len(vals), "warmup": args.warmup,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": args.seq_len / value * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1), bf16-rounded", "config": {**WORKLOAD, "batch_per_gpu": 1},
