@@ -299,3 +299,162 @@ def adapter_forward_backward(q_bshd, k_bshd, v_bshd, grad_out_bshd, gumbels, num
     t = lambda x: np.ascontiguousarray(np.transpose(x, (1, 0, 2, 3)))  # noqa: E731
     return dict(out=t(round_to_dtype(fw["out"], dtype)), dq=t(dq), dk=t(dk), dv=t(dv),
                 weights=fw["weights"], leaf=fw["leaf"])
+
+
+# --------------------------------------------------------------------------------------
+# A10: deterministic (exact) tree attention  (_tree_mha.py:271-321)
+# --------------------------------------------------------------------------------------
+
+def leaf_log_probs(q, k):
+    """log p(leaf n | q) = sum over the path's levels of logsigmoid(+-q.k[node]) (power-of-two N).
+
+    q (L,B,H,D), k (K,B,H,D) -> (L,B,H,N) float32, leaves in index order (_tree_mha.py:285-306).
+    """
+    L, B, H, D = q.shape
+    K = k.shape[0]
+    N = K + 1
+    log_n = log_n_of(N)
+    dots = np.einsum("lbhd,kbhd->lbhk", q.astype(np.float32), k.astype(np.float32),
+                     dtype=np.float32)
+    lp = np.zeros((L, B, H, 1), dtype=np.float32)
+    for d in range(log_n):
+        s = dots[..., (1 << d) - 1:(1 << (d + 1)) - 1]          # nodes of level d in order
+        left, right = log_sigmoid_pair(s)
+        lp = np.stack([lp + left, lp + right], axis=-1).reshape(L, B, H, -1).astype(np.float32)
+    return lp
+
+
+def deterministic_attention(q, k, v, is_causal, query_offset=0):
+    """Exact attention over all N root-to-leaf paths (_tree_mha.py:271-321).
+
+    Non-causal: weights = exp(log p(leaf)); causal: leaves n > l + query_offset masked, then
+    softmax over the leaves. Returns (out (L,B,H,D) f32, weights (L,B,H,N) f32).
+    """
+    lp = leaf_log_probs(q, k)
+    L = q.shape[0]
+    N = lp.shape[-1]
+    if is_causal:
+        mask = np.arange(N)[None, :] > (np.arange(L)[:, None] + query_offset)
+        lp = np.where(mask[:, None, None, :], -np.inf, lp)
+        m = lp.max(-1, keepdims=True)
+        e = np.exp(lp - m)
+        w = (e / e.sum(-1, keepdims=True)).astype(np.float32)
+    else:
+        w = np.exp(lp).astype(np.float32)
+    out = np.einsum("lbhn,nbhd->lbhd", w, v.astype(np.float32), dtype=np.float32)
+    return out, w
+
+
+# --------------------------------------------------------------------------------------
+# A9: causal sampler  (_tree_mha.py:125-268)
+# --------------------------------------------------------------------------------------
+
+def _lse2(a, b):
+    m = np.maximum(a, b)
+    m_safe = np.where(np.isfinite(m), m, 0.0)
+    return (m_safe + np.log(np.exp(a - m_safe) + np.exp(b - m_safe))).astype(np.float32)
+
+
+def boundary_log_masses(q_t, k, boundary, log_n):
+    """Pass 1 of the causal sampler for one query: masses M[d] along the boundary path.
+
+    q_t (B,H,D); returns (nodes [log_n], M (B,H,log_n+1) with M[log_n] = 0, dots (B,H,log_n)).
+    M[d] = logsumexp(M[d+1] + lp_on, off_mass + lp_off) where the off-path child is masked
+    (-inf) when the boundary goes left, and counts log(#leaves of the left subtree) when it
+    goes right (_tree_mha.py:145-196).
+    """
+    nodes = []
+    node = 0
+    for d in range(log_n):
+        nodes.append(node)
+        node = 2 * node + 1 + ((boundary >> (log_n - 1 - d)) & 1)
+    kb = k[nodes].astype(np.float32)                       # (log_n, B, H, D)
+    dots = np.einsum("bhd,pbhd->bhp", q_t.astype(np.float32), kb, dtype=np.float32)
+    B, H = q_t.shape[:2]
+    M = np.zeros((B, H, log_n + 1), dtype=np.float32)
+    for d in range(log_n - 1, -1, -1):
+        direction = (boundary >> (log_n - 1 - d)) & 1
+        left, right = log_sigmoid_pair(dots[..., d])
+        if direction == 0:
+            on, off, off_mass = left, right, np.float32(-np.inf)
+        else:
+            on, off = right, left
+            off_mass = np.float32(np.log(np.float32(1 << (log_n - 1 - d))))
+        M[..., d] = _lse2(M[..., d + 1] + on, off_mass + off)
+    return nodes, M, dots
+
+
+def sample_paths_causal(q, k, gumbels, num_samples, causal_offset=0):
+    """Causal Gumbel-max sampling with the reference's two-pass boundary correction.
+
+    q (L,B,H,D), k (K,B,H,D); gumbels (L, log_n, B, H, S, 2) float32 -- one draw per (query,
+    level) as the reference draws them (_tree_mha.py:255). The correction of level d applies
+    only when EVERY (b, h, s) sample sits on the boundary node (_tree_mha.py:204-207).
+    Returns (leaf (L,B,H,S), log_prob (L,B,H,S), corrected_levels (L,) int).
+    """
+    L, B, H, D = q.shape
+    K = k.shape[0]
+    N = K + 1
+    log_n = log_n_of(N)
+    S = num_samples
+    bidx = np.arange(B)[:, None, None]
+    hidx = np.arange(H)[None, :, None]
+    leaves = np.zeros((L, B, H, S), dtype=np.int64)
+    lps = np.zeros((L, B, H, S), dtype=np.float32)
+    ncorr = np.zeros(L, dtype=np.int64)
+    k32 = k.astype(np.float32)
+    for t in range(L):
+        boundary = t + causal_offset
+        bnodes, M, _ = boundary_log_masses(q[t], k, boundary, log_n)
+        node = np.zeros((B, H, S), dtype=np.int64)
+        acc = np.zeros((B, H, S), dtype=np.float32)
+        corr = 0
+        for d in range(log_n):
+            on_path = bool(np.all(node == bnodes[d]))
+            kn = k32[node, bidx, hidx]                           # (B,H,S,D)
+            s = np.einsum("bhd,bhsd->bhs", q[t].astype(np.float32), kn, dtype=np.float32)
+            left, right = log_sigmoid_pair(s)
+            if on_path:
+                corr = d + 1
+                bdir = (boundary >> (log_n - 1 - d)) & 1
+                parent = M[..., d][..., None]
+                child = M[..., d + 1][..., None]
+                if bdir == 0:
+                    m_left, m_right = child, np.float32(-np.inf)
+                else:
+                    m_left = np.float32(np.log(np.float32(1 << (log_n - 1 - d))))
+                    m_right = child
+                left = (m_left + left - parent).astype(np.float32)
+                right = (m_right + right - parent).astype(np.float32)
+            g = gumbels[t, d]
+            direction = ((right + g[..., 1]) > (left + g[..., 0])).astype(np.int64)
+            acc = (acc + np.where(direction == 1, right, left)).astype(np.float32)
+            node = 2 * node + 1 + direction
+        leaves[t] = node - K
+        lps[t] = acc
+        ncorr[t] = corr
+    return leaves, lps, ncorr
+
+
+def causal_attention(q, k, v, gumbels, num_samples):
+    """hierarchical_attention(..., is_causal=True, mode='stochastic') (_tree_mha.py:379-412).
+
+    L > S: the first S queries take exact causal attention, the rest are sampled with causal
+    offset S (gumbels then cover only those L - S queries). Returns dict(out, weights, leaf).
+    """
+    L = q.shape[0]
+    S = num_samples
+    hybrid = L > S
+    if hybrid:
+        out_det, _ = deterministic_attention(q[:S], k, v, True)
+        leaf, lp, _ = sample_paths_causal(q[S:], k, gumbels, S, causal_offset=S)
+    else:
+        leaf, lp, _ = sample_paths_causal(q, k, gumbels, S, causal_offset=0)
+    N = v.shape[0]
+    lp = np.where((leaf >= 0) & (leaf < N), lp, -np.inf)
+    m = lp.max(-1, keepdims=True)
+    e = np.exp(lp - m)
+    w = (e / e.sum(-1, keepdims=True)).astype(np.float32)
+    out_sto = weighted_value_sum(v, leaf, w)
+    out = np.concatenate([out_det, out_sto], axis=0) if hybrid else out_sto
+    return dict(out=out, weights=w, leaf=leaf)

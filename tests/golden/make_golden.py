@@ -16,6 +16,12 @@ attn-bench's Haar tree build) on CPU, drives them with seeded inputs, and record
 * ``haar_*.npz``  -- haar_internal_node_keys forward + autograd backward in f32/f16/bf16.
 * ``adapter_*.npz`` -- the attn-bench treeattn_cuda adapter fn(q,k,v) end to end in bshd
   (Haar build + attention + backward), fp32 and bf16.
+* ``causal_*.npz`` -- treeattn-torch hierarchical_attention(is_causal=True, stochastic): the
+  exact causal prefix for the first S queries and the boundary-corrected sampler for the
+  rest, with its recorded noise (one (B,H,S,2) draw per query and level) and gradients.
+* ``exact_*.npz`` -- mode="deterministic" (all leaves), causal and not, with gradients.
+
+``python tests/golden/make_golden.py REF [attention|haar|adapter|causal ...]`` regenerates a subset.
 
 The fixtures are small; the tests never need the reference at run time.
 """
@@ -116,6 +122,51 @@ def make_attention(torch, out_dir):
         print("wrote", name)
 
 
+def make_causal(torch, out_dir):
+    """Causal stochastic mode (hybrid exact prefix + corrected sampler) and exact mode."""
+    import treeattn_torch
+
+    for (L, B, H, D, S) in [(4, 1, 2, 16, 4), (16, 1, 2, 16, 4), (32, 2, 2, 16, 8),
+                            (64, 1, 2, 32, 4)]:
+        E = H * D
+        torch.manual_seed(4321)
+        q = torch.randn(L, B, E)
+        k = torch.randn(L - 1, B, E)
+        v = torch.randn(L, B, E)
+        g = torch.randn(L, B, E)
+        qt, kt, vt = (x.clone().requires_grad_(True) for x in (q, k, v))
+        torch.manual_seed(0)
+        with GumbelRecorder(torch) as rec:
+            out, w = treeattn_torch.hierarchical_attention(
+                qt, kt, vt, num_heads=H, is_causal=True, mode="stochastic", num_samples=S)
+        out.backward(g)
+        log_n = (L - 1).bit_length()
+        lsto = L - S if L > S else L
+        gum = np.stack([_np(t) for t in rec.tensors]).reshape(lsto, log_n, B, H, S, 2)
+        fn = os.path.join(out_dir, f"causal_L{L}_B{B}_H{H}_D{D}_S{S}.npz")
+        np.savez_compressed(fn, q=_np(q), k=_np(k), v=_np(v), grad_out=_np(g), gumbels=gum,
+                            out=_np(out), weights=_np(w), dq=_np(qt.grad), dk=_np(kt.grad),
+                            dv=_np(vt.grad), shape=np.array([L, B, H, D, S]))
+        print("wrote", fn)
+    for causal in (False, True):
+        for (L, B, H, D) in [(16, 1, 2, 16), (32, 2, 2, 16)]:
+            E = H * D
+            torch.manual_seed(99)
+            q = torch.randn(L, B, E)
+            k = torch.randn(L - 1, B, E)
+            v = torch.randn(L, B, E)
+            g = torch.randn(L, B, E)
+            qt, kt, vt = (x.clone().requires_grad_(True) for x in (q, k, v))
+            out, w = treeattn_torch.hierarchical_attention(
+                qt, kt, vt, num_heads=H, is_causal=causal, mode="deterministic")
+            out.backward(g)
+            fn = os.path.join(out_dir, f"exact_{'causal' if causal else 'full'}_L{L}_B{B}_H{H}_D{D}.npz")
+            np.savez_compressed(fn, q=_np(q), k=_np(k), v=_np(v), grad_out=_np(g), out=_np(out),
+                                weights=_np(w), dq=_np(qt.grad), dk=_np(kt.grad), dv=_np(vt.grad),
+                                shape=np.array([L, B, H, D]))
+            print("wrote", fn)
+
+
 def make_haar(torch, out_dir):
     from attn_bench.baselines._treeattn_common import haar_internal_node_keys
 
@@ -167,9 +218,15 @@ def main():
 
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     out_dir = os.path.dirname(os.path.abspath(__file__))
-    make_attention(torch, out_dir)
-    make_haar(torch, out_dir)
-    make_adapter(torch, out_dir)
+    which = sys.argv[2:] or ["attention", "haar", "adapter", "causal"]
+    if "attention" in which:
+        make_attention(torch, out_dir)
+    if "haar" in which:
+        make_haar(torch, out_dir)
+    if "adapter" in which:
+        make_adapter(torch, out_dir)
+    if "causal" in which:
+        make_causal(torch, out_dir)
 
 
 if __name__ == "__main__":

@@ -78,3 +78,55 @@ def test_oracle_adapter_matches_reference(path):
     np.testing.assert_allclose(res["out"], f["out"], atol=tol["out"], rtol=tol["out"])
     for n in ("dq", "dk", "dv"):
         np.testing.assert_allclose(res[n], f[n], atol=tol["g"], rtol=tol["g"], err_msg=n)
+
+
+CAUSAL = sorted(glob.glob(os.path.join(GOLDEN, "causal_*.npz")))
+EXACT = sorted(glob.glob(os.path.join(GOLDEN, "exact_*.npz")))
+
+
+def test_causal_fixtures_present():
+    assert len(CAUSAL) == 4 and len(EXACT) == 4
+
+
+@pytest.mark.parametrize("path", CAUSAL, ids=os.path.basename)
+def test_oracle_causal_matches_reference(path):
+    import torch
+
+    from oracle import tree_oracle_torch as OT
+
+    f = np.load(path)
+    L, B, H, D, S = (int(x) for x in f["shape"])
+    q, k, v, g = (_heads(f[n], H) for n in ("q", "k", "v", "grad_out"))
+    res = O.causal_attention(q, k, v, f["gumbels"], S)
+    np.testing.assert_allclose(res["out"].reshape(L, B, -1), f["out"], atol=5e-5, rtol=5e-5)
+    np.testing.assert_allclose(res["weights"], f["weights"], atol=5e-5, rtol=5e-5)
+    # the torch restatement reproduces outputs and the reference's autograd gradients
+    qt, kt, vt = (torch.tensor(x, requires_grad=True) for x in (q, k, v))
+    out, w, leaf = OT.causal_attention(qt, kt, vt, torch.tensor(f["gumbels"]), S)
+    np.testing.assert_array_equal(leaf.numpy(), res["leaf"])
+    out.backward(torch.tensor(g))
+    np.testing.assert_allclose(out.detach().numpy().reshape(L, B, -1), f["out"], atol=5e-5, rtol=5e-5)
+    for name, t in (("dq", qt), ("dk", kt), ("dv", vt)):
+        np.testing.assert_allclose(t.grad.numpy().reshape(f[name].shape), f[name], atol=2e-4,
+                                   rtol=2e-4, err_msg=name)
+
+
+@pytest.mark.parametrize("path", EXACT, ids=os.path.basename)
+def test_oracle_exact_matches_reference(path):
+    import torch
+
+    from oracle import tree_oracle_torch as OT
+
+    f = np.load(path)
+    L, B, H, D = (int(x) for x in f["shape"])
+    causal = "causal" in os.path.basename(path)
+    q, k, v, g = (_heads(f[n], H) for n in ("q", "k", "v", "grad_out"))
+    out, w = O.deterministic_attention(q, k, v, causal)
+    np.testing.assert_allclose(out.reshape(L, B, -1), f["out"], atol=5e-5, rtol=5e-5)
+    np.testing.assert_allclose(w, f["weights"], atol=5e-5, rtol=5e-5)
+    qt, kt, vt = (torch.tensor(x, requires_grad=True) for x in (q, k, v))
+    ot, _ = OT.deterministic_attention(qt, kt, vt, causal)
+    ot.backward(torch.tensor(g))
+    for name, t in (("dq", qt), ("dk", kt), ("dv", vt)):
+        np.testing.assert_allclose(t.grad.numpy().reshape(f[name].shape), f[name], atol=2e-4,
+                                   rtol=2e-4, err_msg=name)
