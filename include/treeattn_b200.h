@@ -190,6 +190,90 @@ int ta_backward(const ta_shape* shape, const void* q, ta_layout q_layout, const 
                 ta_layout dk_layout, int32_t dk_dtype, void* dv, ta_layout dv_layout,
                 void* workspace, size_t workspace_bytes, ta_stream_t stream);
 
+/*
+ * Coefficient form of the deterministic backward, for callers that form their own per-level
+ * coefficients (the causal sampler). `shape->num_samples` is the number of paths per query
+ * P/L. For every path p of a head (head-major [b*H+h][l*P/L + j]): keys[p] = path bits (leaf
+ * index), vals[p] = l*P/L + j, coef[p][ta_branch_prob_stride(N)] = dLoss/d(q . k[node]) at
+ * each level, value_weight[p] = weight of the path's leaf in out. Computes
+ *   dq[l] = sum_{p of l, d} coef k[node],  dk[n] = sum_{(p,d) through n} coef q[l(p)],
+ *   dv[leaf] = sum_{p ending there} value_weight dO[l(p)]
+ * with the same sorted, atomics-free reduction as ta_backward. dk / dv in TA_F32 or the input
+ * dtype; workspace: ta_backward_workspace_size(shape).
+ */
+int ta_backward_coef(const ta_shape* shape, const void* q, ta_layout q_layout, const void* k_int,
+                     ta_layout k_layout, const void* grad_out, ta_layout grad_out_layout,
+                     const float* coef, const float* value_weight, const uint32_t* keys,
+                     const uint32_t* vals, void* dq, ta_layout dq_layout, void* dk,
+                     ta_layout dk_layout, int32_t dk_dtype, void* dv, ta_layout dv_layout,
+                     int32_t dv_dtype, void* workspace, size_t workspace_bytes,
+                     ta_stream_t stream);
+
+/* ---- causal mode (A9) ------------------------------------------------------------- */
+
+/*
+ * Causal stochastic sampling for queries [0, L), query t's causal boundary leaf being
+ * t + query_offset: pass 1 computes the boundary-path log-masses M[d] of every (b, h)
+ * (float32 masses, (L, B, H, log2 N + 1)); pass 2 samples S paths per (b, h), correcting
+ * level d's branch log-probabilities to m_child + lp - M[d] when every sample of the query
+ * sits on the boundary node. Gumbel draws: one exponential_() of numel B*H*S*2 per (query,
+ * level) at rng->offset + (t * log2 N + d) * rng->offset_step (ta_philox_plan of that
+ * numel), or `gumbels` (L, log2 N, B, H, S, 2). Writes leaf, weights (softmax over the S
+ * paths), out = sum w v[leaf], corrected[t] = number of leading corrected levels, and
+ * branch_prob as ta_forward. One CTA per query: B*H*S*8 bytes of shared memory.
+ * Replaces _sample_paths_causal (treeattn_torch/_tree_mha.py:125-268) and the stochastic
+ * branch of hierarchical_attention (:379-412).
+ */
+int ta_causal_forward(const ta_shape* shape, int64_t query_offset, const void* q,
+                      ta_layout q_layout, const void* k_int, ta_layout k_layout, const void* v,
+                      ta_layout v_layout, void* out, ta_layout out_layout, const ta_rng* rng,
+                      const float* gumbels, int32_t* leaf, float* weights, float* branch_prob,
+                      int32_t* corrected, float* masses, ta_stream_t stream);
+
+/*
+ * Backward coefficients of ta_causal_forward for L*(S+1) paths per head (each query's S
+ * samples, then its boundary path carrying the gradient of the corrected levels' masses),
+ * in the layout ta_backward_coef takes (num_samples = S + 1).
+ * Replaces autograd through _sample_paths_causal (treeattn_torch/_tree_mha.py:125-268).
+ */
+int ta_causal_coefficients(const ta_shape* shape, int64_t query_offset, const void* q,
+                           ta_layout q_layout, const void* k_int, ta_layout k_layout,
+                           const void* v, ta_layout v_layout, const void* grad_out,
+                           ta_layout grad_out_layout, const int32_t* leaf, const float* weights,
+                           const float* branch_prob, const int32_t* corrected,
+                           const float* masses, float* coef, float* value_weight,
+                           uint32_t* keys, uint32_t* vals, ta_stream_t stream);
+
+/* ---- exact mode (A10) ------------------------------------------------------------- */
+
+/*
+ * Exact tree attention over all N leaves: log p(leaf) = sum over its path of
+ * logsigmoid(+-q . k[node]); non-causal weights exp(log p); causal weights mask leaves
+ * n > l + query_offset and softmax over the rest. out[l] = sum_n w_n v_n, optional weights
+ * (L, B, H, N) float32. shape->num_samples is ignored; workspace of
+ * ta_exact_workspace_size(shape) bytes (queries are processed in blocks that fit it).
+ * Replaces _deterministic_attention (treeattn_torch/_tree_mha.py:271-321).
+ */
+size_t ta_exact_workspace_size(const ta_shape* shape);
+int ta_exact_forward(const ta_shape* shape, int32_t causal, int64_t query_offset,
+                     const void* q, ta_layout q_layout, const void* k_int, ta_layout k_layout,
+                     const void* v, ta_layout v_layout, void* out, ta_layout out_layout,
+                     float* weights, void* workspace, size_t workspace_bytes,
+                     ta_stream_t stream);
+
+/*
+ * Gradients of ta_exact_forward: dq (input dtype) is written; dk and dv are float32 and are
+ * written, or added to when `accumulate` is nonzero (so a causal call can add the exact
+ * prefix's share). Deterministic: per-query coefficient rows and fixed-order GEMMs.
+ * Replaces autograd through _deterministic_attention (_tree_mha.py:271-321).
+ */
+int ta_exact_backward(const ta_shape* shape, int32_t causal, int64_t query_offset,
+                      const void* q, ta_layout q_layout, const void* k_int, ta_layout k_layout,
+                      const void* v, ta_layout v_layout, const void* grad_out,
+                      ta_layout grad_out_layout, void* dq, ta_layout dq_layout, float* dk,
+                      ta_layout dk_layout, float* dv, ta_layout dv_layout, int32_t accumulate,
+                      void* workspace, size_t workspace_bytes, ta_stream_t stream);
+
 /* ---- reference-granularity entry points (treeattn_cuda.cpp:479-488) ---------------- */
 
 /*

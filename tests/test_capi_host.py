@@ -90,8 +90,8 @@ def test_hierarchical_attention_argument_errors():
         ta.hierarchical_attention(q, torch.randn(7, 1, 32), q, num_heads=2, num_samples=0)
     with pytest.raises(ValueError, match="shape"):
         ta.hierarchical_attention(q[0], torch.randn(7, 32), q, num_heads=2)
-    with pytest.raises(NotImplementedError):
-        ta.hierarchical_attention(q, torch.randn(7, 1, 32), q, num_heads=2, is_causal=True)
+    with pytest.raises(ValueError, match="mode"):
+        ta.hierarchical_attention(q, torch.randn(7, 1, 32), q, num_heads=2, mode="other")
     # degenerate trees are handled without kernels, as in the reference (_autograd.py:660-683)
     v1 = torch.randn(1, 1, 32)
     out, w = ta.hierarchical_attention(q, torch.empty(0, 1, 32), v1, num_heads=2, num_samples=4)
@@ -122,4 +122,4 @@ def test_bench_adapter_metadata():
     a = adapter()
     assert a.name == "treeattn_b200" and a.layout == "bshd" and a.supports_backward
     assert a.is_compatible(torch.bfloat16, 128, False)[0]
-    assert not a.is_compatible(torch.bfloat16, 128, True)[0]
+    assert a.is_compatible(torch.bfloat16, 128, True)[0]

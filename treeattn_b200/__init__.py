@@ -13,6 +13,8 @@ Public API (drop-in for the TreeAttention reference's hot path):
 
 from . import ops
 from .autograd import (
+    CausalTreeAttentionFunction,
+    ExactTreeAttentionFunction,
     TreeAttentionBshdFunction,
     TreeAttentionFunction,
     hierarchical_attention,
@@ -37,6 +39,8 @@ __all__ = [
     "hierarchical_attention",
     "tree_attention",
     "TreeAttentionFunction",
+    "CausalTreeAttentionFunction",
+    "ExactTreeAttentionFunction",
     "TreeAttentionBshdFunction",
     "resolve_num_samples",
     "get_runtime_stats",

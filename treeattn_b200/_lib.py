@@ -84,6 +84,17 @@ SIGNATURES = {
     "ta_backward_workspace_size": (_SZ, [ctypes.POINTER(Shape)]),
     "ta_backward": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _L, _P, _P,
                                    _P, _P, _L, _P, _L, _I32, _P, _L, _P, _SZ, _P]),
+    "ta_backward_coef": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _P, _P,
+                                        _P, _P, _L, _P, _L, _I32, _P, _L, _I32, _P, _SZ, _P]),
+    "ta_causal_forward": (ctypes.c_int, [ctypes.POINTER(Shape), _I64, _P, _L, _P, _L, _P, _L, _P,
+                                         _L, ctypes.POINTER(Rng), _P, _P, _P, _P, _P, _P, _P]),
+    "ta_causal_coefficients": (ctypes.c_int, [ctypes.POINTER(Shape), _I64, _P, _L, _P, _L, _P, _L,
+                                              _P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "ta_exact_workspace_size": (_SZ, [ctypes.POINTER(Shape)]),
+    "ta_exact_forward": (ctypes.c_int, [ctypes.POINTER(Shape), _I32, _I64, _P, _L, _P, _L, _P, _L,
+                                        _P, _L, _P, _P, _SZ, _P]),
+    "ta_exact_backward": (ctypes.c_int, [ctypes.POINTER(Shape), _I32, _I64, _P, _L, _P, _L, _P, _L,
+                                         _P, _L, _P, _L, _P, _L, _P, _L, _I32, _P, _SZ, _P]),
     "ta_sample_paths": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L,
                                        ctypes.POINTER(Rng), _P, _P, _P, _P, _P]),
     "ta_replay_paths": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _I32, _P, _P,

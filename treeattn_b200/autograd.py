@@ -56,19 +56,40 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None):
+    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False):
         qv, kv, vv = (t.transpose(0, 1) for t in (q, k, v))  # logical (S, B, H, D) views
         k_int = ops.tree_build(kv)
         out = torch.empty_like(q)
+        ctx.num_samples = num_samples
+        ctx.max_logit = max_logit
+        ctx.causal = causal
+        if causal:
+            st = _causal_fwd(qv, k_int, vv, num_samples, out.transpose(0, 1))
+            ctx.save_for_backward(q, k_int, v, st.leaf, st.weights, st.branch_prob, st.corrected,
+                                  st.masses)
+            ctx.query_offset = st.query_offset
+            return out
         res = ops.forward(qv, k_int, vv, num_samples, max_logit=max_logit, out=out.transpose(0, 1),
                           gumbels=gumbels)
         ctx.save_for_backward(q, k_int, v, res.leaf, res.weights, res.branch_prob)
-        ctx.num_samples = num_samples
-        ctx.max_logit = max_logit
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
+        if ctx.causal:
+            q, k_int, v, leaf, weights, bp, corrected, masses = ctx.saved_tensors
+            st = ops.CausalState(leaf, weights, bp, corrected, masses, ctx.query_offset)
+            B, S, H, D = q.shape
+            dq = torch.empty_like(q)
+            dk_int = torch.empty((B, H, S - 1, D), device=q.device, dtype=torch.float32).permute(2, 0, 1, 3)
+            dv32 = torch.empty((S, B, H, D), device=q.device, dtype=torch.float32)
+            grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
+            _causal_bwd(q.transpose(0, 1), k_int, v.transpose(0, 1), grad_out.transpose(0, 1), st,
+                        ctx.num_samples, dq.transpose(0, 1), dk_int, dv32)
+            dk = torch.empty_like(q)
+            ops.tree_build_backward(dk_int, dk.transpose(0, 1))
+            dv = dv32.transpose(0, 1).to(v.dtype).contiguous()
+            return dq, dk, dv, None, None, None, None
         q, k_int, v, leaf, weights, bp = ctx.saved_tensors
         B, S, H, D = q.shape
         dq = torch.empty_like(q)
@@ -80,7 +101,80 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
                      dk=dk_int, dv=dv.transpose(0, 1))
         dk = torch.empty_like(q)
         ops.tree_build_backward(dk_int, dk.transpose(0, 1))
-        return dq, dk, dv, None, None, None
+        return dq, dk, dv, None, None, None, None
+
+
+def _causal_fwd(q, k_int, v, num_samples, out):
+    """Causal stochastic forward on (seq,B,H,D) views (_tree_mha.py:379-412): the first S
+    queries take exact causal attention when L > S, the rest the corrected sampler."""
+    S = num_samples
+    if q.shape[0] > S:
+        ops.exact_forward(q[:S], k_int, v, True, 0, out=out[:S], want_weights=False)
+        _, st = ops.causal_forward(q[S:], k_int, v, S, S, out=out[S:])
+    else:
+        _, st = ops.causal_forward(q, k_int, v, S, 0, out=out)
+    return st
+
+
+def _causal_bwd(q, k_int, v, grad_out, st, num_samples, dq, dk32, dv32):
+    S = num_samples
+    if q.shape[0] > S:
+        ops.causal_backward(q[S:], k_int, v, grad_out[S:], st, S, dq=dq[S:], dk=dk32, dv=dv32)
+        ops.exact_backward(q[:S], k_int, v, grad_out[:S], True, 0, dq=dq[:S], dk=dk32, dv=dv32,
+                           accumulate=True)
+    else:
+        ops.causal_backward(q, k_int, v, grad_out, st, S, dq=dq, dk=dk32, dv=dv32)
+
+
+class CausalTreeAttentionFunction(torch.autograd.Function):
+    """Causal stochastic tree attention on (seq, B, H, D) views: exact causal prefix for the
+    first S queries (when L > S) and the boundary-corrected sampler for the rest.
+    Returns (out, weights of the sampled queries (L', B, H, S) float32)."""
+
+    @staticmethod
+    def forward(ctx, q, k_int, v, num_samples):
+        out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+        st = _causal_fwd(q, k_int, v, num_samples, out)
+        ctx.save_for_backward(q, k_int, v, st.leaf, st.weights, st.branch_prob, st.corrected,
+                              st.masses)
+        ctx.query_offset = st.query_offset
+        ctx.num_samples = num_samples
+        ctx.mark_non_differentiable(st.weights)
+        return out, st.weights
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_weights):
+        del grad_weights
+        q, k_int, v, leaf, weights, bp, corrected, masses = ctx.saved_tensors
+        st = ops.CausalState(leaf, weights, bp, corrected, masses, ctx.query_offset)
+        dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+        dk = torch.empty(k_int.shape, device=q.device, dtype=torch.float32)
+        dv = torch.empty(v.shape, device=q.device, dtype=torch.float32)
+        _causal_bwd(q, k_int, v, grad_out, st, ctx.num_samples, dq, dk, dv)
+        return dq, dk.to(k_int.dtype), dv.to(v.dtype), None
+
+
+class ExactTreeAttentionFunction(torch.autograd.Function):
+    """mode='deterministic': attention over all leaves (_tree_mha.py:271-321)."""
+
+    @staticmethod
+    def forward(ctx, q, k_int, v, causal):
+        out, w = ops.exact_forward(q, k_int, v, causal, 0, want_weights=True)
+        ctx.save_for_backward(q, k_int, v)
+        ctx.causal = causal
+        ctx.mark_non_differentiable(w)
+        return out, w
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_weights):
+        del grad_weights
+        q, k_int, v = ctx.saved_tensors
+        dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+        dk = torch.empty(k_int.shape, device=q.device, dtype=torch.float32)
+        dv = torch.empty(v.shape, device=q.device, dtype=torch.float32)
+        ops.exact_backward(q, k_int, v, grad_out, ctx.causal, 0, dq=dq, dk=dk, dv=dv,
+                           accumulate=False)
+        return dq, dk.to(k_int.dtype), dv.to(v.dtype), None
 
 
 def hierarchical_attention(
@@ -97,18 +191,18 @@ def hierarchical_attention(
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Hierarchical (tree) attention: query (L,B,E), key (N-1,B,E), value (N,B,E).
 
-    Returns ``(output (L,B,E), weights (L,B,H,S) float32)``. ``block_size`` is accepted for
-    signature compatibility; the fused kernels have no host-side query blocking.
-    Mirrors treeattn_cuda/_autograd.py:863-915 (stochastic, non-causal).
+    Returns ``(output (L,B,E), weights float32)``: (L,B,H,S) for the non-causal sampler, the
+    sampled queries' (L-S,B,H,S) in causal mode when L > S (as the reference), and (L,B,H,N)
+    in mode='deterministic'. ``block_size`` is accepted for signature compatibility; the fused
+    kernels have no host-side query blocking. Mirrors treeattn_cuda/_autograd.py:863-915
+    (non-causal stochastic) and treeattn_torch/_tree_mha.py:324-413 (causal, deterministic).
     """
     del block_size
-    if mode != "stochastic":
-        raise NotImplementedError("treeattn_b200 implements mode='stochastic'")
-    if is_causal:
-        raise NotImplementedError("treeattn_b200 implements is_causal=False")
+    if mode not in ("stochastic", "deterministic"):
+        raise ValueError(f"unknown mode {mode!r}")
     if query.dim() != 3 or value.dim() != 3:
         raise ValueError("query and value must have shape (L, B, E) and (N, B, E)")
-    if num_samples is None or num_samples <= 0:
+    if mode == "stochastic" and (num_samples is None or num_samples <= 0):
         raise ValueError(f"num_samples must be > 0, got {num_samples}")
     l_q, batch, embed = query.shape
     num_leaves = value.shape[0]
@@ -131,7 +225,12 @@ def hierarchical_attention(
     if not ops.is_power_of_two(num_leaves):
         raise ValueError(f"treeattn_b200 requires a power-of-two number of leaves, got {num_leaves}")
     k = key.reshape(num_leaves - 1, batch, num_heads, width)
-    out, weights = TreeAttentionFunction.apply(q, k, v, num_samples, max_logit)
+    if mode == "deterministic":
+        out, weights = ExactTreeAttentionFunction.apply(q, k, v, bool(is_causal))
+    elif is_causal:
+        out, weights = CausalTreeAttentionFunction.apply(q, k, v, num_samples)
+    else:
+        out, weights = TreeAttentionFunction.apply(q, k, v, num_samples, max_logit)
     return out.reshape(l_q, batch, embed), weights
 
 
@@ -156,14 +255,14 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     """attn-bench kernel contract: bshd q/k/v (B,S,H,D) -> out (B,S,H,D).
 
     ``k`` are leaf keys; the internal-node keys are their sequence-axis Haar transform in
-    the reference's layout. ``softmax_scale`` is ignored, as in the reference adapters
+    the reference's layout. ``causal=True`` follows treeattn-torch's causal mode (exact causal
+    prefix for the first ``num_samples`` queries, boundary-corrected sampling for the rest,
+    attn_bench/baselines/treeattn_torch.py:48-90). ``softmax_scale`` is ignored, as in the reference adapters
     (baselines/treeattn_cuda.py:25). ``num_samples`` defaults to ``TREEATTN_NUM_SAMPLES``.
     ``gumbels`` (float32 (log2 S, S, B, H, num_samples, 2)) replaces the generator's noise,
     for replaying a recorded draw.
     """
     del softmax_scale
-    if causal:
-        raise ValueError("treeattn_b200 does not support causal attention yet")
     if num_samples is None:
         num_samples = resolve_num_samples()
     if num_samples is None:
@@ -174,4 +273,4 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     if not ops.is_power_of_two(S) or S < 2:
         raise ValueError(f"treeattn_b200 requires power-of-two seqlen, got {S}")
     q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
-    return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels)
+    return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels, bool(causal))

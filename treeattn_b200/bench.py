@@ -50,7 +50,7 @@ def adapter():
         name=BASELINE_NAME,
         fn=_call,
         supports_backward=True,
-        supports_causal=False,
+        supports_causal=True,
         allowed_dtypes=frozenset({torch.float16, torch.bfloat16, torch.float32}),
         allowed_head_dims=frozenset({32, 64, 96, 128}),
         layout="bshd",

@@ -192,45 +192,42 @@ extern "C" size_t ta_backward_workspace_size(const ta_shape* shape) {
   return bwd_layout(shape).total;
 }
 
-extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
-                           ta_layout kl, const void* v, ta_layout vl, const void* gout,
-                           ta_layout gl, const int32_t* leaf, const float* weights,
-                           const float* branch_prob, void* dq, ta_layout dql, void* dk,
-                           ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl, void* ws,
-                           size_t ws_bytes, ta_stream_t stream) {
+// Shared setup of ta_backward / ta_backward_coef.
+static int bwd_setup(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                     ta_layout kl, const void* gout, ta_layout gl, void* dq, ta_layout dql,
+                     void* dk, ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl,
+                     int32_t dv_dtype, void* ws, size_t ws_bytes, BwdParams& p) {
   int rc = check_shape(shape, true);
   if (rc) return rc;
   const int es = dtype_size(shape->dtype);
   if (dk_dtype != TA_F32 && dk_dtype != shape->dtype)
     return fail(TA_ERR_INVALID, "dk_dtype must be TA_F32 or the input dtype");
+  if (dv_dtype != TA_F32 && dv_dtype != shape->dtype)
+    return fail(TA_ERR_INVALID, "dv_dtype must be TA_F32 or the input dtype");
   if ((rc = check_view("q", q, ql, es, false)) || (rc = check_view("k_int", k, kl, es, false)) ||
-      (rc = check_view("v", v, vl, es, false)) || (rc = check_view("grad_out", gout, gl, es, false)) ||
+      (rc = check_view("grad_out", gout, gl, es, false)) ||
       (rc = check_view("dq", dq, dql, es, false)) ||
       (rc = check_view("dk", dk, dkl, dtype_size(dk_dtype), false)) ||
-      (rc = check_view("dv", dv, dvl, es, false)))
+      (rc = check_view("dv", dv, dvl, dtype_size(dv_dtype), false)))
     return rc;
-  if (!leaf || !weights || !branch_prob)
-    return fail(TA_ERR_INVALID, "leaf, weights and branch_prob must not be NULL");
   if (shape->num_queries * shape->num_samples >= (1ll << 31))
     return fail(TA_ERR_UNSUPPORTED, "L * S must be < 2^31");
   const BwdLayout w = bwd_layout(shape);
   if (ws == nullptr || ws_bytes < w.total)
     return fail(TA_ERR_WORKSPACE, "backward workspace too small (%zu < %zu)", ws_bytes, w.total);
-  BwdParams p{};
-  p.q = (const char*)q; p.k = (const char*)k; p.v = (const char*)v; p.dout = (const char*)gout;
+  p = BwdParams{};
+  p.q = (const char*)q; p.k = (const char*)k; p.dout = (const char*)gout;
   p.dq = (char*)dq; p.dk = (char*)dk; p.dv = (char*)dv;
   p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
   p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
-  p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
   p.gs = gl.seq; p.gb = gl.batch; p.gh = gl.head;
   p.dqs = dql.seq; p.dqb = dql.batch; p.dqh = dql.head;
   p.dks = dkl.seq; p.dkb = dkl.batch; p.dkh = dkl.head;
   p.dvs = dvl.seq; p.dvb = dvl.batch; p.dvh = dvl.head;
-  p.leaf = leaf; p.weights = weights;
   char* base = (char*)ws;
   p.keys[0] = (uint32_t*)(base + w.keys[0]); p.keys[1] = (uint32_t*)(base + w.keys[1]);
   p.vals[0] = (uint32_t*)(base + w.vals[0]); p.vals[1] = (uint32_t*)(base + w.vals[1]);
-  p.dlp = (float*)(base + w.dlp); p.sig = branch_prob; p.hist = (uint32_t*)(base + w.hist);
+  p.dlp = (float*)(base + w.dlp); p.hist = (uint32_t*)(base + w.hist);
   p.partial = (float*)(base + w.partial); p.flags = (uint8_t*)(base + w.flags);
   p.B = (int32_t)shape->batch; p.L = (int32_t)shape->num_queries; p.H = (int32_t)shape->num_heads;
   p.S = (int32_t)shape->num_samples; p.N = (int32_t)shape->num_leaves;
@@ -239,17 +236,62 @@ extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, c
   p.sig_stride = (p.log_n + 3) & ~3;
   p.top_levels = smem_tree_levels(p.log_n, p.nchunks * 16, kTreeSmemBudget);
   p.dk_f32 = dk_dtype == TA_F32 ? 1 : 0;
+  p.dv_f32 = dv_dtype == TA_F32 ? 1 : 0;
   p.P = shape->num_queries * shape->num_samples;
   p.tiles_per_seg = (int32_t)((p.P + kSortTile - 1) / kSortTile);
   p.chunk = chunk_of(shape);
   p.chunks_per_seg = (int32_t)((p.P + p.chunk - 1) / p.chunk);
   p.max_logit = shape->max_logit;
   if (p.log_n > 30) return fail(TA_ERR_UNSUPPORTED, "tree too deep");
-  cudaStream_t st = (cudaStream_t)stream;
+  return TA_OK;
+}
+
+static int bwd_run(const ta_shape* shape, BwdParams& p, cudaStream_t st) {
   switch (shape->dtype) {
-    case TA_F32: rc = run_backward_typed<float>(p, st); break;
-    case TA_F16: rc = run_backward_typed<__half>(p, st); break;
-    default: rc = run_backward_typed<__nv_bfloat16>(p, st); break;
+    case TA_F32: return run_backward_typed<float>(p, st);
+    case TA_F16: return run_backward_typed<__half>(p, st);
+    default: return run_backward_typed<__nv_bfloat16>(p, st);
   }
-  return rc;
+}
+
+extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
+                           ta_layout kl, const void* v, ta_layout vl, const void* gout,
+                           ta_layout gl, const int32_t* leaf, const float* weights,
+                           const float* branch_prob, void* dq, ta_layout dql, void* dk,
+                           ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl, void* ws,
+                           size_t ws_bytes, ta_stream_t stream) {
+  BwdParams p;
+  int rc = bwd_setup(shape, q, ql, k, kl, gout, gl, dq, dql, dk, dkl, dk_dtype, dv, dvl,
+                     shape ? shape->dtype : 0, ws, ws_bytes, p);
+  if (rc) return rc;
+  if ((rc = check_view("v", v, vl, dtype_size(shape->dtype), false))) return rc;
+  if (!leaf || !weights || !branch_prob)
+    return fail(TA_ERR_INVALID, "leaf, weights and branch_prob must not be NULL");
+  p.v = (const char*)v; p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
+  p.leaf = leaf; p.weights = weights; p.sig = branch_prob;
+  return bwd_run(shape, p, (cudaStream_t)stream);
+}
+
+extern "C" int ta_backward_coef(const ta_shape* shape, const void* q, ta_layout ql,
+                                const void* k, ta_layout kl, const void* gout, ta_layout gl,
+                                const float* coef, const float* value_weight,
+                                const uint32_t* keys, const uint32_t* vals, void* dq,
+                                ta_layout dql, void* dk, ta_layout dkl, int32_t dk_dtype,
+                                void* dv, ta_layout dvl, int32_t dv_dtype, void* ws,
+                                size_t ws_bytes, ta_stream_t stream) {
+  BwdParams p;
+  int rc = bwd_setup(shape, q, ql, k, kl, gout, gl, dq, dql, dk, dkl, dk_dtype, dv, dvl,
+                     dv_dtype, ws, ws_bytes, p);
+  if (rc) return rc;
+  if (!coef || !value_weight || !keys || !vals)
+    return fail(TA_ERR_INVALID, "coef, value_weight, keys and vals must not be NULL");
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t n = (size_t)(shape->batch * shape->num_heads) * (size_t)p.P;
+  cudaMemcpyAsync(p.keys[0], keys, n * 4, cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(p.vals[0], vals, n * 4, cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(p.dlp, value_weight, n * 4, cudaMemcpyDeviceToDevice, st);
+  if ((rc = check_launch("backward inputs"))) return rc;
+  p.sig = coef;
+  p.coef_mode = 1;
+  return bwd_run(shape, p, st);
 }

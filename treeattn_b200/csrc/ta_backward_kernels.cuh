@@ -63,6 +63,8 @@ struct BwdParams {
   float max_logit;
   int32_t top_levels;  // tree levels staged in shared memory by the query pass
   int32_t chunk;       // sorted paths per node-pass chunk
+  int32_t coef_mode;   // sig holds final per-level coefficients, dlp holds value weights
+  int32_t dv_f32;      // dv written as float32 (else input dtype)
 };
 
 // The tensor-core node pass serves bf16 inputs whose head_dim is a multiple of 32 (<= 256).
@@ -120,7 +122,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
   if (l >= p.L) return;  // whole group leaves together (no block barrier follows)
 
   // g_s = dO . v[leaf_s]
-  {
+  if (!p.coef_mode) {
     uint4 graw[CPL];
     const char* grow = p.dout + ((int64_t)l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
 #pragma unroll
@@ -154,17 +156,19 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
     }
   }
   __syncwarp(gmask);
-  // dlp_s = w_s (g_s - sum_t w_t g_t)
-  float wg = 0.0f;
-  for (int s = 0; s < p.S; ++s) wg = fmaf(p.weights[j0 + s], s_dlp[s], wg);
-  __syncwarp(gmask);
-  for (int s = t4; s < p.S; s += 4) {
-    const float d = p.weights[j0 + s] * (s_dlp[s] - wg);
-    s_dlp[s] = d;
-    p.dlp[path0 + s] = d;
-    // sort record of path s: (path bits, path id within its head)
-    p.keys[0][path0 + s] = (uint32_t)p.leaf[j0 + s] + K - base_node;
-    p.vals[0][path0 + s] = (uint32_t)(l * p.S + s);
+  if (!p.coef_mode) {
+    // dlp_s = w_s (g_s - sum_t w_t g_t)
+    float wg = 0.0f;
+    for (int s = 0; s < p.S; ++s) wg = fmaf(p.weights[j0 + s], s_dlp[s], wg);
+    __syncwarp(gmask);
+    for (int s = t4; s < p.S; s += 4) {
+      const float d = p.weights[j0 + s] * (s_dlp[s] - wg);
+      s_dlp[s] = d;
+      p.dlp[path0 + s] = d;
+      // sort record of path s: (path bits, path id within its head)
+      p.keys[0][path0 + s] = (uint32_t)p.leaf[j0 + s] + K - base_node;
+      p.vals[0][path0 + s] = (uint32_t)(l * p.S + s);
+    }
   }
   __syncwarp(gmask);
 
@@ -173,8 +177,9 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
 #pragma unroll
   for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
   for (int s = 0; s < p.S; ++s) {
-    const uint32_t bits = (uint32_t)p.leaf[j0 + s] + K - base_node;
-    const float dlp = s_dlp[s];
+    // coefficient mode: the records were written by the caller (before the sort)
+    const uint32_t bits = p.coef_mode ? p.keys[0][path0 + s] : (uint32_t)p.leaf[j0 + s] + K - base_node;
+    const float dlp = p.coef_mode ? 1.0f : s_dlp[s];
     const float* sig = p.sig + (path0 + s) * p.sig_stride;
     for (int d0 = 0; d0 < p.log_n; d0 += DU) {
       uint4 raw[DU][CPL];
@@ -198,7 +203,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
             raw[u][i] = c < p.nchunks ? ldg16(krow + c * 16) : make_uint4(0, 0, 0, 0);
           }
         }
-        const float sgn = ((bits >> (p.log_n - 1 - d)) & 1u) ? -1.0f : 1.0f;
+        const float sgn = (!p.coef_mode && ((bits >> (p.log_n - 1 - d)) & 1u)) ? -1.0f : 1.0f;
         gl[u] = d0 + u < p.log_n ? sgn * __ldg(sig + d) * dlp : 0.0f;
       }
 #pragma unroll
@@ -351,8 +356,9 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
   const int64_t dk_es = p.dk_f32 ? 4 : (int64_t)sizeof(T);
   char* dkb = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh) * dk_es;
   const int64_t dk_row = p.dks * dk_es;
-  char* dvb = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh) * (int64_t)sizeof(T);
-  const int64_t dv_row = p.dvs * (int64_t)sizeof(T);
+  const int64_t dv_es = p.dv_f32 ? 4 : (int64_t)sizeof(T);
+  char* dvb = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh) * dv_es;
+  const int64_t dv_row = p.dvs * dv_es;
   const char* qbase = p.q + ((int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
   const int64_t q_row = p.qs * (int64_t)sizeof(T);
   const char* gbase = p.dout + ((int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
@@ -366,7 +372,7 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
   };
   auto write_row = [&](int d, int64_t node, const float2* f) {
     if (d < ln) store_pairs<T>(dkb + node * dk_row, lane, EP, p.D, f, p.dk_f32);
-    else store_pairs<T>(dvb + node * dv_row, lane, EP, p.D, f, false);
+    else store_pairs<T>(dvb + node * dv_row, lane, EP, p.D, f, p.dv_f32);
   };
   auto put_partial = [&](int slot, const float2* f) {
     float* dst = part + (int64_t)slot * p.D;
@@ -402,7 +408,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
       const uint32_t s = pl - l * (uint32_t)p.S;
       skey[lane] = key;
       cp_async4(sdl + lane, dlp + pl);
-      cp_async4(sw + lane, p.weights + (((int64_t)l * p.B + b) * p.H + h) * p.S + s);
+      if (p.coef_mode) cp_async4(sw + lane, dlp + pl);  // value weight of the path
+      else cp_async4(sw + lane, p.weights + (((int64_t)l * p.B + b) * p.H + h) * p.S + s);
     }
     const int cpr = row_bytes / 16;
     const int q4 = p.sig_stride >> 2;
@@ -466,7 +473,7 @@ __global__ void __launch_bounds__(kNodeWarps * 32) bwd_node_kernel(const BwdPara
       float co = 0.0f;
       if (d < ln) {
         const float sv = sco[r * 32 + d];
-        co = (((skey[r] >> (ln - 1 - d)) & 1u) ? -sv : sv) * sdl[r];
+        co = p.coef_mode ? sv : (((skey[r] >> (ln - 1 - d)) & 1u) ? -sv : sv) * sdl[r];
       } else if (d == ln) {
         co = sw[r];
       }
@@ -691,6 +698,9 @@ __global__ void __launch_bounds__(kFixWarps * 32) bwd_fixup_kernel(const BwdPara
             reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);
             reinterpret_cast<T*>(row)[c0 + 1] = static_cast<T>(tot.y);
           }
+        } else if (p.dv_f32) {
+          char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * 4;
+          *reinterpret_cast<float2*>(reinterpret_cast<float*>(row) + c0) = tot;
         } else {
           char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
           reinterpret_cast<T*>(row)[c0] = static_cast<T>(tot.x);

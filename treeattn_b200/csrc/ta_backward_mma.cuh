@@ -94,7 +94,8 @@ __global__ void __launch_bounds__(kMmaThreads) bwd_node_mma_kernel(const BwdPara
   const int64_t K = (int64_t)p.N - 1;
   const int64_t dk_es = p.dk_f32 ? 4 : 2;
   char* dkb = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh) * dk_es;
-  char* dvb = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh) * 2;
+  const int64_t dv_es = p.dv_f32 ? 4 : 2;
+  char* dvb = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh) * dv_es;
   float* part = p.partial + chunk * (int64_t)(ln + 1) * 2 * D;
   uint8_t* flg = p.flags + chunk * (int64_t)(ln + 1) * 2;
 
@@ -134,10 +135,10 @@ __global__ void __launch_bounds__(kMmaThreads) bwd_node_mma_kernel(const BwdPara
       for (int u = 0; u < 4; ++u) {
         const int d = 4 * d4 + u;
         if (d < ln)
-          s_co[d * kMmaChunk + tid] = (((my_key >> (ln - 1 - d)) & 1u) ? -vv[u] : vv[u]) * dl;
+          s_co[d * kMmaChunk + tid] = p.coef_mode ? vv[u] : (((my_key >> (ln - 1 - d)) & 1u) ? -vv[u] : vv[u]) * dl;
       }
     }
-    s_co[ln * kMmaChunk + tid] = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
+    s_co[ln * kMmaChunk + tid] = p.coef_mode ? dl : p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
   }
   cp_async_wait_0();
   __syncthreads();
@@ -269,8 +270,11 @@ __global__ void __launch_bounds__(kMmaThreads) bwd_node_mma_kernel(const BwdPara
               else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(v.x, v.y);
             } else {
               const int64_t leaf = (int64_t)pre + base_node - K;
-              *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
-                  __floats2bfloat162_rn(v.x, v.y);
+              if (p.dv_f32)
+                *reinterpret_cast<float2*>(reinterpret_cast<float*>(dvb + leaf * p.dvs * 4) + c) = v;
+              else
+                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
+                    __floats2bfloat162_rn(v.x, v.y);
             }
           }
           if (warp == 0 && t == 0 && (before || cont)) {
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(kMmaThreads) bwd_node_mma_kernel(const BwdPara
   }
 
   // 4. unreached nodes: gaps between consecutive runs, and the head's two ends
-  const int64_t zrow_dk = p.dks * dk_es, zrow_dv = p.dvs * 2;
+  const int64_t zrow_dk = p.dks * dk_es, zrow_dv = p.dvs * dv_es;
   auto zero_node = [&](int d, int64_t pre) {
     if (d < ln) {
       char* rowp = dkb + (((int64_t)1 << d) - 1 + pre) * zrow_dk;
@@ -294,8 +298,10 @@ __global__ void __launch_bounds__(kMmaThreads) bwd_node_mma_kernel(const BwdPara
       }
     } else {
       char* rowp = dvb + (pre + base_node - K) * zrow_dv;
-      for (int c = 0; c < D; c += 2)
-        *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+      for (int c = 0; c < D; c += 2) {
+        if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
+        else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+      }
     }
   };
   // path i (> 0) opening a run at level d leaves a gap after the previous run

@@ -28,6 +28,10 @@ _STATS_TEMPLATE = {
     "sample_calls": 0,
     "replay_calls": 0,
     "value_sum_calls": 0,
+    "causal_forward_calls": 0,
+    "causal_backward_calls": 0,
+    "exact_forward_calls": 0,
+    "exact_backward_calls": 0,
 }
 _STATS = dict(_STATS_TEMPLATE)
 
@@ -360,3 +364,127 @@ def profile_collect() -> dict[str, tuple[int, float]]:
         name, cnt, ms = line.split()
         out[name] = (int(cnt), float(ms))
     return out
+
+
+# ---------------------------------------------------------------------------------------
+# causal sampler (A9) and exact mode (A10)
+# ---------------------------------------------------------------------------------------
+
+def reserve_causal_stream(device: torch.device, numel_per_draw: int, draws: int) -> L.Rng:
+    """Reserve ``draws`` exponential_() calls of ``numel_per_draw`` (one per query and level)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    gen = torch.cuda.default_generators[idx]
+    sms, mtps = device_rng_geometry(device)
+    step, stride = philox_plan(numel_per_draw, sms, mtps)
+    seed = gen.initial_seed()
+    offset = gen.get_offset()
+    gen.set_offset(offset + draws * step)
+    return L.Rng(seed, offset, step, stride)
+
+
+@dataclass
+class CausalState:
+    leaf: torch.Tensor
+    weights: torch.Tensor
+    branch_prob: torch.Tensor
+    corrected: torch.Tensor
+    masses: torch.Tensor
+    query_offset: int
+
+
+def causal_forward(q, k_int, v, num_samples, query_offset=0, *, out=None, gumbels=None):
+    """Causal sampler with the boundary correction for queries q (L,B,H,D) whose causal
+    boundaries are t + query_offset. Returns (out, CausalState)."""
+    _require_cuda(q, k_int, v)
+    Lq, B, H, D = q.shape
+    N = v.shape[0]
+    dev = q.device
+    S = num_samples
+    ln = log_n_of(N)
+    shape = L.Shape(B, Lq, N, H, D, S, dtype_code(q.dtype), MAX_LOGIT)
+    if out is None:
+        out = torch.empty((Lq, B, H, D), device=dev, dtype=q.dtype)
+    leaf = torch.empty((Lq, B, H, S), device=dev, dtype=torch.int32)
+    weights = torch.empty((Lq, B, H, S), device=dev, dtype=torch.float32)
+    bp = torch.empty((B * H, Lq * S, branch_prob_stride(N)), device=dev, dtype=torch.float32)
+    corrected = torch.empty((max(Lq, 1),), device=dev, dtype=torch.int32)
+    masses = torch.empty((max(Lq, 1), B, H, ln + 1), device=dev, dtype=torch.float32)
+    rng_p = None
+    if gumbels is not None:
+        gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
+    else:
+        rng_p = ctypes.byref(reserve_causal_stream(dev, B * H * S * 2, Lq * ln))
+    L.call("ta_causal_forward", ctypes.byref(shape), int(query_offset), _ptr(q), layout(q),
+           _ptr(k_int), layout(k_int), _ptr(v), layout(v), _ptr(out), layout(out), rng_p,
+           _ptr(gumbels), _ptr(leaf), _ptr(weights), _ptr(bp), _ptr(corrected), _ptr(masses),
+           _stream(dev))
+    _note("causal_forward")
+    return out, CausalState(leaf, weights, bp, corrected, masses, int(query_offset))
+
+
+def causal_backward(q, k_int, v, grad_out, state: CausalState, num_samples, *, dq, dk, dv):
+    """Gradients of causal_forward: writes dq (input dtype) and float32 dk / dv (all rows)."""
+    Lq, B, H, D = q.shape
+    N = v.shape[0]
+    dev = q.device
+    S = num_samples
+    SP = S + 1
+    stride = branch_prob_stride(N)
+    shape = L.Shape(B, Lq, N, H, D, S, dtype_code(q.dtype), MAX_LOGIT)
+    coef = torch.empty((B * H, Lq * SP, stride), device=dev, dtype=torch.float32)
+    vw = torch.empty((B * H, Lq * SP), device=dev, dtype=torch.float32)
+    keys = torch.empty((B * H, Lq * SP), device=dev, dtype=torch.int32)
+    vals = torch.empty((B * H, Lq * SP), device=dev, dtype=torch.int32)
+    grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
+    L.call("ta_causal_coefficients", ctypes.byref(shape), state.query_offset, _ptr(q), layout(q),
+           _ptr(k_int), layout(k_int), _ptr(v), layout(v), _ptr(grad_out), layout(grad_out),
+           _ptr(state.leaf), _ptr(state.weights), _ptr(state.branch_prob), _ptr(state.corrected),
+           _ptr(state.masses), _ptr(coef), _ptr(vw), _ptr(keys), _ptr(vals), _stream(dev))
+    shape2 = L.Shape(B, Lq, N, H, D, SP, dtype_code(q.dtype), MAX_LOGIT)
+    lib = L.load()
+    ws_bytes = lib.ta_backward_workspace_size(ctypes.byref(shape2))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    L.call("ta_backward_coef", ctypes.byref(shape2), _ptr(q), layout(q), _ptr(k_int), layout(k_int),
+           _ptr(grad_out), layout(grad_out), _ptr(coef), _ptr(vw), _ptr(keys), _ptr(vals),
+           _ptr(dq), layout(dq), _ptr(dk), layout(dk), L.TA_F32, _ptr(dv), layout(dv), L.TA_F32,
+           _ptr(ws), ws_bytes, _stream(dev))
+    _note("causal_backward")
+
+
+def exact_forward(q, k_int, v, causal, query_offset=0, *, out=None, want_weights=True):
+    """Exact attention over all leaves (mode='deterministic'). Returns (out, weights|None)."""
+    _require_cuda(q, k_int, v)
+    Lq, B, H, D = q.shape
+    N = v.shape[0]
+    dev = q.device
+    shape = L.Shape(B, Lq, N, H, D, 1, dtype_code(q.dtype), MAX_LOGIT)
+    if out is None:
+        out = torch.empty((Lq, B, H, D), device=dev, dtype=q.dtype)
+    w = torch.empty((Lq, B, H, N), device=dev, dtype=torch.float32) if want_weights else None
+    lib = L.load()
+    ws_bytes = lib.ta_exact_workspace_size(ctypes.byref(shape))
+    if ws_bytes == 0:
+        raise ValueError("invalid shape for exact attention")
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    L.call("ta_exact_forward", ctypes.byref(shape), 1 if causal else 0, int(query_offset), _ptr(q),
+           layout(q), _ptr(k_int), layout(k_int), _ptr(v), layout(v), _ptr(out), layout(out),
+           _ptr(w), _ptr(ws), ws_bytes, _stream(dev))
+    _note("exact_forward")
+    return out, w
+
+
+def exact_backward(q, k_int, v, grad_out, causal, query_offset=0, *, dq, dk, dv, accumulate):
+    """Gradients of exact_forward: dq written (input dtype); float32 dk / dv written or added."""
+    Lq, B, H, D = q.shape
+    N = v.shape[0]
+    dev = q.device
+    shape = L.Shape(B, Lq, N, H, D, 1, dtype_code(q.dtype), MAX_LOGIT)
+    lib = L.load()
+    ws_bytes = lib.ta_exact_workspace_size(ctypes.byref(shape))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
+    L.call("ta_exact_backward", ctypes.byref(shape), 1 if causal else 0, int(query_offset), _ptr(q),
+           layout(q), _ptr(k_int), layout(k_int), _ptr(v), layout(v), _ptr(grad_out), layout(grad_out),
+           _ptr(dq), layout(dq), _ptr(dk), layout(dk), _ptr(dv), layout(dv), 1 if accumulate else 0,
+           _ptr(ws), ws_bytes, _stream(dev))
+    _note("exact_backward")
