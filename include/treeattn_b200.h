@@ -136,6 +136,20 @@ int ta_tree_build(int32_t dtype, int64_t batch, int64_t seq_len, int64_t num_hea
                   ta_stream_t stream);
 
 /*
+ * ta_tree_build without a workspace, for callers that cannot allocate device memory (a host
+ * whose runtime owns all HBM in its own pool, or a C/FFI caller with no device allocator).
+ * It has no counterpart in the reference. The scratch is a fixed per-device array of
+ * TA_NOALLOC_SCRATCH_BYTES; shapes needing more (ta_tree_build_workspace_size) return
+ * TA_ERR_WORKSPACE. It needs no zeroing. The first call on a device does the set-up
+ * (looks up the array's address), so make it before any stream capture. Calls that
+ * overlap on one device race on the shared scratch: serialise them.
+ */
+#define TA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int ta_tree_build_noalloc(int32_t dtype, int64_t batch, int64_t seq_len, int64_t num_heads,
+                          int64_t head_dim, const void* k_leaf, ta_layout k_leaf_layout,
+                          void* k_int, ta_layout k_int_layout, ta_stream_t stream);
+
+/*
  * Gradient of ta_tree_build: dk_leaf = transpose(Haar) dk_int, computed in float32 and
  * written once in `dtype`. dk_int is float32, (S-1, B, H, D) view.
  * Replaces autograd through haar_internal_node_keys (_treeattn_common.py:54-86).

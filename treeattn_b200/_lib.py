@@ -76,6 +76,7 @@ SIGNATURES = {
     "ta_branch_prob_stride": (_I32, [_I64]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
+    "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),
     "ta_tree_build_backward_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "ta_tree_build_backward": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P,
                                               _SZ, _P]),
