@@ -163,12 +163,16 @@ def run_ours(args):
     q, k, v, go = (torch.randn(B, S, H, D, device=dev, generator=gen).to(dtype) for _ in range(4))
     for t in (q, k, v):
         t.requires_grad_(True)
-    torch.manual_seed(rank)
+    # every rank draws its slice of ONE global problem's noise (same seed everywhere), so
+    # the N-rank run computes exactly what one GPU would on the global batch
+    from treeattn_b200.sharding import shard_for_rank
+    shard = shard_for_rank(world * B, H, rank, world, "batch") if world > 1 else None
+    torch.manual_seed(0)
 
     def step():
         for t in (q, k, v):
             t.grad = None
-        out = ta.tree_attention(q, k, v, False, None, num_samples=P)
+        out = ta.tree_attention(q, k, v, False, None, num_samples=P, shard=shard)
         out.backward(go)
 
     def barrier():
@@ -215,7 +219,7 @@ def run_ours(args):
             dk_ = hk.to(dev, non_blocking=True).requires_grad_(True)
             dv_ = hv.to(dev, non_blocking=True).requires_grad_(True)
             g_ = hgo.to(dev, non_blocking=True)
-            out = ta.tree_attention(dq_, dk_, dv_, False, None, num_samples=P)
+            out = ta.tree_attention(dq_, dk_, dv_, False, None, num_samples=P, shard=shard)
             out.backward(g_)
             hout.copy_(out.detach(), non_blocking=True)
             hdq.copy_(dq_.grad, non_blocking=True)
@@ -277,7 +281,8 @@ def run_ours(args):
         "data": "synthetic N(0,1) q/k/v/grad_out from a seeded CUDA generator",
         "config": {**WORKLOAD, "batch_per_gpu": B, "seq_len": S, "heads": H, "head_dim": D,
                    "num_samples": P, "global_batch": world * B,
-                   "parallelism": f"head-sharded x{world} (independent (batch, head) trees, no collective)",
+                   "parallelism": f"batch-sharded x{world} (independent (batch, head) trees, no collective; "
+                                  "each rank draws its slice of the global problem's noise)",
                    "l2": "inputs larger than L2 (q, k, v, grad_out: 4 x %d MiB)" % (B * S * H * D * 2 >> 20)},
         "value_per_gpu": value / world,
         "gpu_launches": int(sum(c for c, _ in prof.values())),

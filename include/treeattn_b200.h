@@ -119,6 +119,22 @@ int ta_philox_plan(int64_t numel, int32_t sm_count, int32_t max_threads_per_sm,
 int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth0,
                    int32_t depths, ta_stream_t stream);
 
+/*
+ * One shard of the draw ta_gumbel_fill makes for a (rows, batch_total, head_total, row_elems)
+ * tensor (rows = queries, row_elems = 2 * samples): out[d][r][b][h][i] (float32,
+ * (depths, rows, batch_count, head_count, row_elems)) is the full draw's element
+ * (r, batch0 + b, head0 + h, i). rng is the plan of the FULL numel, so ranks that each fill
+ * their own (batch, head) shard see exactly the noise of one unsharded call: head/batch
+ * sharding with no collective. The full draw must stay below 2^31 elements. No counterpart
+ * in the reference (it is single-GPU); extends the per-depth draws of _autograd.py:188-195.
+ */
+typedef struct ta_shard {
+  int64_t batch_total, batch0, batch_count;
+  int64_t head_total, head0, head_count;
+} ta_shard;
+int ta_gumbel_fill_shard(float* out, const ta_rng* rng, int64_t rows, const ta_shard* shard,
+                         int64_t row_elems, int32_t depth0, int32_t depths, ta_stream_t stream);
+
 /* ---- tree build (A1) ---------------------------------------------------------------- */
 
 /*

@@ -9,9 +9,10 @@ Public API (drop-in for the TreeAttention reference's hot path):
   -- the attn-bench kernel contract on bshd tensors (Haar tree build included).
 * ``bench.adapter()`` -- an attn-bench ``KernelAdapter`` for ``treeattn_b200``.
 * ``ops`` -- tensor-level wrappers of every C-ABI entry point.
+* ``sharding`` -- head/batch sharding over one process per GPU (no collective).
 """
 
-from . import ops
+from . import ops, sharding
 from .autograd import (
     CausalTreeAttentionFunction,
     ExactTreeAttentionFunction,
@@ -47,4 +48,5 @@ __all__ = [
     "reset_runtime_stats",
     "has_native_kernels",
     "ops",
+    "sharding",
 ]

@@ -28,6 +28,12 @@ class Layout(ctypes.Structure):
     _fields_ = [("seq", ctypes.c_int64), ("batch", ctypes.c_int64), ("head", ctypes.c_int64)]
 
 
+class Shard(ctypes.Structure):
+    _fields_ = [("batch_total", ctypes.c_int64), ("batch0", ctypes.c_int64),
+                ("batch_count", ctypes.c_int64), ("head_total", ctypes.c_int64),
+                ("head0", ctypes.c_int64), ("head_count", ctypes.c_int64)]
+
+
 class Shape(ctypes.Structure):
     _fields_ = [
         ("batch", ctypes.c_int64),
@@ -74,6 +80,8 @@ SIGNATURES = {
                                       ctypes.POINTER(_I64)]),
     "ta_gumbel_fill": (ctypes.c_int, [_P, _I64, ctypes.POINTER(Rng), _I32, _I32, _P]),
     "ta_branch_prob_stride": (_I32, [_I64]),
+    "ta_gumbel_fill_shard": (ctypes.c_int, [_P, ctypes.POINTER(Rng), _I64, ctypes.POINTER(Shard),
+                                            _I64, _I32, _I32, _P]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),

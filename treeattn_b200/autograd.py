@@ -56,7 +56,7 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False):
+    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False, shard=None):
         qv, kv, vv = (t.transpose(0, 1) for t in (q, k, v))  # logical (S, B, H, D) views
         k_int = ops.tree_build(kv)
         out = torch.empty_like(q)
@@ -70,7 +70,7 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
             ctx.query_offset = st.query_offset
             return out
         res = ops.forward(qv, k_int, vv, num_samples, max_logit=max_logit, out=out.transpose(0, 1),
-                          gumbels=gumbels)
+                          gumbels=gumbels, shard=shard)
         ctx.save_for_backward(q, k_int, v, res.leaf, res.weights, res.branch_prob)
         return out
 
@@ -89,7 +89,7 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
             dk = torch.empty_like(q)
             ops.tree_build_backward(dk_int, dk.transpose(0, 1))
             dv = dv32.transpose(0, 1).to(v.dtype).contiguous()
-            return dq, dk, dv, None, None, None, None
+            return dq, dk, dv, None, None, None, None, None
         q, k_int, v, leaf, weights, bp = ctx.saved_tensors
         B, S, H, D = q.shape
         dq = torch.empty_like(q)
@@ -101,7 +101,7 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
                      dk=dk_int, dv=dv.transpose(0, 1))
         dk = torch.empty_like(q)
         ops.tree_build_backward(dk_int, dk.transpose(0, 1))
-        return dq, dk, dv, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None
 
 
 def _causal_fwd(q, k_int, v, num_samples, out):
@@ -251,7 +251,7 @@ def resolve_num_samples() -> int | None:
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                    softmax_scale: float | None = None, *, num_samples: int | None = None,
                    max_logit: float = ops.MAX_LOGIT,
-                   gumbels: torch.Tensor | None = None) -> torch.Tensor:
+                   gumbels: torch.Tensor | None = None, shard=None) -> torch.Tensor:
     """attn-bench kernel contract: bshd q/k/v (B,S,H,D) -> out (B,S,H,D).
 
     ``k`` are leaf keys; the internal-node keys are their sequence-axis Haar transform in
@@ -260,9 +260,13 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     attn_bench/baselines/treeattn_torch.py:48-90). ``softmax_scale`` is ignored, as in the reference adapters
     (baselines/treeattn_cuda.py:25). ``num_samples`` defaults to ``TREEATTN_NUM_SAMPLES``.
     ``gumbels`` (float32 (log2 S, S, B, H, num_samples, 2)) replaces the generator's noise,
-    for replaying a recorded draw.
+    for replaying a recorded draw. ``shard`` (``sharding.ShardSpec``, non-causal only) marks
+    q/k/v as this rank's (batch, head) block of a larger problem; the result is that block
+    of the unsharded call's result.
     """
     del softmax_scale
+    if shard is not None and causal:
+        raise ValueError("causal mode couples all heads of a query and cannot be head/batch sharded")
     if num_samples is None:
         num_samples = resolve_num_samples()
     if num_samples is None:
@@ -273,4 +277,5 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     if not ops.is_power_of_two(S) or S < 2:
         raise ValueError(f"treeattn_b200 requires power-of-two seqlen, got {S}")
     q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
-    return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels, bool(causal))
+    return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels, bool(causal),
+                                           shard)

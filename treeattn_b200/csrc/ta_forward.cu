@@ -329,6 +329,35 @@ __global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t n
   if (e0 + 3u * stride < numel) o[e0 + 3u * stride] = gumbel_from_uniform(u4.w);
 }
 
+// Gumbel noise of one shard of a larger (rows, batch, heads, row_elems) draw: local element
+// (r, b, h, i) of the (rows, batch_count, head_count, row_elems) output takes the value torch's
+// draw puts at global element ((r * batch_total + batch0 + b) * head_total + head0 + h) *
+// row_elems + i. One philox 4-vector per element (a shard's elements are spread over
+// the subsequences, so the vectors are not shared).
+__global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
+    float* out, uint64_t local_numel, ta_shard sh, int64_t row_elems, uint32_t stride,
+    uint64_t seed, uint64_t offset, uint64_t offset_step) {
+  const uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= local_numel) return;
+  const int depth = blockIdx.y;
+  const uint64_t row = e / (uint64_t)row_elems;
+  const uint64_t inner = e - row * (uint64_t)row_elems;
+  const uint64_t h = row % (uint64_t)sh.head_count;
+  const uint64_t t = row / (uint64_t)sh.head_count;
+  const uint64_t b = t % (uint64_t)sh.batch_count;
+  const uint64_t r = t / (uint64_t)sh.batch_count;
+  const uint64_t g = ((r * sh.batch_total + sh.batch0 + b) * sh.head_total + sh.head0 + h) *
+                         (uint64_t)row_elems + inner;
+  const uint32_t tid = (uint32_t)(g % stride);
+  const uint64_t bundle = g / stride;
+  curandStatePhilox4_32_10_t st;
+  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * (bundle >> 2), &st);
+  const float4 u4 = _curand_uniform4(st.output);
+  const uint32_t c = (uint32_t)(bundle & 3);
+  const float u = c == 0 ? u4.x : c == 1 ? u4.y : c == 2 ? u4.z : u4.w;
+  out[(uint64_t)depth * local_numel + e] = gumbel_from_uniform(u);
+}
+
 // ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
@@ -563,6 +592,33 @@ extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int3
       out, (uint32_t)numel, stride, calls, rng->seed,
       rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step, depths);
   return check_launch("gumbel fill");
+}
+
+extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, int64_t rows,
+                                    const ta_shard* shard, int64_t row_elems, int32_t depth0,
+                                    int32_t depths, ta_stream_t stream) {
+  if (!out || !rng || !shard || rows < 0 || row_elems <= 0 || depth0 < 0 || depths < 0 ||
+      depths > 65535)
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: invalid arguments");
+  const ta_shard& s = *shard;
+  if (s.batch_total <= 0 || s.head_total <= 0 || s.batch_count <= 0 || s.head_count <= 0 ||
+      s.batch0 < 0 || s.head0 < 0 || s.batch0 + s.batch_count > s.batch_total ||
+      s.head0 + s.head_count > s.head_total)
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: shard outside the full batch/heads");
+  const double global = (double)rows * s.batch_total * s.head_total * row_elems;
+  if (global >= 2147483648.0)
+    return fail(TA_ERR_UNSUPPORTED, "ta_gumbel_fill_shard: the full draw exceeds 2^31 elements");
+  if (rng->draw_stride <= 0 || rng->draw_stride >= (1ll << 31) || (rng->offset & 3) ||
+      (rng->offset_step & 3))
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: invalid rng");
+  const uint64_t local = (uint64_t)rows * s.batch_count * s.head_count * row_elems;
+  if (local == 0 || depths == 0) return TA_OK;
+  TA_PROFILE("gumbel_fill", (cudaStream_t)stream);
+  dim3 grid((unsigned)((local + 255) / 256), (unsigned)depths);
+  gumbel_fill_shard_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      out, local, s, row_elems, (uint32_t)rng->draw_stride, rng->seed,
+      rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
+  return check_launch("gumbel fill (shard)");
 }
 
 extern "C" int32_t ta_branch_prob_stride(int64_t num_leaves) {

@@ -144,6 +144,24 @@ def gumbel_fill(out: torch.Tensor, rng: L.Rng, depth0: int = 0) -> torch.Tensor:
     return out
 
 
+def gumbel_fill_shard(out: torch.Tensor, rng: L.Rng, rows: int, shard, row_elems: int,
+                      depth0: int = 0) -> torch.Tensor:
+    """Fill float32 ``out`` (depths, rows * batch_count * head_count * row_elems) with this
+    shard's slice of the full (rows, batch_total, head_total, row_elems) draw of ``rng``
+    (``rng`` is the plan of the FULL numel)."""
+    _require_cuda(out)
+    if out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 tensor")
+    depths = out.shape[0] if out.dim() > 1 else 1
+    if out.numel() != depths * rows * shard.batch_count * shard.head_count * row_elems:
+        raise ValueError("out does not hold this shard's draw")
+    sh = L.Shard(shard.batch_total, shard.batch0, shard.batch_count, shard.head_total,
+                 shard.head0, shard.head_count)
+    L.call("ta_gumbel_fill_shard", _ptr(out), ctypes.byref(rng), rows, ctypes.byref(sh),
+           row_elems, depth0, depths, _stream(out.device))
+    return out
+
+
 def branch_prob_stride(num_leaves: int) -> int:
     return (log_n_of(num_leaves) + 3) & ~3
 
@@ -212,7 +230,7 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
             max_logit: float = MAX_LOGIT, out: torch.Tensor | None = None,
             gumbels: torch.Tensor | None = None, want_packed: bool = False,
             rng: L.Rng | None = None, for_backward: bool = True,
-            fused_rng: bool = False) -> ForwardResult:
+            fused_rng: bool = False, shard=None) -> ForwardResult:
     """Fused sampler + softmax + value gather. q (L,B,H,D), k_int (N-1,B,H,D), v (N,B,H,D).
 
     The Gumbel noise comes from torch's default CUDA generator (reserved here, exactly as
@@ -220,7 +238,9 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
     (log2 N, L, B, H, S, 2)) or an explicit ``rng`` is given. By default all depths' noise is
     drawn first by ``ta_gumbel_fill`` (each philox 4-vector used four times);
     ``fused_rng=True`` draws it inside the sampler instead. ``for_backward`` also returns the
-    per-path branch probabilities ``ta_backward`` needs.
+    per-path branch probabilities ``ta_backward`` needs. ``shard`` (a
+    ``sharding.ShardSpec``) marks q/k/v as one (batch, head) block of a larger problem: the
+    noise is then the matching slice of the full problem's draw (see ``gumbel_fill_shard``).
     """
     _require_cuda(q, k_int, v)
     Lq, B, H, D = q.shape
@@ -239,6 +259,17 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
                              dtype=torch.uint8)
     numel = Lq * B * H * num_samples * 2
     rng_p = None
+    if shard is not None and not shard.is_full and gumbels is None:
+        if (shard.batch_count, shard.head_count) != (B, H):
+            raise ValueError(f"shard {shard} does not match q's (batch, heads) = ({B}, {H})")
+        if fused_rng:
+            raise ValueError("fused_rng does not support shards")
+        if rng is None:
+            rng = reserve_gumbel_stream(dev, Lq * shard.batch_total * shard.head_total * num_samples * 2,
+                                        log_n_of(N))
+        gumbels = gumbel_fill_shard(
+            torch.empty((log_n_of(N), numel), device=dev, dtype=torch.float32), rng, Lq, shard,
+            num_samples * 2)
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
     else:
