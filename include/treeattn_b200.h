@@ -120,20 +120,22 @@ int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int32_t depth0,
                    int32_t depths, ta_stream_t stream);
 
 /*
- * One shard of the draw ta_gumbel_fill makes for a (rows, batch_total, head_total, row_elems)
- * tensor (rows = queries, row_elems = 2 * samples): out[d][r][b][h][i] (float32,
- * (depths, rows, batch_count, head_count, row_elems)) is the full draw's element
- * (r, batch0 + b, head0 + h, i). rng is the plan of the FULL numel, so ranks that each fill
- * their own (batch, head) shard see exactly the noise of one unsharded call: head/batch
- * sharding with no collective. The full draw must stay below 2^31 elements. No counterpart
- * in the reference (it is single-GPU); extends the per-depth draws of _autograd.py:188-195.
+ * One shard of the draw ta_gumbel_fill makes for a (row_total, batch_total, head_total,
+ * row_elems) tensor (rows = queries, row_elems = 2 * samples): out[d][r][b][h][i] (float32,
+ * (depths, row_count, batch_count, head_count, row_elems)) is the full draw's element
+ * (row0 + r, batch0 + b, head0 + h, i). rng is the plan of the FULL numel, so ranks that
+ * each fill their own (query, batch, head) block see exactly the noise of one unsharded call:
+ * head/batch sharding with no collective, and the query split of sequence parallelism. The
+ * full draw must stay below 2^31 elements. No counterpart in the reference (it is
+ * single-GPU); extends the per-depth draws of _autograd.py:188-195.
  */
 typedef struct ta_shard {
+  int64_t row_total, row0, row_count;
   int64_t batch_total, batch0, batch_count;
   int64_t head_total, head0, head_count;
 } ta_shard;
-int ta_gumbel_fill_shard(float* out, const ta_rng* rng, int64_t rows, const ta_shard* shard,
-                         int64_t row_elems, int32_t depth0, int32_t depths, ta_stream_t stream);
+int ta_gumbel_fill_shard(float* out, const ta_rng* rng, const ta_shard* shard, int64_t row_elems,
+                         int32_t depth0, int32_t depths, ta_stream_t stream);
 
 /* ---- tree build (A1) ---------------------------------------------------------------- */
 
@@ -204,9 +206,9 @@ int32_t ta_branch_prob_stride(int64_t num_leaves);
 /* ---- fused deterministic backward (A8) -------------------------------------------- */
 
 /*
- * Gradients of ta_forward given its leaf, weights and branch_prob outputs. dq and dv are written in
- * shape->dtype; dk in `dk_dtype` (TA_F32 for a float32 accumulation buffer, or
- * shape->dtype). No float atomics: dK/dV are reduced by sorting paths by leaf and summing
+ * Gradients of ta_forward given its leaf, weights and branch_prob outputs. dq is written in
+ * shape->dtype; dk in `dk_dtype` and dv in `dv_dtype` (each TA_F32 for a float32 buffer, e.g.
+ * partial gradients that are reduced across ranks afterwards, or shape->dtype). No float atomics: dK/dV are reduced by sorting paths by leaf and summing
  * each node's contributions in a fixed order, so results are bitwise repeatable.
  * Replaces _StochasticNonCausalTreeAttention.backward (_autograd.py:707-860):
  * prepare_non_causal_backward, scatter_weighted_grad_v_forward and
@@ -218,7 +220,7 @@ int ta_backward(const ta_shape* shape, const void* q, ta_layout q_layout, const 
                 ta_layout grad_out_layout, const int32_t* leaf, const float* weights,
                 const float* branch_prob, void* dq, ta_layout dq_layout, void* dk,
                 ta_layout dk_layout, int32_t dk_dtype, void* dv, ta_layout dv_layout,
-                void* workspace, size_t workspace_bytes, ta_stream_t stream);
+                int32_t dv_dtype, void* workspace, size_t workspace_bytes, ta_stream_t stream);
 
 /*
  * Coefficient form of the deterministic backward, for callers that form their own per-level

@@ -29,7 +29,8 @@ class Layout(ctypes.Structure):
 
 
 class Shard(ctypes.Structure):
-    _fields_ = [("batch_total", ctypes.c_int64), ("batch0", ctypes.c_int64),
+    _fields_ = [("row_total", ctypes.c_int64), ("row0", ctypes.c_int64), ("row_count", ctypes.c_int64),
+                ("batch_total", ctypes.c_int64), ("batch0", ctypes.c_int64),
                 ("batch_count", ctypes.c_int64), ("head_total", ctypes.c_int64),
                 ("head0", ctypes.c_int64), ("head_count", ctypes.c_int64)]
 
@@ -80,8 +81,8 @@ SIGNATURES = {
                                       ctypes.POINTER(_I64)]),
     "ta_gumbel_fill": (ctypes.c_int, [_P, _I64, ctypes.POINTER(Rng), _I32, _I32, _P]),
     "ta_branch_prob_stride": (_I32, [_I64]),
-    "ta_gumbel_fill_shard": (ctypes.c_int, [_P, ctypes.POINTER(Rng), _I64, ctypes.POINTER(Shard),
-                                            _I64, _I32, _I32, _P]),
+    "ta_gumbel_fill_shard": (ctypes.c_int, [_P, ctypes.POINTER(Rng), ctypes.POINTER(Shard), _I64,
+                                            _I32, _I32, _P]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),
@@ -92,7 +93,7 @@ SIGNATURES = {
                                   ctypes.POINTER(Rng), _P, _P, _P, _P, _P, _P]),
     "ta_backward_workspace_size": (_SZ, [ctypes.POINTER(Shape)]),
     "ta_backward": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _L, _P, _P,
-                                   _P, _P, _L, _P, _L, _I32, _P, _L, _P, _SZ, _P]),
+                                   _P, _P, _L, _P, _L, _I32, _P, _L, _I32, _P, _SZ, _P]),
     "ta_backward_coef": (ctypes.c_int, [ctypes.POINTER(Shape), _P, _L, _P, _L, _P, _L, _P, _P, _P,
                                         _P, _P, _L, _P, _L, _I32, _P, _L, _I32, _P, _SZ, _P]),
     "ta_causal_forward": (ctypes.c_int, [ctypes.POINTER(Shape), _I64, _P, _L, _P, _L, _P, _L, _P,

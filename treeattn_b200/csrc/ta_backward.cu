@@ -258,11 +258,11 @@ extern "C" int ta_backward(const ta_shape* shape, const void* q, ta_layout ql, c
                            ta_layout kl, const void* v, ta_layout vl, const void* gout,
                            ta_layout gl, const int32_t* leaf, const float* weights,
                            const float* branch_prob, void* dq, ta_layout dql, void* dk,
-                           ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl, void* ws,
-                           size_t ws_bytes, ta_stream_t stream) {
+                           ta_layout dkl, int32_t dk_dtype, void* dv, ta_layout dvl,
+                           int32_t dv_dtype, void* ws, size_t ws_bytes, ta_stream_t stream) {
   BwdParams p;
   int rc = bwd_setup(shape, q, ql, k, kl, gout, gl, dq, dql, dk, dkl, dk_dtype, dv, dvl,
-                     shape ? shape->dtype : 0, ws, ws_bytes, p);
+                     dv_dtype, ws, ws_bytes, p);
   if (rc) return rc;
   if ((rc = check_view("v", v, vl, dtype_size(shape->dtype), false))) return rc;
   if (!leaf || !weights || !branch_prob)

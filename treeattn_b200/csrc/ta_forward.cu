@@ -330,31 +330,32 @@ __global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t n
 }
 
 // Gumbel noise of one shard of a larger (rows, batch, heads, row_elems) draw: local element
-// (r, b, h, i) of the (rows, batch_count, head_count, row_elems) output takes the value torch's
-// draw puts at global element ((r * batch_total + batch0 + b) * head_total + head0 + h) *
-// row_elems + i. One philox 4-vector per element (a shard's elements are spread over
+// (r, b, h, i) of the (row_count, batch_count, head_count, row_elems) output takes the value
+// torch's draw puts at global element
+// (((row0 + r) * batch_total + batch0 + b) * head_total + head0 + h) * row_elems + i. One philox 4-vector per element (a shard's elements are spread over
 // the subsequences, so the vectors are not shared).
+struct ShardDivs {
+  FastDiv row_elems, head_count, batch_count, stride;
+  uint32_t row0, batch_total, batch0, head_total, head0;
+};
+
 __global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
-    float* out, uint64_t local_numel, ta_shard sh, int64_t row_elems, uint32_t stride,
-    uint64_t seed, uint64_t offset, uint64_t offset_step) {
-  const uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float* out, uint32_t local_numel, ShardDivs sd, uint64_t seed, uint64_t offset,
+    uint64_t offset_step) {
+  const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= local_numel) return;
   const int depth = blockIdx.y;
-  const uint64_t row = e / (uint64_t)row_elems;
-  const uint64_t inner = e - row * (uint64_t)row_elems;
-  const uint64_t h = row % (uint64_t)sh.head_count;
-  const uint64_t t = row / (uint64_t)sh.head_count;
-  const uint64_t b = t % (uint64_t)sh.batch_count;
-  const uint64_t r = t / (uint64_t)sh.batch_count;
-  const uint64_t g = ((r * sh.batch_total + sh.batch0 + b) * sh.head_total + sh.head0 + h) *
-                         (uint64_t)row_elems + inner;
-  const uint32_t tid = (uint32_t)(g % stride);
-  const uint64_t bundle = g / stride;
-  curandStatePhilox4_32_10_t st;
-  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * (bundle >> 2), &st);
-  const float4 u4 = _curand_uniform4(st.output);
-  const uint32_t c = (uint32_t)(bundle & 3);
-  const float u = c == 0 ? u4.x : c == 1 ? u4.y : c == 2 ? u4.z : u4.w;
+  // 32-bit index math throughout: the full draw is below 2^31 elements
+  const uint32_t row = sd.row_elems.div(e);
+  const uint32_t inner = e - row * sd.row_elems.d;
+  const uint32_t t = sd.head_count.div(row);
+  const uint32_t h = row - t * sd.head_count.d;
+  const uint32_t r = sd.batch_count.div(t);
+  const uint32_t b = t - r * sd.batch_count.d;
+  const uint32_t g =
+      (((sd.row0 + r) * sd.batch_total + sd.batch0 + b) * sd.head_total + sd.head0 + h) *
+          sd.row_elems.d + inner;
+  const float u = torch_uniform(seed, offset + (uint64_t)depth * offset_step, g, sd.stride);
   out[(uint64_t)depth * local_numel + e] = gumbel_from_uniform(u);
 }
 
@@ -594,29 +595,37 @@ extern "C" int ta_gumbel_fill(float* out, int64_t numel, const ta_rng* rng, int3
   return check_launch("gumbel fill");
 }
 
-extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, int64_t rows,
-                                    const ta_shard* shard, int64_t row_elems, int32_t depth0,
-                                    int32_t depths, ta_stream_t stream) {
-  if (!out || !rng || !shard || rows < 0 || row_elems <= 0 || depth0 < 0 || depths < 0 ||
-      depths > 65535)
+extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, const ta_shard* shard,
+                                    int64_t row_elems, int32_t depth0, int32_t depths,
+                                    ta_stream_t stream) {
+  if (!out || !rng || !shard || row_elems <= 0 || depth0 < 0 || depths < 0 || depths > 65535)
     return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: invalid arguments");
   const ta_shard& s = *shard;
-  if (s.batch_total <= 0 || s.head_total <= 0 || s.batch_count <= 0 || s.head_count <= 0 ||
-      s.batch0 < 0 || s.head0 < 0 || s.batch0 + s.batch_count > s.batch_total ||
+  if (s.row_total < 0 || s.batch_total <= 0 || s.head_total <= 0 || s.row_count < 0 ||
+      s.batch_count <= 0 || s.head_count <= 0 || s.row0 < 0 || s.batch0 < 0 || s.head0 < 0 ||
+      s.row0 + s.row_count > s.row_total || s.batch0 + s.batch_count > s.batch_total ||
       s.head0 + s.head_count > s.head_total)
-    return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: shard outside the full batch/heads");
-  const double global = (double)rows * s.batch_total * s.head_total * row_elems;
+    return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: shard outside the full draw");
+  const double global = (double)s.row_total * s.batch_total * s.head_total * row_elems;
   if (global >= 2147483648.0)
     return fail(TA_ERR_UNSUPPORTED, "ta_gumbel_fill_shard: the full draw exceeds 2^31 elements");
   if (rng->draw_stride <= 0 || rng->draw_stride >= (1ll << 31) || (rng->offset & 3) ||
       (rng->offset_step & 3))
     return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: invalid rng");
-  const uint64_t local = (uint64_t)rows * s.batch_count * s.head_count * row_elems;
+  const uint64_t local = (uint64_t)s.row_count * s.batch_count * s.head_count * row_elems;
   if (local == 0 || depths == 0) return TA_OK;
+  ShardDivs sd;
+  sd.row_elems.init((uint32_t)row_elems);
+  sd.head_count.init((uint32_t)s.head_count);
+  sd.batch_count.init((uint32_t)s.batch_count);
+  sd.stride.init((uint32_t)rng->draw_stride);
+  sd.row0 = (uint32_t)s.row0;
+  sd.batch_total = (uint32_t)s.batch_total; sd.batch0 = (uint32_t)s.batch0;
+  sd.head_total = (uint32_t)s.head_total; sd.head0 = (uint32_t)s.head0;
   TA_PROFILE("gumbel_fill", (cudaStream_t)stream);
   dim3 grid((unsigned)((local + 255) / 256), (unsigned)depths);
   gumbel_fill_shard_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      out, local, s, row_elems, (uint32_t)rng->draw_stride, rng->seed,
+      (float*)out, (uint32_t)local, sd, rng->seed,
       rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
   return check_launch("gumbel fill (shard)");
 }

@@ -145,20 +145,22 @@ def gumbel_fill(out: torch.Tensor, rng: L.Rng, depth0: int = 0) -> torch.Tensor:
 
 
 def gumbel_fill_shard(out: torch.Tensor, rng: L.Rng, rows: int, shard, row_elems: int,
-                      depth0: int = 0) -> torch.Tensor:
+                      depth0: int = 0, *, row_total: int | None = None, row0: int = 0) -> torch.Tensor:
     """Fill float32 ``out`` (depths, rows * batch_count * head_count * row_elems) with this
-    shard's slice of the full (rows, batch_total, head_total, row_elems) draw of ``rng``
-    (``rng`` is the plan of the FULL numel)."""
+    shard's slice of the full (row_total, batch_total, head_total, row_elems) draw of ``rng``
+    (``rng`` is the plan of the FULL numel); the shard's rows are row0 .. row0 + rows - 1
+    (all rows by default)."""
     _require_cuda(out)
     if out.dtype != torch.float32 or not out.is_contiguous():
         raise ValueError("out must be a contiguous float32 tensor")
     depths = out.shape[0] if out.dim() > 1 else 1
     if out.numel() != depths * rows * shard.batch_count * shard.head_count * row_elems:
         raise ValueError("out does not hold this shard's draw")
-    sh = L.Shard(shard.batch_total, shard.batch0, shard.batch_count, shard.head_total,
-                 shard.head0, shard.head_count)
-    L.call("ta_gumbel_fill_shard", _ptr(out), ctypes.byref(rng), rows, ctypes.byref(sh),
-           row_elems, depth0, depths, _stream(out.device))
+    row_total = rows if row_total is None else row_total
+    sh = L.Shard(row_total, row0, rows, shard.batch_total, shard.batch0, shard.batch_count,
+                 shard.head_total, shard.head0, shard.head_count)
+    L.call("ta_gumbel_fill_shard", _ptr(out), ctypes.byref(rng), ctypes.byref(sh), row_elems,
+           depth0, depths, _stream(out.device))
     return out
 
 
@@ -230,7 +232,8 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
             max_logit: float = MAX_LOGIT, out: torch.Tensor | None = None,
             gumbels: torch.Tensor | None = None, want_packed: bool = False,
             rng: L.Rng | None = None, for_backward: bool = True,
-            fused_rng: bool = False, shard=None) -> ForwardResult:
+            fused_rng: bool = False, shard=None,
+            query_rows: tuple[int, int] | None = None) -> ForwardResult:
     """Fused sampler + softmax + value gather. q (L,B,H,D), k_int (N-1,B,H,D), v (N,B,H,D).
 
     The Gumbel noise comes from torch's default CUDA generator (reserved here, exactly as
@@ -241,6 +244,8 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
     per-path branch probabilities ``ta_backward`` needs. ``shard`` (a
     ``sharding.ShardSpec``) marks q/k/v as one (batch, head) block of a larger problem: the
     noise is then the matching slice of the full problem's draw (see ``gumbel_fill_shard``).
+    ``query_rows`` = (row0, row_total) does the same along the query axis: q holds queries
+    row0 .. row0 + L - 1 of a row_total-query problem (sequence parallelism).
     """
     _require_cuda(q, k_int, v)
     Lq, B, H, D = q.shape
@@ -259,17 +264,23 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
                              dtype=torch.uint8)
     numel = Lq * B * H * num_samples * 2
     rng_p = None
-    if shard is not None and not shard.is_full and gumbels is None:
-        if (shard.batch_count, shard.head_count) != (B, H):
-            raise ValueError(f"shard {shard} does not match q's (batch, heads) = ({B}, {H})")
+    sharded = (shard is not None and not shard.is_full) or query_rows is not None
+    if sharded and gumbels is None:
+        from .sharding import ShardSpec
+        spec = shard if shard is not None else ShardSpec(B, 0, B, H, 0, H)
+        if (spec.batch_count, spec.head_count) != (B, H):
+            raise ValueError(f"shard {spec} does not match q's (batch, heads) = ({B}, {H})")
+        row0, row_total = query_rows if query_rows is not None else (0, Lq)
+        if row0 < 0 or row0 + Lq > row_total:
+            raise ValueError(f"query rows {row0}..{row0 + Lq} outside {row_total}")
         if fused_rng:
             raise ValueError("fused_rng does not support shards")
         if rng is None:
-            rng = reserve_gumbel_stream(dev, Lq * shard.batch_total * shard.head_total * num_samples * 2,
-                                        log_n_of(N))
+            rng = reserve_gumbel_stream(
+                dev, row_total * spec.batch_total * spec.head_total * num_samples * 2, log_n_of(N))
         gumbels = gumbel_fill_shard(
-            torch.empty((log_n_of(N), numel), device=dev, dtype=torch.float32), rng, Lq, shard,
-            num_samples * 2)
+            torch.empty((log_n_of(N), numel), device=dev, dtype=torch.float32), rng, Lq, spec,
+            num_samples * 2, row_total=row_total, row0=row0)
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
     else:
@@ -292,7 +303,8 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
 
 def backward(q, k_int, v, grad_out, leaf, weights, branch_prob, num_samples, *,
              max_logit=MAX_LOGIT, dq=None, dk=None, dv=None, dk_dtype: torch.dtype | None = None):
-    """Deterministic gradients (dq, dk, dv) of ``forward``. All (seq, B, H, D) views."""
+    """Deterministic gradients (dq, dk, dv) of ``forward``. All (seq, B, H, D) views; dk and
+    dv may be float32 buffers whatever the input dtype."""
     _require_cuda(q, k_int, v, grad_out, leaf, weights, branch_prob)
     Lq, B, H, D = q.shape
     N = v.shape[0]
@@ -314,7 +326,8 @@ def backward(q, k_int, v, grad_out, leaf, weights, branch_prob, num_samples, *,
     L.call("ta_backward", ctypes.byref(shape), _ptr(q), layout(q), _ptr(k_int), layout(k_int),
            _ptr(v), layout(v), _ptr(grad_out), layout(grad_out), _ptr(leaf.contiguous()),
            _ptr(weights.contiguous()), _ptr(branch_prob), _ptr(dq), layout(dq), _ptr(dk), layout(dk),
-           dtype_code(dk.dtype), _ptr(dv), layout(dv), _ptr(ws), ws_bytes, _stream(dev))
+           dtype_code(dk.dtype), _ptr(dv), layout(dv), dtype_code(dv.dtype), _ptr(ws), ws_bytes,
+           _stream(dev))
     _note("backward")
     return dq, dk, dv
 
@@ -423,9 +436,12 @@ class CausalState:
     query_offset: int
 
 
-def causal_forward(q, k_int, v, num_samples, query_offset=0, *, out=None, gumbels=None):
+def causal_forward(q, k_int, v, num_samples, query_offset=0, *, out=None, gumbels=None,
+                   rng: L.Rng | None = None):
     """Causal sampler with the boundary correction for queries q (L,B,H,D) whose causal
-    boundaries are t + query_offset. Returns (out, CausalState)."""
+    boundaries are t + query_offset. Returns (out, CausalState). The noise of query t, level d
+    is the draw at ``rng.offset + (t * log2 N + d) * rng.offset_step`` (reserved from the
+    generator when ``rng`` is None)."""
     _require_cuda(q, k_int, v)
     Lq, B, H, D = q.shape
     N = v.shape[0]
@@ -444,7 +460,9 @@ def causal_forward(q, k_int, v, num_samples, query_offset=0, *, out=None, gumbel
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
     else:
-        rng_p = ctypes.byref(reserve_causal_stream(dev, B * H * S * 2, Lq * ln))
+        if rng is None:
+            rng = reserve_causal_stream(dev, B * H * S * 2, Lq * ln)
+        rng_p = ctypes.byref(rng)
     L.call("ta_causal_forward", ctypes.byref(shape), int(query_offset), _ptr(q), layout(q),
            _ptr(k_int), layout(k_int), _ptr(v), layout(v), _ptr(out), layout(out), rng_p,
            _ptr(gumbels), _ptr(leaf), _ptr(weights), _ptr(bp), _ptr(corrected), _ptr(masses),
