@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--batch", type=int, default=WORKLOAD["batch_per_gpu"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--mode", choices=["shard", "sp"], default="shard",
+                   help="shard: (batch, head)-sharded headline workload; sp: sequence-parallel "
+                        "causal long context (B=1, S=65536, H=32, d=128, 16 paths unless overridden)")
     return p.parse_args()
 
 
@@ -381,11 +384,104 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sp(args):
+    """Sequence-parallel causal long context: the global problem is fixed and split over the
+    ranks by sequence position (strong scaling). N=1 runs the plain causal op."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    import treeattn_b200 as ta
+    from treeattn_b200 import ops
+    from treeattn_b200.sequence_parallel import sp_tree_attention
+
+    d = dict(seq_len=65536, heads=32, num_samples=16)
+    S = args.seq_len if args.seq_len != WORKLOAD["seq_len"] else d["seq_len"]
+    H = args.heads if args.heads != WORKLOAD["heads"] else d["heads"]
+    P = args.num_samples if args.num_samples != WORKLOAD["num_samples"] else d["num_samples"]
+    B, D, n = 1, args.head_dim, S // world
+    gen = torch.Generator(device=dev).manual_seed(0)
+    full = [torch.randn(B, S, H, D, device=dev, generator=gen).to(torch.bfloat16) for _ in range(4)]
+    sl = slice(rank * n, (rank + 1) * n)
+    q, k, v, go = (t[:, sl].contiguous() for t in full)
+    del full
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        torch.manual_seed(0)
+        if world > 1:
+            out = sp_tree_attention(q, k, v, True, num_samples=P)
+        else:
+            out = ta.tree_attention(q, k, v, True, None, num_samples=P)
+        out.backward(go)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(dev.index)
+    ops.profile_enable(True)
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    ms_step = ms / args.steps
+    if rank == 0:
+        total = sum(t for _, t in prof.values()) or 1.0
+        line = {"metric": "causal long-context fwd+bwd tokens/s (sequence parallel)",
+                "value": B * S / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic N(0,1) q/k/v/grad_out from a seeded CUDA generator",
+                "config": {"workload": "stochastic tree attention, causal (exact prefix + corrected "
+                                       "sampler), sequence split over ranks", "batch": B, "seq_len": S,
+                           "heads": H, "head_dim": D, "num_samples": P,
+                           "parallelism": f"sequence-parallel x{world}: NCCL all-gather of K/V, "
+                                          "reduce-scatter of dK/dV"},
+                "gpu_launches": int(sum(c for c, _ in prof.values())),
+                "kernels": {k_: {"launches_per_step": c / args.steps, "ms_per_step": t / args.steps,
+                                 "share": t / total} for k_, (c, t) in
+                            sorted(prof.items(), key=lambda x: -x[1][1])},
+                "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     sys.path.insert(0, ROOT)
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "sp":
+        run_sp(args)
     else:
         run_ours(args)
 
