@@ -245,14 +245,17 @@ int ta_backward_coef(const ta_shape* shape, const void* q, ta_layout q_layout, c
 
 /*
  * Causal stochastic sampling for queries [0, L), query t's causal boundary leaf being
- * t + query_offset: pass 1 computes the boundary-path log-masses M[d] of every (b, h)
- * (float32 masses, (L, B, H, log2 N + 1)); pass 2 samples S paths per (b, h), correcting
+ * t + query_offset: pass 1 computes the boundary-path log-masses M[d] and boundary logits
+ * s_b[d] of every (b, h) (float32 masses, (L, B, H, 2 log2 N + 1): M[0..log2 N] then
+ * s_b[0..log2 N - 1]); pass 2 samples S paths per (b, h), correcting
  * level d's branch log-probabilities to m_child + lp - M[d] when every sample of the query
  * sits on the boundary node. Gumbel draws: one exponential_() of numel B*H*S*2 per (query,
  * level) at rng->offset + (t * log2 N + d) * rng->offset_step (ta_philox_plan of that
  * numel), or `gumbels` (L, log2 N, B, H, S, 2). Writes leaf, weights (softmax over the S
  * paths), out = sum w v[leaf], corrected[t] = number of leading corrected levels, and
- * branch_prob as ta_forward. One CTA per query: B*H*S*8 bytes of shared memory.
+ * branch_prob (16-byte aligned) as ta_forward. The corrected prefix runs one CTA per query
+ * (B*H*S*8 + B*H*(2 log2 N + 1)*4 bytes of shared memory, at most 200 KiB); the levels after
+ * it run per (batch, head) like ta_forward.
  * Replaces _sample_paths_causal (treeattn_torch/_tree_mha.py:125-268) and the stochastic
  * branch of hierarchical_attention (:379-412).
  */

@@ -10,8 +10,12 @@
 //           b, h, s) sits on the boundary node, the two branch log-probabilities become
 //           m_child + lp - M[d] (m_left/m_right as in pass 1); otherwise they are the raw
 //           logsigmoids. One Gumbel draw of B*H*S*2 values per (query, level).
-// The "every sample" predicate couples all (b, h) of a query, so one CTA owns one query and
-// evaluates the predicate with a block-wide AND between levels.
+// The "every sample" predicate couples all (b, h) of a query, so one CTA per query evaluates
+// it with a block-wide AND between levels (prefix kernel). While it holds, every sample of a
+// (b, h) stands on the boundary node, so those levels need only the boundary logits of pass
+// 1; once it fails it stays false, and the remaining levels of every path are independent
+// raw-logsigmoid steps, run by the non-causal sampler's kernel (kCausalTail in
+// ta_forward.cu) with its per-head shared-memory tree and four-lane dot products.
 //
 // Backward (coefficient form): every path contributes gl_{p,d} = sgn sigmoid(-sgn s) dlp_p at
 // each level (the raw logsigmoid part); the corrected levels add the gradient of the masses,
@@ -57,33 +61,45 @@ __device__ __forceinline__ float log_pow2(int m) {  // log(2^m) correctly rounde
   return (float)((double)m * 0.69314718055994530942);
 }
 
+// Prefix kernel, one CTA per query. Pass 1 (one thread per (b, h)): the boundary logits
+// s_b[d] and masses M[d], stored in masses[t][b][h] = (M[0..ln], s_b[0..ln-1]). Pass 2: while
+// EVERY sample of the query sits on the boundary node, all samples of a (b, h) stand on the
+// same node, whose logit is s_b[d]; the corrected decisions need no other dot product. The
+// first level after which some sample has left the boundary path ends the prefix: each path's
+// node and log-probability go to leaf / weights (the tail kernel continues from there),
+// `corrected` = number of prefix levels.
 template <typename T>
-__global__ void __launch_bounds__(kCausalThreads) causal_fwd_kernel(const CausalParams p) {
+__global__ void __launch_bounds__(kCausalThreads) causal_prefix_kernel(const CausalParams p) {
   extern __shared__ float sm[];
   const int64_t t = blockIdx.x;
   const int ln = p.log_n, S = p.S, BH = p.B * p.H;
   const int J = BH * S;
-  const uint32_t K = (uint32_t)p.N - 1u;
+  const int MS = 2 * ln + 1;
   const int64_t boundary = t + p.query_offset;
-  uint32_t* s_node = reinterpret_cast<uint32_t*>(sm);  // [J]
-  float* s_lp = sm + J;                                // [J]
+  float* s_ms = sm;                                             // [BH][MS]
+  uint32_t* s_node = reinterpret_cast<uint32_t*>(s_ms + BH * MS); // [J]
+  float* s_lp = reinterpret_cast<float*>(s_node + J);           // [J]
   const int tid = threadIdx.x;
-  // boundary nodes of every level
   auto bnode = [&](int d) -> uint32_t { return (1u << d) - 1u + (uint32_t)(boundary >> (ln - d)); };
   auto bdir = [&](int d) -> int { return (int)((boundary >> (ln - 1 - d)) & 1); };
-  float* M = p.masses + t * (int64_t)BH * (ln + 1);
-  // pass 1: boundary masses per (b, h)
-  for (int bh = tid; bh < BH; bh += blockDim.x) {
+  float* Mg = p.masses + t * (int64_t)BH * MS;
+  // boundary logits: all (b, h, level) dots in parallel
+  for (int i = tid; i < BH * ln; i += blockDim.x) {
+    const int bh = i / ln, d = i - bh * ln;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
     const char* qrow = p.q + (t * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
-    const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
-    float* Mb = M + (int64_t)bh * (ln + 1);
+    const char* krow = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh + (int64_t)bnode(d) * p.ks) * sizeof(T);
+    s_ms[bh * MS + ln + 1 + d] = dot_row<T>(qrow, krow, p.D);
+  }
+  __syncthreads();
+  // masses, bottom-up per (b, h)
+  for (int bh = tid; bh < BH; bh += blockDim.x) {
+    float* Mb = s_ms + bh * MS;
     float m = 0.0f;
     Mb[ln] = 0.0f;
     for (int d = ln - 1; d >= 0; --d) {
-      const float s = dot_row<T>(qrow, kbase + (int64_t)bnode(d) * p.ks * sizeof(T), p.D);
       float lpl, lpr;
-      log_sigmoid_pair(s, lpl, lpr);
+      log_sigmoid_pair(Mb[ln + 1 + d], lpl, lpr);
       float on, off, offm;
       if (bdir(d) == 0) { on = lpl; off = lpr; offm = -INFINITY; }
       else { on = lpr; off = lpl; offm = log_pow2(ln - 1 - d); }
@@ -93,38 +109,29 @@ __global__ void __launch_bounds__(kCausalThreads) causal_fwd_kernel(const Causal
       Mb[d] = m;
     }
   }
+  __syncthreads();
+  for (int i = tid; i < BH * MS; i += blockDim.x) Mg[i] = s_ms[i];
   for (int j = tid; j < J; j += blockDim.x) {
     s_node[j] = 0u;
     s_lp[j] = 0.0f;
   }
   __syncthreads();
-  // pass 2: sampling
-  const int M_draw = J * 2;
-  int on_path = 1;
-  int corrected = 0;
-  for (int d = 0; d < ln; ++d) {
-    if (on_path) corrected = d + 1;
+  int d = 0;
+  bool on_path = true;
+  while (on_path && d < ln) {
     const uint64_t off = p.offset + ((uint64_t)t * ln + d) * p.offset_step;
     int mine_on = 1;
     for (int j = tid; j < J; j += blockDim.x) {
       const int bh = j / S, s = j - bh * S;
-      const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-      const uint32_t node = s_node[j];
-      const char* qrow = p.q + (t * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
-      const char* krow = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh + (int64_t)node * p.ks) * sizeof(T);
-      const float x = dot_row<T>(qrow, krow, p.D);
-      float lpl, lpr;
-      log_sigmoid_pair(x, lpl, lpr);
-      const float raw_l = lpl, raw_r = lpr;
-      if (on_path) {
-        const float* Mb = M + (int64_t)bh * (ln + 1);
-        const float parent = Mb[d], child = Mb[d + 1];
-        float ml, mr;
-        if (bdir(d) == 0) { ml = child; mr = -INFINITY; }
-        else { ml = log_pow2(ln - 1 - d); mr = child; }
-        lpl = ml + lpl - parent;
-        lpr = mr + lpr - parent;
-      }
+      const float* Mb = s_ms + bh * MS;
+      const float x = Mb[ln + 1 + d];
+      float raw_l, raw_r;
+      log_sigmoid_pair(x, raw_l, raw_r);
+      const float parent = Mb[d], child = Mb[d + 1];
+      float ml, mr;
+      if (bdir(d) == 0) { ml = child; mr = -INFINITY; }
+      else { ml = log_pow2(ln - 1 - d); mr = child; }
+      const float lpl = ml + raw_l - parent, lpr = mr + raw_r - parent;
       float gl, gr;
       if (p.gumbels != nullptr) {
         const float* gp = p.gumbels + ((t * ln + d) * (int64_t)J + j) * 2;
@@ -134,10 +141,9 @@ __global__ void __launch_bounds__(kCausalThreads) causal_fwd_kernel(const Causal
         gl = torch_gumbel(p.seed, off, 2u * (uint32_t)j, p.stride);
         gr = torch_gumbel(p.seed, off, 2u * (uint32_t)j + 1u, p.stride);
       }
-      (void)M_draw;
       const int dir = (lpr + gr > lpl + gl) ? 1 : 0;
       s_lp[j] += dir ? lpr : lpl;
-      const uint32_t nn = 2u * node + 1u + (uint32_t)dir;
+      const uint32_t nn = 2u * s_node[j] + 1u + (uint32_t)dir;
       s_node[j] = nn;
       if (p.sig != nullptr) {
         const int64_t path = (int64_t)bh * p.L * S + t * S + s;
@@ -145,106 +151,101 @@ __global__ void __launch_bounds__(kCausalThreads) causal_fwd_kernel(const Causal
       }
       if (d + 1 < ln && nn != bnode(d + 1)) mine_on = 0;
     }
-    on_path = __syncthreads_and(on_path && mine_on);
+    ++d;
+    on_path = __syncthreads_and(mine_on) != 0;
   }
-  if (tid == 0) p.corrected[t] = corrected;
-  __syncthreads();
-  // softmax over the S paths of each (b, h) and the value gather
-  for (int bh = tid; bh < BH; bh += blockDim.x) {
+  if (tid == 0) p.corrected[t] = d;
+  for (int j = tid; j < J; j += blockDim.x) {
+    const int bh = j / S, s = j - bh * S;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-    float m = -INFINITY;
-    for (int s = 0; s < S; ++s) {
-      const int64_t lf = (int64_t)s_node[bh * S + s] - K;
-      if (lf >= 0 && lf < p.N) m = fmaxf(m, s_lp[bh * S + s]);
-    }
-    float sum = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      const int64_t lf = (int64_t)s_node[bh * S + s] - K;
-      if (lf >= 0 && lf < p.N) sum += expf(s_lp[bh * S + s] - m);
-    }
-    const float lse = m + logf(sum);
-    for (int s = 0; s < S; ++s) {
-      const int j = bh * S + s;
-      const int64_t lf = (int64_t)s_node[j] - K;
-      const float w = (lf >= 0 && lf < p.N) ? expf(s_lp[j] - lse) : 0.0f;
-      const int64_t o = ((t * p.B + b) * p.H + h) * (int64_t)S + s;
-      p.weights[o] = w;
-      p.leaf[o] = (int32_t)lf;
-      s_lp[j] = w;
-    }
-  }
-  __syncthreads();
-  const int Dc = p.D;
-  for (int idx = tid; idx < BH * Dc; idx += blockDim.x) {
-    const int bh = idx / Dc, c = idx - bh * Dc;
-    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-    float acc = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      int64_t lf = (int64_t)s_node[bh * S + s] - K;
-      lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-      const T* vrow = reinterpret_cast<const T*>(p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh + lf * p.vs) * sizeof(T));
-      acc = fmaf(s_lp[bh * S + s], static_cast<float>(vrow[c]), acc);
-    }
-    reinterpret_cast<T*>(p.out + (t * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T))[c] = static_cast<T>(acc);
+    const int64_t o = ((t * p.B + b) * p.H + h) * (int64_t)S + s;
+    p.leaf[o] = (int32_t)s_node[j];
+    p.weights[o] = s_lp[j];
   }
 }
 
-// Backward coefficients of query t: real paths (gl = sgn sigmoid(-sgn s) dlp) and the boundary
-// path (gradient of the corrected levels' masses), plus sort records.
+// Backward coefficients of query t, one thread per path: real paths get
+// gl = sgn sigmoid(-sgn s) dlp (s from the forward's branch probabilities), and one boundary
+// path per (b, h) carries the gradient of the corrected levels' masses, from the boundary
+// logits the prefix kernel stored. Writes the sort records of ta_backward_coef.
 template <typename T>
 __global__ void __launch_bounds__(kCausalThreads) causal_coef_kernel(const CausalParams p) {
+  extern __shared__ float sm[];
   const int64_t t = blockIdx.x;
   const int ln = p.log_n, S = p.S, BH = p.B * p.H, SP = S + 1;
+  const int J = BH * S;
+  const int MS = 2 * ln + 1;
   const uint32_t K = (uint32_t)p.N - 1u;
   const uint32_t base_node = (1u << ln) - 1u;
   const int64_t boundary = t + p.query_offset;
   const int corrected = p.corrected[t];
-  auto bnode = [&](int d) -> uint32_t { return (1u << d) - 1u + (uint32_t)(boundary >> (ln - d)); };
+  float* s_wg = sm;       // [J] w g
+  float* s_dl = sm + J;   // [J] dlp
+  const int tid = threadIdx.x;
   auto bdir = [&](int d) -> int { return (int)((boundary >> (ln - 1 - d)) & 1); };
-  for (int bh = threadIdx.x; bh < BH; bh += blockDim.x) {
+  for (int j = tid; j < J; j += blockDim.x) {
+    const int bh = j / S;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-    const int64_t o0 = ((t * p.B + b) * p.H + h) * (int64_t)S;
+    const int64_t o = ((t * p.B + b) * p.H + h) * (int64_t)S + (j - bh * S);
     const char* grow = p.dout + (t * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
-    const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-    // g_s, dlp_s
+    int64_t lf = p.leaf[o];
+    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+    const char* vrow = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh + lf * p.vs) * sizeof(T);
+    const float g = dot_row<T>(grow, vrow, p.D);
+    s_dl[j] = g;
+    s_wg[j] = p.weights[o] * g;
+  }
+  __syncthreads();
+  for (int j = tid; j < J; j += blockDim.x) {
+    const int bh = j / S, s = j - bh * S;
+    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const int64_t o = ((t * p.B + b) * p.H + h) * (int64_t)S + s;
     float wg = 0.0f;
-    float dsum = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      int64_t lf = p.leaf[o0 + s];
-      lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-      wg = fmaf(p.weights[o0 + s], dot_row<T>(grow, vbase + lf * p.vs * sizeof(T), p.D), wg);
-    }
-    const int64_t pbase = (int64_t)bh * p.L * SP + t * SP;
-    float A[32];
-    for (int d = 0; d < 32; ++d) A[d] = 0.0f;
-    for (int s = 0; s < S; ++s) {
-      int64_t lf = p.leaf[o0 + s];
-      const int64_t lfc = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-      const float g = dot_row<T>(grow, vbase + lfc * p.vs * sizeof(T), p.D);
-      const float w = p.weights[o0 + s];
-      const float dl = w * (g - wg);
-      dsum += dl;
-      const uint32_t bits = (uint32_t)lf + K - base_node;
-      const float* sg = p.sig + ((int64_t)bh * p.L * S + t * S + s) * p.sig_stride;
-      float* co = p.coef + (pbase + s) * p.sig_stride;
-      for (int d = 0; d < ln; ++d) {
-        const int dir = (int)((bits >> (ln - 1 - d)) & 1u);
-        co[d] = (dir ? -sg[d] : sg[d]) * dl;
-        if (d < corrected && dir == bdir(d)) A[d] += dl;
+    for (int u = 0; u < S; ++u) wg += s_wg[bh * S + u];  // same order for every path of bh
+    const float w = p.weights[o];
+    const float dl = w * (s_dl[j] - wg);
+    const int64_t lf = p.leaf[o];
+    const uint32_t bits = (uint32_t)lf + K - base_node;
+    const int64_t pidx = (int64_t)bh * p.L * SP + t * SP + s;
+    const float* sg = p.sig + ((int64_t)bh * p.L * S + t * S + s) * p.sig_stride;
+    float* co = p.coef + pidx * p.sig_stride;
+    for (int d4 = 0; d4 < ln; d4 += 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(sg + d4);
+      const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+      float cv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d4 + e;
+        const int dir = d < ln ? (int)((bits >> (ln - 1 - d)) & 1u) : 0;
+        cv[e] = d < ln ? (dir ? -gv[e] : gv[e]) * dl : 0.0f;
       }
-      p.dvw[pbase + s] = w;
-      p.keys[pbase + s] = bits;
-      p.vals[pbase + s] = (uint32_t)(t * SP + s);
+      *reinterpret_cast<float4*>(co + d4) = make_float4(cv[0], cv[1], cv[2], cv[3]);
     }
-    // boundary path: gradient of the masses M[d] of the corrected levels
-    const char* qrow = p.q + (t * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
-    const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
-    const float* Mb = p.masses + (t * (int64_t)BH + bh) * (ln + 1);
+    p.dvw[pidx] = w;
+    p.keys[pidx] = bits;
+    p.vals[pidx] = (uint32_t)(t * SP + s);
+    s_dl[j] = dl;  // only this thread reads or writes entry j in this pass
+  }
+  __syncthreads();
+  // boundary path of each (b, h): gradient of the masses M[d] of the corrected levels
+  for (int bh = tid; bh < BH; bh += blockDim.x) {
+    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const float* Mb = p.masses + (t * (int64_t)BH + bh) * MS;
+    const int64_t o0 = ((t * p.B + b) * p.H + h) * (int64_t)S;
+    const int64_t pbase = (int64_t)bh * p.L * SP + t * SP;
+    float dsum = 0.0f;
+    for (int u = 0; u < S; ++u) dsum += s_dl[bh * S + u];
     float* cb = p.coef + (pbase + S) * p.sig_stride;
     float dM = 0.0f;  // gradient reaching M[d]
     for (int d = 0; d < ln; ++d) {
       if (d < corrected) dM -= dsum;
-      const float s = dot_row<T>(qrow, kbase + (int64_t)bnode(d) * p.ks * sizeof(T), p.D);
+      float A = 0.0f;  // dlp of the samples that took the boundary branch at level d
+      if (d < corrected)
+        for (int u = 0; u < S; ++u) {
+          const uint32_t bits = (uint32_t)p.leaf[o0 + u] + K - base_node;
+          if ((int)((bits >> (ln - 1 - d)) & 1u) == bdir(d)) A += s_dl[bh * S + u];
+        }
+      const float s = Mb[ln + 1 + d];
       const float sig_m = 1.0f / (1.0f + expf(s));   // sigmoid(-s)
       const float sig_p = 1.0f / (1.0f + expf(-s));  // sigmoid(s)
       float lpl, lpr;
@@ -260,8 +261,9 @@ __global__ void __launch_bounds__(kCausalThreads) causal_coef_kernel(const Causa
         doff = sig_m;
       }
       cb[d] = dM * (pi * don + (1.0f - pi) * doff);
-      dM = pi * dM + (d < corrected ? A[d] : 0.0f);
+      dM = pi * dM + A;
     }
+    for (int d = ln; d < p.sig_stride; ++d) cb[d] = 0.0f;
     p.dvw[pbase + S] = 0.0f;
     p.keys[pbase + S] = (uint32_t)boundary;
     p.vals[pbase + S] = (uint32_t)(t * SP + S);
@@ -320,25 +322,29 @@ extern "C" int ta_causal_forward(const ta_shape* shape, int64_t query_offset, co
     p.stride.init(1);
   }
   const int J = p.B * p.H * p.S;
-  const size_t smem = (size_t)J * 8;
+  const size_t smem = (size_t)J * 8 + (size_t)p.B * p.H * (2 * p.log_n + 1) * 4;
   if (smem > 200 * 1024) return fail(TA_ERR_UNSUPPORTED, "batch * heads * samples too large for one CTA");
+  if (branch_prob && ((uintptr_t)branch_prob & 15))
+    return fail(TA_ERR_INVALID, "branch_prob must be 16-byte aligned");
   if (p.L == 0) return TA_OK;
   cudaStream_t st = (cudaStream_t)stream;
   switch (shape->dtype) {
-#define TA_LAUNCH(TY)                                                                          \
-  {                                                                                            \
-    if (smem > 48 * 1024)                                                                      \
-      cudaFuncSetAttribute(causal_fwd_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                           (int)smem);                                                         \
-    TA_PROFILE("causal_fwd", st);                                                              \
-    causal_fwd_kernel<TY><<<(unsigned)p.L, kCausalThreads, smem, st>>>(p);                     \
+#define TA_LAUNCH(TY)                                                                             \
+  {                                                                                               \
+    if (smem > 48 * 1024)                                                                         \
+      cudaFuncSetAttribute(causal_prefix_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           (int)smem);                                                            \
+    TA_PROFILE("causal_prefix", st);                                                              \
+    causal_prefix_kernel<TY><<<(unsigned)p.L, kCausalThreads, smem, st>>>(p);                     \
   }
     case TA_F32: TA_LAUNCH(float) break;
     case TA_F16: TA_LAUNCH(__half) break;
     default: TA_LAUNCH(__nv_bfloat16) break;
 #undef TA_LAUNCH
   }
-  return check_launch("causal forward");
+  if ((rc = check_launch("causal forward prefix"))) return rc;
+  return causal_tail(shape, q, ql, k, kl, v, vl, out, ol, gumbels ? nullptr : rng, gumbels,
+                     corrected, leaf, weights, branch_prob, st);
 }
 
 // The coefficient half of the causal backward: writes, for L*(S+1) paths per head (S sampled
@@ -365,10 +371,23 @@ extern "C" int ta_causal_coefficients(const ta_shape* shape, int64_t query_offse
   p.coef = coef; p.dvw = value_weight; p.keys = keys; p.vals = vals;
   if (p.L == 0) return TA_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  const size_t smem = (size_t)p.B * p.H * p.S * 8;
+  if (smem > 200 * 1024) return fail(TA_ERR_UNSUPPORTED, "batch * heads * samples too large for one CTA");
+  if (((uintptr_t)branch_prob & 15) || ((uintptr_t)coef & 15))
+    return fail(TA_ERR_INVALID, "branch_prob and coef must be 16-byte aligned");
   switch (shape->dtype) {
-    case TA_F32: { TA_PROFILE("causal_coef", st); causal_coef_kernel<float><<<(unsigned)p.L, 64, 0, st>>>(p); } break;
-    case TA_F16: { TA_PROFILE("causal_coef", st); causal_coef_kernel<__half><<<(unsigned)p.L, 64, 0, st>>>(p); } break;
-    default: { TA_PROFILE("causal_coef", st); causal_coef_kernel<__nv_bfloat16><<<(unsigned)p.L, 64, 0, st>>>(p); } break;
+#define TA_LAUNCH(TY)                                                                           \
+  {                                                                                             \
+    if (smem > 48 * 1024)                                                                       \
+      cudaFuncSetAttribute(causal_coef_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           (int)smem);                                                          \
+    TA_PROFILE("causal_coef", st);                                                              \
+    causal_coef_kernel<TY><<<(unsigned)p.L, kCausalThreads, smem, st>>>(p);                     \
+  }
+    case TA_F32: TA_LAUNCH(float) break;
+    case TA_F16: TA_LAUNCH(__half) break;
+    default: TA_LAUNCH(__nv_bfloat16) break;
+#undef TA_LAUNCH
   }
   return check_launch("causal coefficients");
 }

@@ -18,6 +18,10 @@ int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int check_view(const char* name, const void* ptr, ta_layout lay, int esize, bool allow_null);
 int check_shape(const ta_shape* s, bool need_pow2);
+int causal_tail(const ta_shape* shape, const void* q, ta_layout ql, const void* k, ta_layout kl,
+                const void* v, ta_layout vl, void* out, ta_layout ol, const ta_rng* rng,
+                const float* gumbels, const int32_t* corrected, int32_t* leaf, float* weights,
+                float* branch_prob, cudaStream_t st);
 int pick_cpl(int nchunks);
 
 // Per-launch CUDA-event timing, enabled by ta_profile_enable(1): a scope records an event

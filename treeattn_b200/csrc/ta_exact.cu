@@ -5,9 +5,9 @@
 // exp(log p) (they sum to one over a complete tree), causal weights mask leaves n > l + offset
 // and softmax over the rest; out = sum_n w_n v_n.
 //
-// Forward: one CTA per (query, batch, head) computes every node logit (K dots), every leaf's
-// weight and the weighted value sum. Backward: the same CTA layout forms two coefficient rows
-// per query --
+// Per block of queries: node logits S = Q K^T (GEMM), one CTA per (query, batch, head) for
+// the leaf weights, out = W V (GEMM). Backward: g = dO V^T (GEMM), the same per-query CTAs
+// form two coefficient rows --
 //   W[l][n] = w_n                                     (dV = W^T dO)
 //   C[l][node] = sigmoid(-s) DL(left) - sigmoid(s) DL(right)   (dq = C K, dK = C^T Q)
 // with dlp_n = w_n (g_n - sum_m w_m g_m) (causal) or w_n g_n (non-causal), g_n = dO . v_n, and
@@ -34,7 +34,7 @@ struct ExactParams {
   int32_t B, H, D, N, log_n, causal;
   int64_t l0, nq;          // query block [l0, l0 + nq)
   int64_t query_offset;    // causal boundary of query l is l + query_offset
-  int32_t mode;            // 0: forward (out); 1: weights only; 2: backward coefficients
+  float* partial;          // split-K partial tiles (kSplitPartialBytes)
 };
 
 __device__ __forceinline__ float block_reduce_sum(float v, float* s_red) {
@@ -60,48 +60,21 @@ __device__ __forceinline__ float block_reduce_max(float v, float* s_red) {
   return t;
 }
 
-template <typename T>
-__device__ __forceinline__ float row_dot(const float* a_smem, const char* row, int D) {
-  using E = Elem<T>;
-  float acc = 0.0f;
-  for (int c = 0; c < D; c += E::EPC) {
-    float f[E::EPC];
-    E::unpack(ldg16(row + c * sizeof(T)), f);
-#pragma unroll
-    for (int e = 0; e < E::EPC; ++e) acc = fmaf(a_smem[c + e], f[e], acc);
-  }
-  return acc;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kExactThreads) exact_kernel(const ExactParams p) {
-  extern __shared__ float sm[];
-  float* s_q = sm;                 // [D] query
-  float* s_g = sm + p.D;           // [D] grad_out (backward)
-  float* s_red = s_g + p.D;        // [32]
-  float* s_col = s_red + 32;       // [kExactThreads] column partial sums
+// Leaf weights of one (query, batch, head) from its node logits (already in node_buf):
+// log p(leaf) walks the leaf's path (root first, as the reference accumulates); causal rows
+// mask leaves beyond the boundary and softmax the rest, non-causal rows take exp(log p).
+// Consecutive leaves share their upper ancestors, so a warp's walk is mostly broadcast
+// reads of the same logits.
+__global__ void __launch_bounds__(kExactThreads) exact_weights_kernel(const ExactParams p) {
+  __shared__ float s_red[32];
   const int64_t lb = blockIdx.x / (p.B * p.H);
   const int bh = (int)(blockIdx.x - lb * p.B * p.H);
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int64_t l = p.l0 + lb;
-  const int K = p.N - 1, N = p.N, ln = p.log_n, D = p.D;
+  const int K = p.N - 1, N = p.N, ln = p.log_n;
   const int tid = threadIdx.x;
-  float* sd = p.node_buf + (lb * p.B * p.H + bh) * (int64_t)K;
+  const float* sd = p.node_buf + (lb * p.B * p.H + bh) * (int64_t)K;
   float* w = p.leaf_buf + (lb * p.B * p.H + bh) * (int64_t)N;
-
-  const char* qrow = p.q + (l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T);
-  for (int c = tid; c < D; c += blockDim.x) s_q[c] = static_cast<float>(reinterpret_cast<const T*>(qrow)[c]);
-  if (p.mode == 2) {
-    const char* grow = p.dout + (l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
-    for (int c = tid; c < D; c += blockDim.x) s_g[c] = static_cast<float>(reinterpret_cast<const T*>(grow)[c]);
-  }
-  __syncthreads();
-  // node logits
-  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
-  for (int n = tid; n < K; n += blockDim.x)
-    sd[n] = row_dot<T>(s_q, kbase + (int64_t)n * p.ks * sizeof(T), D);
-  __syncthreads();
-  // leaf log-probabilities (path order: root first, as the reference accumulates)
   const int64_t limit = l + p.query_offset;
   auto leaf_lp = [&](int n) -> float {
     const uint32_t bits = (uint32_t)n;
@@ -116,68 +89,51 @@ __global__ void __launch_bounds__(kExactThreads) exact_kernel(const ExactParams 
   };
   float lse = 0.0f;
   if (p.causal) {
+    // one walk per leaf: log p kept in w between the passes
     float m = -INFINITY;
-    for (int n = tid; n < N; n += blockDim.x)
-      if (n <= limit) m = fmaxf(m, leaf_lp(n));
+    for (int n = tid; n < N; n += blockDim.x) {
+      const float lp = n <= limit ? leaf_lp(n) : -INFINITY;
+      w[n] = lp;
+      m = fmaxf(m, lp);
+    }
     m = block_reduce_max(m, s_red);
-    float s = 0.0f;
+    float sum = 0.0f;
     for (int n = tid; n < N; n += blockDim.x)
-      if (n <= limit) s += expf(leaf_lp(n) - m);
-    s = block_reduce_sum(s, s_red);
-    lse = m + logf(s);
+      if (n <= limit) sum += expf(w[n] - m);
+    sum = block_reduce_sum(sum, s_red);
+    lse = m + logf(sum);
   }
   for (int n = tid; n < N; n += blockDim.x) {
     float wn;
-    if (p.causal) wn = n <= limit ? expf(leaf_lp(n) - lse) : 0.0f;
+    if (p.causal) wn = n <= limit ? expf(w[n] - lse) : 0.0f;
     else wn = expf(leaf_lp(n));
     w[n] = wn;
     if (p.weights) p.weights[((l * p.B + b) * p.H + h) * (int64_t)N + n] = wn;
   }
-  __syncthreads();
-  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-  if (p.mode == 1) return;
-  if (p.mode == 0) {
-    // out[c] = sum_n w_n v[n][c]: groups of D threads split the leaves, then a fixed-order sum
-    const int groups = max(1, (int)blockDim.x / D);
-    const int gidx = tid / D, c = tid - gidx * D;
-    float acc = 0.0f;
-    if (gidx < groups && c < D)
-      for (int n = gidx; n < N; n += groups)
-        acc = fmaf(w[n], static_cast<float>(reinterpret_cast<const T*>(vbase + (int64_t)n * p.vs * sizeof(T))[c]), acc);
-    if (D > (int)blockDim.x) {  // wide rows: each thread loops over columns
-      for (int cc = tid; cc < D; cc += blockDim.x) {
-        float a2 = 0.0f;
-        for (int n = 0; n < N; ++n)
-          a2 = fmaf(w[n], static_cast<float>(reinterpret_cast<const T*>(vbase + (int64_t)n * p.vs * sizeof(T))[cc]), a2);
-        reinterpret_cast<T*>(p.out + (l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T))[cc] = static_cast<T>(a2);
-      }
-      return;
-    }
-    s_col[tid] = acc;
-    __syncthreads();
-    if (tid < D) {
-      float t = 0.0f;
-      for (int g = 0; g < groups; ++g) t += s_col[g * D + tid];
-      reinterpret_cast<T*>(p.out + (l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T))[tid] = static_cast<T>(t);
-    }
-    return;
-  }
-  // backward: dlp_n, subtree sums, node coefficients
+}
+
+// Backward coefficients of one (query, batch, head): dlp_buf holds g_n = dO . v_n (from a
+// GEMM), leaf_buf the weights w, node_buf the node logits. Writes
+// C[node] = sigmoid(-s) DL(left) - sigmoid(s) DL(right) over the logits, with
+// dlp_n = w_n (g_n - sum_m w_m g_m) (causal) or w_n g_n, and DL(child) the sum of dlp over
+// the child's leaves (accumulated bottom-up over the weights, which the dV product has
+// already consumed).
+__global__ void __launch_bounds__(kExactThreads) exact_coef_kernel(const ExactParams p) {
+  __shared__ float s_red[32];
+  const int64_t lb = blockIdx.x / (p.B * p.H);
+  const int bh = (int)(blockIdx.x - lb * p.B * p.H);
+  const int K = p.N - 1, N = p.N, ln = p.log_n;
+  const int tid = threadIdx.x;
+  float* w = p.leaf_buf + (lb * p.B * p.H + bh) * (int64_t)N;
   float* dl = p.dlp_buf + (lb * p.B * p.H + bh) * (int64_t)N;
+  float* cb = p.node_buf + (lb * p.B * p.H + bh) * (int64_t)K;
   float wg = 0.0f;
-  for (int n = tid; n < N; n += blockDim.x) {
-    const float g = row_dot<T>(s_g, vbase + (int64_t)n * p.vs * sizeof(T), D);
-    dl[n] = g;
-    wg += w[n] * g;
+  if (p.causal) {
+    for (int n = tid; n < N; n += blockDim.x) wg += w[n] * dl[n];
+    wg = block_reduce_sum(wg, s_red);
   }
-  if (p.causal) wg = block_reduce_sum(wg, s_red);
-  __syncthreads();
   for (int n = tid; n < N; n += blockDim.x) dl[n] = p.causal ? w[n] * (dl[n] - wg) : w[n] * dl[n];
   __syncthreads();
-  // bottom-up over levels: DL(node) = dlp summed over the node's leaves (stored over the
-  // weights, which the dV product has already consumed), and the node's coefficient C
-  // replaces its logit once both children's sums are known
-  float* cb = p.node_buf + (lb * p.B * p.H + bh) * (int64_t)K;
   float* dlnode = w;  // K < N entries
   for (int d = ln - 1; d >= 0; --d) {
     const int first = (1 << d) - 1, cnt = 1 << d;
@@ -193,7 +149,6 @@ __global__ void __launch_bounds__(kExactThreads) exact_kernel(const ExactParams 
       }
       dlnode[node] = lsum + rsum;
       const float s = cb[node];
-      // C = sigmoid(-s) DL(left) - sigmoid(s) DL(right)
       const float sl = 1.0f / (1.0f + expf(s)), sr = 1.0f / (1.0f + expf(-s));
       cb[node] = sl * lsum - sr * rsum;
     }
@@ -203,33 +158,50 @@ __global__ void __launch_bounds__(kExactThreads) exact_kernel(const ExactParams 
 
 // ---------------------------------------------------------------------------------------
 // strided batched GEMM, fixed summation order: Y[m][n] (+)= sum_k A[m][k] * B[k][n]
-// A float32, B in T, Y float32 or T. One batch per (b, h) of the query block.
+// A and B float32 or T, Y float32 or T; one batch per (b, h). Tiles of BM x BN with a 4x4
+// register block per thread (BM * BN = 4096). With `splits` > 1 the k range is cut into
+// that many slices whose partial tiles go to `partial` ([split][b*H+h][M][Nn], float32) and
+// a second kernel sums them in slice order -- deterministic split-K for the skinny
+// products (M = a query block, k = all nodes or leaves).
 // ---------------------------------------------------------------------------------------
 struct GemmParams {
-  const float* A; int64_t sAm, sAk, sAb, sAh;  // batch strides per b and per h
-  const char* Bm; int64_t sBk, sBn, sBb, sBh;  // elements of T
-  char* Y; int64_t sYm, sYn, sYb, sYh;         // elements of the output type
+  const char* A; int64_t sAm, sAk, sAb, sAh;  // elements of A's type
+  const char* Bm; int64_t sBk, sBn, sBb, sBh; // elements of B's type
+  char* Y; int64_t sYm, sYn, sYb, sYh;        // elements of the output type
   int32_t M, Nn, Kd, H, accumulate, y_f32;
+  int32_t splits, kchunk;                     // split-K: slices of kchunk (multiple of 16)
+  float* partial;
 };
 
-template <typename T>
+template <typename TA_, typename TB_, typename TY, int BM>
 __global__ void __launch_bounds__(256) gemm_kernel(const GemmParams g) {
-  __shared__ float sA[16][65];
-  __shared__ float sB[16][65];
-  const int bh = blockIdx.z;
+  constexpr int BN = 4096 / BM;
+  constexpr int TX = BN / 4;  // threads along n
+  __shared__ float sA[16][BM + 1];
+  __shared__ float sB[16][BN + 1];
+  const int z = blockIdx.z;
+  const int split = z % g.splits, bh = z / g.splits;
   const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const float* A = g.A + (int64_t)b * g.sAb + (int64_t)h * g.sAh;
-  const T* Bm = reinterpret_cast<const T*>(g.Bm) + (int64_t)b * g.sBb + (int64_t)h * g.sBh;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
+  const TA_* A = reinterpret_cast<const TA_*>(g.A) + (int64_t)b * g.sAb + (int64_t)h * g.sAh;
+  const TB_* Bm = reinterpret_cast<const TB_*>(g.Bm) + (int64_t)b * g.sBb + (int64_t)h * g.sBh;
+  const int kbeg = split * g.kchunk;
+  const int kend = min(g.Kd, kbeg + g.kchunk);
   float acc[4][4] = {};
-  for (int k0 = 0; k0 < g.Kd; k0 += 16) {
-    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-      const int kk = i >> 6, mm = i & 63;
+  for (int k0 = kbeg; k0 < kend; k0 += 16) {
+    // the fast thread index runs along whichever operand axis is contiguous
+    for (int i = threadIdx.x; i < 16 * BM; i += 256) {
+      const int kk = g.sAk == 1 ? (i & 15) : i / BM;
+      const int mm = g.sAk == 1 ? (i >> 4) : i - kk * BM;
       const int m = m0 + mm, k = k0 + kk;
-      sA[kk][mm] = (m < g.M && k < g.Kd) ? A[(int64_t)m * g.sAm + (int64_t)k * g.sAk] : 0.0f;
-      const int n = n0 + mm;
-      sB[kk][mm] = (n < g.Nn && k < g.Kd) ? static_cast<float>(Bm[(int64_t)k * g.sBk + (int64_t)n * g.sBn]) : 0.0f;
+      sA[kk][mm] = (m < g.M && k < kend) ? static_cast<float>(A[(int64_t)m * g.sAm + (int64_t)k * g.sAk]) : 0.0f;
+    }
+    for (int i = threadIdx.x; i < 16 * BN; i += 256) {
+      const int kk = g.sBk == 1 ? (i & 15) : i / BN;
+      const int nn = g.sBk == 1 ? (i >> 4) : i - kk * BN;
+      const int n = n0 + nn, k = k0 + kk;
+      sB[kk][nn] = (n < g.Nn && k < kend) ? static_cast<float>(Bm[(int64_t)k * g.sBk + (int64_t)n * g.sBn]) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -254,23 +226,63 @@ __global__ void __launch_bounds__(256) gemm_kernel(const GemmParams g) {
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= g.Nn) continue;
-      const int64_t off = (int64_t)b * g.sYb + (int64_t)h * g.sYh + (int64_t)m * g.sYm + (int64_t)n * g.sYn;
-      if (g.y_f32) {
-        float* y = reinterpret_cast<float*>(g.Y) + off;
-        *y = g.accumulate ? *y + acc[i][j] : acc[i][j];
-      } else {
-        T* y = reinterpret_cast<T*>(g.Y) + off;
-        *y = static_cast<T>(g.accumulate ? static_cast<float>(*y) + acc[i][j] : acc[i][j]);
+      if (g.splits > 1) {
+        const int64_t BHn = gridDim.z / g.splits;
+        g.partial[(((int64_t)split * BHn + bh) * g.M + m) * g.Nn + n] = acc[i][j];
+        continue;
       }
+      const int64_t off = (int64_t)b * g.sYb + (int64_t)h * g.sYh + (int64_t)m * g.sYm + (int64_t)n * g.sYn;
+      TY* y = reinterpret_cast<TY*>(g.Y) + off;
+      *y = static_cast<TY>(g.accumulate ? static_cast<float>(*y) + acc[i][j] : acc[i][j]);
     }
   }
 }
 
-template <typename T>
-static void launch_gemm(const GemmParams& g, int BH, cudaStream_t st) {
-  const dim3 grid((unsigned)((g.Nn + 63) / 64), (unsigned)((g.M + 63) / 64), (unsigned)BH);
-  TA_PROFILE("exact_gemm", st);
-  gemm_kernel<T><<<grid, 256, 0, st>>>(g);
+template <typename TY>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const GemmParams g, int BH) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per = (int64_t)g.M * g.Nn;
+  if (i >= per * BH) return;
+  const int bh = (int)(i / per);
+  const int64_t r = i - bh * per;
+  const int m = (int)(r / g.Nn), n = (int)(r - (int64_t)m * g.Nn);
+  float t = 0.0f;
+  for (int s = 0; s < g.splits; ++s) t += g.partial[((int64_t)s * BH + bh) * per + r];
+  const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+  TY* y = reinterpret_cast<TY*>(g.Y) + (int64_t)b * g.sYb + (int64_t)h * g.sYh + (int64_t)m * g.sYm + (int64_t)n * g.sYn;
+  *y = static_cast<TY>(g.accumulate ? static_cast<float>(*y) + t : t);
+}
+
+constexpr int64_t kSplitPartialBytes = (int64_t)64 << 20;  // split-K partial tiles
+
+template <typename TA_, typename TB_, typename TY>
+static void launch_gemm(GemmParams g, int BH, cudaStream_t st, const char* what) {
+  TA_PROFILE(what, st);
+  // tile shape: 16 x 256 or 32 x 128 for a handful of query rows, else 64 x 64
+  const int BM = g.M <= 16 && g.Nn > 128 ? 16 : (g.M <= 32 ? 32 : 64), BN = 4096 / BM;
+  const int64_t tiles = (int64_t)((g.Nn + BN - 1) / BN) * ((g.M + BM - 1) / BM) * BH;
+  // split k when the tile grid cannot fill the GPU several times over and k is long
+  constexpr int64_t kTarget = 8 * 148;
+  int splits = 1;
+  if (tiles < kTarget && g.Kd >= 1024 && g.partial) {
+    splits = (int)((kTarget + tiles - 1) / tiles);
+    const int64_t cap = kSplitPartialBytes / ((int64_t)BH * g.M * g.Nn * 4);
+    if (splits > cap) splits = (int)cap;
+    if (splits > g.Kd / 256) splits = g.Kd / 256;
+    if (splits < 1) splits = 1;
+  }
+  g.kchunk = splits > 1 ? ((g.Kd + splits - 1) / splits + 15) / 16 * 16 : g.Kd;
+  if (splits > 1) splits = (g.Kd + g.kchunk - 1) / g.kchunk;
+  g.splits = splits;
+  const dim3 grid((unsigned)((g.Nn + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM),
+                  (unsigned)(BH * splits));
+  if (BM == 16) gemm_kernel<TA_, TB_, TY, 16><<<grid, 256, 0, st>>>(g);
+  else if (BM == 32) gemm_kernel<TA_, TB_, TY, 32><<<grid, 256, 0, st>>>(g);
+  else gemm_kernel<TA_, TB_, TY, 64><<<grid, 256, 0, st>>>(g);
+  if (splits > 1) {
+    const int64_t n = (int64_t)BH * g.M * g.Nn;
+    split_reduce_kernel<TY><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, BH);
+  }
 }
 
 static int64_t exact_block(int64_t L, int64_t B, int64_t H, int64_t N) {
@@ -282,57 +294,83 @@ static int64_t exact_block(int64_t L, int64_t B, int64_t H, int64_t N) {
 }
 
 template <typename T>
-static int run_exact(ExactParams p, int64_t L, cudaStream_t st, bool backward,
-                     const GemmParams* proto, char* dq, ta_layout dql, char* dk, ta_layout dkl,
-                     char* dv, ta_layout dvl, int32_t accumulate) {
+static int run_exact(ExactParams p, int64_t L, cudaStream_t st, bool backward, float* partial,
+                     char* dq, ta_layout dql, char* dk, ta_layout dkl, char* dv, ta_layout dvl,
+                     int32_t accumulate) {
   const int64_t qb = exact_block(L, p.B, p.H, p.N);
-  const size_t smem = (size_t)(2 * p.D + 32 + kExactThreads) * 4;
+  const int BH = p.B * p.H;
+  const int K = p.N - 1;
   for (int64_t l0 = 0; l0 < L; l0 += qb) {
     p.l0 = l0;
     p.nq = qb < L - l0 ? qb : L - l0;
-    p.mode = backward ? 1 : 0;
+    const unsigned rows = (unsigned)(p.nq * BH);
+    // node logits S = Q K^T for the block
+    GemmParams g{};
+    g.partial = partial;
+    g.A = p.q + (l0 * p.qs) * sizeof(T); g.sAm = p.qs; g.sAk = 1; g.sAb = p.qb; g.sAh = p.qh;
+    g.Bm = p.k; g.sBk = 1; g.sBn = p.ks; g.sBb = p.kb; g.sBh = p.kh;
+    g.Y = (char*)p.node_buf; g.sYm = (int64_t)BH * K; g.sYn = 1; g.sYb = (int64_t)p.H * K; g.sYh = K;
+    g.M = (int32_t)p.nq; g.Nn = K; g.Kd = p.D; g.H = p.H;
+    launch_gemm<T, T, float>(g, BH, st, "exact_gemm_logits");
     {
       TA_PROFILE(backward ? "exact_bwd_weights" : "exact_fwd", st);
-      exact_kernel<T><<<(unsigned)(p.nq * p.B * p.H), kExactThreads, smem, st>>>(p);
+      exact_weights_kernel<<<rows, kExactThreads, 0, st>>>(p);
     }
     int rc = check_launch("exact attention");
     if (rc) return rc;
-    if (!backward) continue;
-    // leaf_buf now holds w; dV (+)= W^T dO for this block
-    const int BH = p.B * p.H;
-    GemmParams g{};
-    g.A = p.leaf_buf; g.sAm = 1; g.sAk = (int64_t)BH * p.N; g.sAb = (int64_t)p.H * p.N; g.sAh = p.N;
+    if (!backward) {
+      // out = W V
+      g = GemmParams{};
+      g.partial = partial;
+      g.A = (const char*)p.leaf_buf; g.sAm = (int64_t)BH * p.N; g.sAk = 1; g.sAb = (int64_t)p.H * p.N; g.sAh = p.N;
+      g.Bm = p.v; g.sBk = p.vs; g.sBn = 1; g.sBb = p.vb; g.sBh = p.vh;
+      g.Y = p.out + (l0 * p.os) * sizeof(T); g.sYm = p.os; g.sYn = 1; g.sYb = p.ob; g.sYh = p.oh;
+      g.M = (int32_t)p.nq; g.Nn = p.D; g.Kd = p.N; g.H = p.H;
+      launch_gemm<float, T, T>(g, BH, st, "exact_gemm_out");
+      if ((rc = check_launch("exact attention gemm"))) return rc;
+      continue;
+    }
+    // g_n = dO . v_n for the block
+    g = GemmParams{};
+    g.partial = partial;
+    g.A = p.dout + (l0 * p.gs) * sizeof(T); g.sAm = p.gs; g.sAk = 1; g.sAb = p.gb; g.sAh = p.gh;
+    g.Bm = p.v; g.sBk = 1; g.sBn = p.vs; g.sBb = p.vb; g.sBh = p.vh;
+    g.Y = (char*)p.dlp_buf; g.sYm = (int64_t)BH * p.N; g.sYn = 1; g.sYb = (int64_t)p.H * p.N; g.sYh = p.N;
+    g.M = (int32_t)p.nq; g.Nn = p.N; g.Kd = p.D; g.H = p.H;
+    launch_gemm<T, T, float>(g, BH, st, "exact_gemm_g");
+    // dV (+)= W^T dO
+    g = GemmParams{};
+    g.partial = partial;
+    g.A = (const char*)p.leaf_buf; g.sAm = 1; g.sAk = (int64_t)BH * p.N; g.sAb = (int64_t)p.H * p.N; g.sAh = p.N;
     g.Bm = p.dout + (l0 * p.gs) * sizeof(T); g.sBk = p.gs; g.sBn = 1; g.sBb = p.gb; g.sBh = p.gh;
     g.Y = dv; g.sYm = dvl.seq; g.sYn = 1; g.sYb = dvl.batch; g.sYh = dvl.head;
-    g.M = p.N; g.Nn = p.D; g.Kd = (int32_t)p.nq; g.H = p.H; g.y_f32 = 1;
+    g.M = p.N; g.Nn = p.D; g.Kd = (int32_t)p.nq; g.H = p.H;
     g.accumulate = (accumulate || l0 > 0) ? 1 : 0;
-    launch_gemm<T>(g, BH, st);
-    // coefficients C for the block
-    p.mode = 2;
+    launch_gemm<float, T, float>(g, BH, st, "exact_gemm_dv");
     {
       TA_PROFILE("exact_bwd_coef", st);
-      exact_kernel<T><<<(unsigned)(p.nq * p.B * p.H), kExactThreads, smem, st>>>(p);
+      exact_coef_kernel<<<rows, kExactThreads, 0, st>>>(p);
     }
     if ((rc = check_launch("exact attention backward"))) return rc;
-    const int K = p.N - 1;
     // dq = C K   (rows of this block; written, not accumulated)
     g = GemmParams{};
-    g.A = p.node_buf; g.sAm = (int64_t)BH * K; g.sAk = 1; g.sAb = (int64_t)p.H * K; g.sAh = K;
+    g.partial = partial;
+    g.A = (const char*)p.node_buf; g.sAm = (int64_t)BH * K; g.sAk = 1; g.sAb = (int64_t)p.H * K; g.sAh = K;
     g.Bm = p.k; g.sBk = p.ks; g.sBn = 1; g.sBb = p.kb; g.sBh = p.kh;
     g.Y = dq + (l0 * dql.seq) * sizeof(T); g.sYm = dql.seq; g.sYn = 1; g.sYb = dql.batch; g.sYh = dql.head;
-    g.M = (int32_t)p.nq; g.Nn = p.D; g.Kd = K; g.H = p.H; g.y_f32 = 0; g.accumulate = 0;
-    launch_gemm<T>(g, BH, st);
+    g.M = (int32_t)p.nq; g.Nn = p.D; g.Kd = K; g.H = p.H;
+    launch_gemm<float, T, T>(g, BH, st, "exact_gemm_dq");
     // dK (+)= C^T Q
     g = GemmParams{};
-    g.A = p.node_buf; g.sAm = 1; g.sAk = (int64_t)BH * K; g.sAb = (int64_t)p.H * K; g.sAh = K;
+    g.partial = partial;
+    g.A = (const char*)p.node_buf; g.sAm = 1; g.sAk = (int64_t)BH * K; g.sAb = (int64_t)p.H * K; g.sAh = K;
     g.Bm = p.q + (l0 * p.qs) * sizeof(T); g.sBk = p.qs; g.sBn = 1; g.sBb = p.qb; g.sBh = p.qh;
     g.Y = dk; g.sYm = dkl.seq; g.sYn = 1; g.sYb = dkl.batch; g.sYh = dkl.head;
-    g.M = K; g.Nn = p.D; g.Kd = (int32_t)p.nq; g.H = p.H; g.y_f32 = 1;
+    g.M = K; g.Nn = p.D; g.Kd = (int32_t)p.nq; g.H = p.H;
     g.accumulate = (accumulate || l0 > 0) ? 1 : 0;
-    launch_gemm<T>(g, BH, st);
+    launch_gemm<float, T, float>(g, BH, st, "exact_gemm_dk");
     if ((rc = check_launch("exact attention gemm"))) return rc;
   }
-  (void)proto;
   return TA_OK;
 }
 
@@ -350,7 +388,8 @@ using namespace ta;
 extern "C" size_t ta_exact_workspace_size(const ta_shape* shape) {
   if (exact_checks(shape) != TA_OK) return 0;
   const int64_t qb = exact_block(shape->num_queries, shape->batch, shape->num_heads, shape->num_leaves);
-  return (size_t)(qb * shape->batch * shape->num_heads * 3 * shape->num_leaves * 4) + 256;
+  return (size_t)(qb * shape->batch * shape->num_heads * 3 * shape->num_leaves * 4) + 256 +
+         (size_t)kSplitPartialBytes;
 }
 
 static int exact_common(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
@@ -376,6 +415,7 @@ static int exact_common(const ta_shape* shape, const void* q, ta_layout ql, cons
   p.node_buf = base;
   p.leaf_buf = base + qb * p.B * p.H * (int64_t)p.N;
   p.dlp_buf = p.leaf_buf + qb * p.B * p.H * (int64_t)p.N;
+  p.partial = (float*)(((uintptr_t)(p.dlp_buf + qb * p.B * p.H * (int64_t)p.N) + 255) & ~(uintptr_t)255);
   return TA_OK;
 }
 
@@ -393,9 +433,9 @@ extern "C" int ta_exact_forward(const ta_shape* shape, int32_t causal, int64_t q
   p.query_offset = query_offset;
   cudaStream_t st = (cudaStream_t)stream;
   switch (shape->dtype) {
-    case TA_F32: return run_exact<float>(p, shape->num_queries, st, false, nullptr, nullptr, {}, nullptr, {}, nullptr, {}, 0);
-    case TA_F16: return run_exact<__half>(p, shape->num_queries, st, false, nullptr, nullptr, {}, nullptr, {}, nullptr, {}, 0);
-    default: return run_exact<__nv_bfloat16>(p, shape->num_queries, st, false, nullptr, nullptr, {}, nullptr, {}, nullptr, {}, 0);
+    case TA_F32: return run_exact<float>(p, shape->num_queries, st, false, p.partial, nullptr, {}, nullptr, {}, nullptr, {}, 0);
+    case TA_F16: return run_exact<__half>(p, shape->num_queries, st, false, p.partial, nullptr, {}, nullptr, {}, nullptr, {}, 0);
+    default: return run_exact<__nv_bfloat16>(p, shape->num_queries, st, false, p.partial, nullptr, {}, nullptr, {}, nullptr, {}, 0);
   }
 }
 
@@ -417,8 +457,8 @@ extern "C" int ta_exact_backward(const ta_shape* shape, int32_t causal, int64_t 
   p.query_offset = query_offset;
   cudaStream_t st = (cudaStream_t)stream;
   switch (shape->dtype) {
-    case TA_F32: return run_exact<float>(p, shape->num_queries, st, true, nullptr, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
-    case TA_F16: return run_exact<__half>(p, shape->num_queries, st, true, nullptr, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
-    default: return run_exact<__nv_bfloat16>(p, shape->num_queries, st, true, nullptr, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
+    case TA_F32: return run_exact<float>(p, shape->num_queries, st, true, p.partial, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
+    case TA_F16: return run_exact<__half>(p, shape->num_queries, st, true, p.partial, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
+    default: return run_exact<__nv_bfloat16>(p, shape->num_queries, st, true, p.partial, (char*)dq, dql, (char*)dk, dkl, (char*)dv, dvl, accumulate);
   }
 }

@@ -26,7 +26,10 @@ namespace ta {
 constexpr int kFwdThreads = 256;
 constexpr int kFwdGroups = kFwdThreads / 4;  // queries per CTA
 
-enum FwdMode { kFull = 0, kSampleOnly = 1, kReplay = 2, kReplaySoftmax = 3 };
+// kCausalTail: the causal sampler's levels after its corrected prefix (ta_causal.cu), each
+// path starting from the node and log-probability the prefix kernel left in leaf / weights,
+// one torch draw of B*H*S*2 per (query, level), no logit clamp; outputs as kFull.
+enum FwdMode { kFull = 0, kSampleOnly = 1, kReplay = 2, kReplaySoftmax = 3, kCausalTail = 4 };
 
 struct FwdParams {
   const char* q;
@@ -50,6 +53,7 @@ struct FwdParams {
   float max_logit;
   int32_t mode;
   int32_t top_levels;  // tree levels staged in shared memory
+  const int32_t* corrected;  // kCausalTail: levels the prefix kernel already sampled, per query
 };
 
 template <typename T, int CPL>
@@ -98,8 +102,13 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
       qraw[i] = c < p.nchunks ? ldg16(qrow + c * 16) : make_uint4(0, 0, 0, 0);
     }
   }
-  const bool replay = p.mode >= kReplay;
+  const bool replay = p.mode == kReplay || p.mode == kReplaySoftmax;
+  const bool causal = p.mode == kCausalTail;
   const uint32_t M = 2u * (uint32_t)p.L * (uint32_t)p.B * (uint32_t)p.H * (uint32_t)p.S;
+  const int d0 = causal ? p.corrected[l] : 0;
+  // causal draws: per (query, level), element 2 * ((b*H + h)*S + s) + side
+  const uint32_t jq = (uint32_t)(b * p.H + h) * (uint32_t)p.S;
+  const uint32_t Jq = (uint32_t)(p.B * p.H * p.S);
 
   for (int s0 = 0; s0 < p.S; s0 += 4) {
     const int ns = min(4, p.S - s0);
@@ -107,7 +116,19 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
     float lp = 0.0f;  // path s0 + t4
     const uint32_t jm = j0 + s0 + t4;
     float sig4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int depth = 0; depth < p.log_n; ++depth) {
+    if (causal) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        node[t] = t < ns ? (uint32_t)p.leaf[j0 + s0 + t] : 0u;
+      if (t4 < ns) {
+        lp = p.weights[jm];
+        if (sig_row0 != nullptr && (d0 & 3)) {  // keep the prefix kernel's entries of this quad
+          const float4 o = *reinterpret_cast<const float4*>(sig_row0 + (int64_t)(s0 + t4) * p.sig_stride + (d0 & ~3));
+          sig4[0] = o.x; sig4[1] = o.y; sig4[2] = o.z; sig4[3] = o.w;
+        }
+      }
+    }
+    for (int depth = d0; depth < p.log_n; ++depth) {
       uint4 raw[4][CPL];
       if (depth < p.top_levels) {
 #pragma unroll
@@ -152,7 +173,19 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
           dir = (byte >> (depth & 7)) & 1;
         } else {
           float gl, gr;
-          if (p.gumbels != nullptr) {
+          if (causal) {
+            const uint32_t jl = jq + (uint32_t)(s0 + t4);
+            if (p.gumbels != nullptr) {
+              const float2 gg = *reinterpret_cast<const float2*>(
+                  p.gumbels + (((uint64_t)l * p.log_n + depth) * Jq + jl) * 2u);
+              gl = gg.x;
+              gr = gg.y;
+            } else {
+              const uint64_t off = p.offset + ((uint64_t)l * p.log_n + depth) * p.offset_step;
+              gl = torch_gumbel(p.seed, off, 2u * jl, p.stride);
+              gr = torch_gumbel(p.seed, off, 2u * jl + 1u, p.stride);
+            }
+          } else if (p.gumbels != nullptr) {
             const float2 gg = *reinterpret_cast<const float2*>(p.gumbels + (uint64_t)depth * M + 2u * jm);
             gl = gg.x;
             gr = gg.y;
@@ -227,7 +260,7 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
       }
     }
   }
-  if (p.mode != kFull) return;
+  if (p.mode != kFull && p.mode != kCausalTail) return;
 
   // out[l,b,h] = sum_s w_s v[leaf_s]
   float acc[NE];
@@ -423,7 +456,8 @@ static void launch_fwd(const FwdParams& p, cudaStream_t st, bool value_only) {
                       (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(fwd_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  TA_PROFILE(p.mode == kFull ? "fwd_fused" : (p.mode == kSampleOnly ? "sample_paths" : "replay_paths"), st);
+  TA_PROFILE(p.mode == kFull ? "fwd_fused" : p.mode == kSampleOnly ? "sample_paths"
+             : p.mode == kCausalTail ? "causal_tail" : "replay_paths", st);
   fwd_kernel<T, CPL><<<grid, kFwdThreads, smem, st>>>(p);
 }
 
@@ -514,6 +548,36 @@ extern "C" int ta_forward(const ta_shape* shape, const void* q, ta_layout ql, co
   p.mode = kFull;
   return run_fwd(p, shape->dtype, (cudaStream_t)stream, false);
 }
+
+namespace ta {
+
+// Levels after the causal prefix (see kCausalTail); called by ta_causal_forward once the
+// prefix kernel has left each path's node in `leaf`, its log-probability in `weights`, its
+// prefix branch probabilities in branch_prob and the prefix length in `corrected`.
+int causal_tail(const ta_shape* shape, const void* q, ta_layout ql, const void* k, ta_layout kl,
+                const void* v, ta_layout vl, void* out, ta_layout ol, const ta_rng* rng,
+                const float* gumbels, const int32_t* corrected, int32_t* leaf, float* weights,
+                float* branch_prob, cudaStream_t st) {
+  FwdParams p{};
+  fill_common(p, shape);
+  int rc = fill_rng(p, rng, gumbels);
+  if (rc) return rc;
+  p.q = (const char*)q; p.k = (const char*)k; p.v = (const char*)v; p.out = (char*)out;
+  p.qs = ql.seq; p.qb = ql.batch; p.qh = ql.head;
+  p.ks = kl.seq; p.kb = kl.batch; p.kh = kl.head;
+  p.vs = vl.seq; p.vb = vl.batch; p.vh = vl.head;
+  p.os = ol.seq; p.ob = ol.batch; p.oh = ol.head;
+  p.leaf = leaf; p.weights = weights; p.packed = nullptr;
+  p.sig = branch_prob;
+  p.P = shape->num_queries * shape->num_samples;
+  p.sig_stride = (p.log_n + 3) & ~3;
+  p.max_logit = INFINITY;  // treeattn-torch's causal sampler does not clamp
+  p.corrected = corrected;
+  p.mode = kCausalTail;
+  return run_fwd(p, shape->dtype, st, false);
+}
+
+}  // namespace ta
 
 extern "C" int ta_sample_paths(const ta_shape* shape, const void* q, ta_layout ql, const void* k,
                                ta_layout kl, const ta_rng* rng, const float* gumbels,

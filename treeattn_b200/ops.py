@@ -455,7 +455,7 @@ def causal_forward(q, k_int, v, num_samples, query_offset=0, *, out=None, gumbel
     weights = torch.empty((Lq, B, H, S), device=dev, dtype=torch.float32)
     bp = torch.empty((B * H, Lq * S, branch_prob_stride(N)), device=dev, dtype=torch.float32)
     corrected = torch.empty((max(Lq, 1),), device=dev, dtype=torch.int32)
-    masses = torch.empty((max(Lq, 1), B, H, ln + 1), device=dev, dtype=torch.float32)
+    masses = torch.empty((max(Lq, 1), B, H, 2 * ln + 1), device=dev, dtype=torch.float32)
     rng_p = None
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
