@@ -154,6 +154,26 @@ int ta_tree_build(int32_t dtype, int64_t batch, int64_t seq_len, int64_t num_hea
                   ta_stream_t stream);
 
 /*
+ * ta_tree_build / ta_tree_build_backward with a choice of node order. TA_LAYOUT_REFERENCE is
+ * the reference's: attn-bench's build returns its coefficients in position order (node n =
+ * position n + 1) and the samplers read that array as a heap, so a heap node does not hold
+ * its own subtree's summary (_treeattn_common.py:54-86 read by _tree_mha.py:99-121).
+ * TA_LAYOUT_TREE puts each coefficient on the heap node of the subtree it summarises:
+ * node (depth d, index i) = (mean(left half) - mean(right half)) / 2 of leaves
+ * [i * 2^(log2 S - d), (i + 1) * 2^(log2 S - d)), each op rounded to the input dtype. No
+ * counterpart in the reference (a semantic fix behind a flag).
+ */
+enum { TA_LAYOUT_REFERENCE = 0, TA_LAYOUT_TREE = 1 };
+int ta_tree_build_ex(int32_t dtype, int64_t batch, int64_t seq_len, int64_t num_heads,
+                     int64_t head_dim, const void* k_leaf, ta_layout k_leaf_layout, void* k_int,
+                     ta_layout k_int_layout, int32_t node_layout, void* workspace,
+                     size_t workspace_bytes, ta_stream_t stream);
+int ta_tree_build_backward_ex(int32_t dtype, int64_t batch, int64_t seq_len, int64_t num_heads,
+                              int64_t head_dim, const float* dk_int, ta_layout dk_int_layout,
+                              void* dk_leaf, ta_layout dk_leaf_layout, int32_t node_layout,
+                              void* workspace, size_t workspace_bytes, ta_stream_t stream);
+
+/*
  * ta_tree_build without a workspace, for callers that cannot allocate device memory (a host
  * whose runtime owns all HBM in its own pool, or a C/FFI caller with no device allocator).
  * It has no counterpart in the reference. The scratch is a fixed per-device array of

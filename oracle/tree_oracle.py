@@ -88,6 +88,28 @@ def haar_internal_node_keys(k_sbhd: np.ndarray, dtype: str = "f32") -> np.ndarra
     return out[1:].copy()
 
 
+def tree_layout_rows(num_leaves: int) -> np.ndarray:
+    """Heap row of every position-order coefficient (tree-correct layout, no reference
+    counterpart): position p >= 1 with l = ctz(p) holds the level-l pair of the block of
+    2^(l+1) leaves starting at p - 2^l, i.e. heap node (depth log2 N - 1 - l, index
+    p >> (l + 1)). Returns rows[p - 1] for p = 1 .. N-1."""
+    ln = num_leaves.bit_length() - 1
+    rows = np.empty(num_leaves - 1, dtype=np.int64)
+    for pos in range(1, num_leaves):
+        lvl = (pos & -pos).bit_length() - 1
+        d = ln - 1 - lvl
+        rows[pos - 1] = (1 << d) - 1 + (pos >> (lvl + 1))
+    return rows
+
+
+def tree_layout_node_keys(k_sbhd: np.ndarray, dtype: str = "f32") -> np.ndarray:
+    """The Haar build with each coefficient moved to its subtree's heap node."""
+    ref = haar_internal_node_keys(k_sbhd, dtype)
+    out = np.empty_like(ref)
+    out[tree_layout_rows(k_sbhd.shape[0])] = ref
+    return out
+
+
 def haar_internal_node_keys_backward(grad_internal: np.ndarray) -> np.ndarray:
     """Exact (float32) transpose of the Haar build: grad wrt leaf keys.
 
@@ -282,19 +304,25 @@ def path_bits_from_leaf(leaf: np.ndarray, num_leaves: int) -> np.ndarray:
 # --------------------------------------------------------------------------------------
 
 def adapter_forward_backward(q_bshd, k_bshd, v_bshd, grad_out_bshd, gumbels, num_samples,
-                             dtype="f32", max_logit=MAX_LOGIT):
+                             dtype="f32", max_logit=MAX_LOGIT, node_layout="reference"):
     """fn(q,k,v) of the attn-bench adapter, with its backward.
 
     Inputs are float32 arrays holding ``dtype`` values, layout (B,S,H,D).
     Returns dict(out, dq, dk, dv, weights, leaf) in bshd (out rounded to ``dtype``).
+    ``node_layout="tree"`` uses the tree-correct node order (no reference counterpart).
     """
     q = np.transpose(q_bshd, (1, 0, 2, 3))
     k = np.transpose(k_bshd, (1, 0, 2, 3))
     v = np.transpose(v_bshd, (1, 0, 2, 3))
     k_int = haar_internal_node_keys(k, dtype)
+    rows = tree_layout_rows(k.shape[0]) if node_layout == "tree" else None
+    if rows is not None:
+        k_int = k_int[np.argsort(rows)]
     fw = forward(q, k_int, v, gumbels, num_samples, max_logit)
     do = np.transpose(grad_out_bshd, (1, 0, 2, 3))
     dq, dk_int, dv = backward(q, k_int, v, do, fw["leaf"], fw["weights"], max_logit)
+    if rows is not None:
+        dk_int = dk_int[rows]
     dk = haar_internal_node_keys_backward(dk_int)
     t = lambda x: np.ascontiguousarray(np.transpose(x, (1, 0, 2, 3)))  # noqa: E731
     return dict(out=t(round_to_dtype(fw["out"], dtype)), dq=t(dq), dk=t(dk), dv=t(dv),

@@ -123,3 +123,13 @@ def test_bench_adapter_metadata():
     assert a.name == "treeattn_b200" and a.layout == "bshd" and a.supports_backward
     assert a.is_compatible(torch.bfloat16, 128, False)[0]
     assert a.is_compatible(torch.bfloat16, 128, True)[0]
+
+
+def test_tree_aware_accounting():
+    from treeattn_b200 import bench as tb
+    from_dense = 4.0 * 1 * 16 * 16384 * 16384 * 128
+    f = tb.fwd_flops(1, 16384, 16, 128, False, 8)
+    assert f == 16384 * 16 * 8 * 15 * 2 * 128
+    assert f < from_dense / 100
+    assert tb.bwd_flops(1, 16384, 16, 128, False, 8) > f
+    assert tb.compulsory_bytes(1, 16384, 16, 128) == 12 * 16384 * 16 * 128 * 2

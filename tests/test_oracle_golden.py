@@ -130,3 +130,22 @@ def test_oracle_exact_matches_reference(path):
     for name, t in (("dq", qt), ("dk", kt), ("dv", vt)):
         np.testing.assert_allclose(t.grad.numpy().reshape(f[name].shape), f[name], atol=2e-4,
                                    rtol=2e-4, err_msg=name)
+
+
+def test_tree_layout_nodes_summarise_their_subtrees():
+    # float32 leaves whose halving steps are exact: node (d, i) = (mean L - mean R) / 2
+    rng = np.random.default_rng(3)
+    S = 64
+    k = rng.integers(-8, 8, size=(S, 1, 2, 4)).astype(np.float32)
+    nodes = O.tree_layout_node_keys(k, "f32")
+    ln = 6
+    for d in range(ln):
+        span = S >> d
+        for i in range(1 << d):
+            lo = k[i * span:i * span + span // 2].mean(axis=0)
+            hi = k[i * span + span // 2:(i + 1) * span].mean(axis=0)
+            np.testing.assert_allclose(nodes[(1 << d) - 1 + i], (lo - hi) / 2, rtol=0, atol=1e-6)
+    # a permutation of the reference array
+    ref = O.haar_internal_node_keys(k, "f32")
+    assert sorted(O.tree_layout_rows(S).tolist()) == list(range(S - 1))
+    np.testing.assert_array_equal(np.sort(nodes.ravel()), np.sort(ref.ravel()))

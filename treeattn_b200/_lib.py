@@ -22,6 +22,8 @@ TA_ERR_WORKSPACE = 4
 TA_F32 = 0
 TA_F16 = 1
 TA_BF16 = 2
+TA_LAYOUT_REFERENCE = 0
+TA_LAYOUT_TREE = 1
 
 
 class Layout(ctypes.Structure):
@@ -86,6 +88,9 @@ SIGNATURES = {
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),
+    "ta_tree_build_ex": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _I32, _P, _SZ, _P]),
+    "ta_tree_build_backward_ex": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _I32,
+                                                 _P, _SZ, _P]),
     "ta_tree_build_backward_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "ta_tree_build_backward": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P,
                                               _SZ, _P]),

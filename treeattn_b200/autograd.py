@@ -56,9 +56,11 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False, shard=None):
+    def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False, shard=None,
+                node_layout="reference"):
         qv, kv, vv = (t.transpose(0, 1) for t in (q, k, v))  # logical (S, B, H, D) views
-        k_int = ops.tree_build(kv)
+        k_int = ops.tree_build(kv, node_layout=node_layout)
+        ctx.node_layout = node_layout
         out = torch.empty_like(q)
         ctx.num_samples = num_samples
         ctx.max_logit = max_logit
@@ -87,9 +89,9 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
             _causal_bwd(q.transpose(0, 1), k_int, v.transpose(0, 1), grad_out.transpose(0, 1), st,
                         ctx.num_samples, dq.transpose(0, 1), dk_int, dv32)
             dk = torch.empty_like(q)
-            ops.tree_build_backward(dk_int, dk.transpose(0, 1))
+            ops.tree_build_backward(dk_int, dk.transpose(0, 1), ctx.node_layout)
             dv = dv32.transpose(0, 1).to(v.dtype).contiguous()
-            return dq, dk, dv, None, None, None, None, None
+            return dq, dk, dv, None, None, None, None, None, None
         q, k_int, v, leaf, weights, bp = ctx.saved_tensors
         B, S, H, D = q.shape
         dq = torch.empty_like(q)
@@ -100,8 +102,8 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
                      weights, bp, ctx.num_samples, max_logit=ctx.max_logit, dq=dq.transpose(0, 1),
                      dk=dk_int, dv=dv.transpose(0, 1))
         dk = torch.empty_like(q)
-        ops.tree_build_backward(dk_int, dk.transpose(0, 1))
-        return dq, dk, dv, None, None, None, None, None
+        ops.tree_build_backward(dk_int, dk.transpose(0, 1), ctx.node_layout)
+        return dq, dk, dv, None, None, None, None, None, None
 
 
 def _causal_fwd(q, k_int, v, num_samples, out):
@@ -251,7 +253,8 @@ def resolve_num_samples() -> int | None:
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                    softmax_scale: float | None = None, *, num_samples: int | None = None,
                    max_logit: float = ops.MAX_LOGIT,
-                   gumbels: torch.Tensor | None = None, shard=None) -> torch.Tensor:
+                   gumbels: torch.Tensor | None = None, shard=None,
+                   node_layout: str = "reference", scale_logits: bool = False) -> torch.Tensor:
     """attn-bench kernel contract: bshd q/k/v (B,S,H,D) -> out (B,S,H,D).
 
     ``k`` are leaf keys; the internal-node keys are their sequence-axis Haar transform in
@@ -263,8 +266,12 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     for replaying a recorded draw. ``shard`` (``sharding.ShardSpec``, non-causal only) marks
     q/k/v as this rank's (batch, head) block of a larger problem; the result is that block
     of the unsharded call's result.
+
+    Two opt-in departures from the reference's semantics: ``node_layout="tree"`` builds the
+    tree-correct node keys (every heap node summarises its own subtree, ``ops.tree_build``),
+    and ``scale_logits=True`` multiplies every tree logit q . k by ``softmax_scale`` (default
+    1/sqrt(head_dim)) by scaling q, which the reference adapters never do.
     """
-    del softmax_scale
     if shard is not None and causal:
         raise ValueError("causal mode couples all heads of a query and cannot be head/batch sharded")
     if num_samples is None:
@@ -276,6 +283,11 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     B, S, H, D = q.shape
     if not ops.is_power_of_two(S) or S < 2:
         raise ValueError(f"treeattn_b200 requires power-of-two seqlen, got {S}")
+    if node_layout not in ops.LAYOUTS:
+        raise ValueError(f"node_layout must be 'reference' or 'tree', got {node_layout!r}")
+    if scale_logits:
+        scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+        q = q * scale
     q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
     return TreeAttentionBshdFunction.apply(q, k, v, num_samples, max_logit, gumbels, bool(causal),
-                                           shard)
+                                           shard, node_layout)

@@ -57,6 +57,40 @@ def adapter():
     )
 
 
+# Tree-aware accounting. attn-bench's flops.py counts dense attention (4 b h s^2 d forward,
+# attn_bench/flops.py:19-27), which overstates a sampled tree by orders of magnitude. Per
+# (query, head), stochastic tree attention does num_samples root-to-leaf walks of log2(N)
+# node dot products (2 d FLOPs each) plus a num_samples-row weighted value sum (2 d each).
+
+def _log2(n: int) -> int:
+    return max(int(n).bit_length() - 1, 0)
+
+
+def fwd_flops(batch: int, seqlen: int, nheads: int, head_dim: int, causal: bool,
+              num_samples: int = 8) -> float:
+    """Forward FLOPs of stochastic tree attention (causal: the same walk, corrected)."""
+    del causal
+    per_query = num_samples * (_log2(seqlen) + 1) * 2.0 * head_dim
+    return float(batch) * seqlen * nheads * per_query
+
+
+def bwd_flops(batch: int, seqlen: int, nheads: int, head_dim: int, causal: bool,
+              num_samples: int = 8) -> float:
+    """Backward: per path and level dq and dK updates (2 x 2d) plus the node logit replay
+    read from the forward's branch probabilities; per path g = dO . v and the dV update."""
+    del causal
+    per_query = num_samples * (_log2(seqlen) * 4.0 + 4.0) * head_dim
+    return float(batch) * seqlen * nheads * per_query
+
+
+def compulsory_bytes(batch: int, seqlen: int, nheads: int, head_dim: int, elem_bytes: int = 2,
+                     backward: bool = True) -> float:
+    """Unique HBM bytes: read q, k, v and write out (forward); read q, k, v, out, dO and write
+    dq, dk, dv (backward). The roofline denominator for these gather-bound kernels."""
+    unit = float(batch) * seqlen * nheads * head_dim * elem_bytes
+    return unit * (4 + (8 if backward else 0))
+
+
 def is_available() -> bool:
     from . import has_native_kernels
 

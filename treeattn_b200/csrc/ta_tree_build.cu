@@ -38,7 +38,22 @@ struct TreeParams {
   int64_t count;       // entries of the pass input sequence
   int64_t pos_scale;   // global position of input entry c is c * pos_scale
   int32_t write_dst;   // forward: store run averages (0 on the last pass)
+  int32_t tree_layout; // node rows in tree order (TA_LAYOUT_TREE) instead of position order
+  int32_t log_s;       // log2 of the sequence length
 };
+
+// Row of the node that holds the Haar coefficient at position pos >= 1. Reference layout:
+// row pos - 1 (the array attn-bench's build returns, which the samplers read as a heap).
+// Tree layout: the coefficient of level l = ctz(pos) pairs the two halves of the block of
+// 2^(l+1) positions starting at pos - 2^l, i.e. heap node (depth log_s - 1 - l, index
+// pos >> (l + 1)), so every heap node holds (mean(left half) - mean(right half)) / 2 of its
+// own subtree.
+__device__ __forceinline__ int64_t node_row(const TreeParams& p, int64_t pos) {
+  if (!p.tree_layout) return pos - 1;
+  const int l = __ffsll(pos) - 1;
+  const int d = p.log_s - 1 - l;
+  return ((int64_t)1 << d) - 1 + (pos >> (l + 1));
+}
 
 // forward: one run of 2^LV entries
 template <typename T, int LV>
@@ -81,7 +96,7 @@ __global__ void __launch_bounds__(kTreeThreads) haar_fwd_kernel(const TreeParams
       }
       // pair (i - 2^(l+1) + 1, i - 2^l + 1): diff lands on the right block's start
       const int64_t pos = (c0 + i + 1 - (1 << l)) * p.pos_scale;
-      st16(nodes + (pos - 1) * p.ns * (int64_t)sizeof(T), E::pack(diff));
+      st16(nodes + node_row(p, pos) * p.ns * (int64_t)sizeof(T), E::pack(diff));
     }
   }
   if (p.write_dst) {
@@ -132,7 +147,7 @@ __global__ void __launch_bounds__(kTreeThreads) haar_bwd_kernel(const TreeParams
         for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] - dstk[l][e]) * 0.5f;
       } else {  // left child: load the parent's diff at position i + 2^l
         const int64_t pos = (c0 + i + (1 << l)) * p.pos_scale;
-        Elem<float>::unpack(ld16_stream(nodes + (pos - 1) * p.ns * 4), dstk[l]);
+        Elem<float>::unpack(ld16_stream(nodes + node_row(p, pos) * p.ns * 4), dstk[l]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] + dstk[l][e]) * 0.5f;
       }
@@ -214,11 +229,14 @@ extern "C" size_t ta_tree_build_backward_workspace_size(int64_t B, int64_t S, in
   return scratch_bytes(B, S, H, D);
 }
 
-extern "C" int ta_tree_build(int32_t dtype, int64_t B, int64_t S, int64_t H, int64_t D,
-                             const void* k_leaf, ta_layout kl, void* k_int, ta_layout nl,
-                             void* ws, size_t ws_bytes, ta_stream_t stream) {
+extern "C" int ta_tree_build_ex(int32_t dtype, int64_t B, int64_t S, int64_t H, int64_t D,
+                                const void* k_leaf, ta_layout kl, void* k_int, ta_layout nl,
+                                int32_t node_layout, void* ws, size_t ws_bytes,
+                                ta_stream_t stream) {
   int rc = check_tree_args(dtype, B, S, H, D);
   if (rc) return rc;
+  if (node_layout != TA_LAYOUT_REFERENCE && node_layout != TA_LAYOUT_TREE)
+    return fail(TA_ERR_INVALID, "unknown node layout %d", node_layout);
   const int es = dtype_size(dtype);
   if ((rc = check_view("k_leaf", k_leaf, kl, es, false)) ||
       (rc = check_view("k_int", k_int, nl, es, false)))
@@ -233,6 +251,8 @@ extern "C" int ta_tree_build(int32_t dtype, int64_t B, int64_t S, int64_t H, int
   p.src = (const char*)k_leaf; p.ss = kl.seq; p.sb = kl.batch; p.sh = kl.head;
   p.count = S;
   p.pos_scale = 1;
+  p.tree_layout = node_layout == TA_LAYOUT_TREE;
+  p.log_s = floor_log2(S);
   char* scratch = (char*)ws;
   while (true) {
     const int lv = p.count > (1 << kRunLog) ? kRunLog : floor_log2(p.count);
@@ -257,12 +277,21 @@ extern "C" int ta_tree_build(int32_t dtype, int64_t B, int64_t S, int64_t H, int
   return TA_OK;
 }
 
-extern "C" int ta_tree_build_backward(int32_t dtype, int64_t B, int64_t S, int64_t H, int64_t D,
-                                      const float* dk_int, ta_layout nl, void* dk_leaf,
-                                      ta_layout ol, void* ws, size_t ws_bytes,
-                                      ta_stream_t stream) {
+extern "C" int ta_tree_build(int32_t dtype, int64_t B, int64_t S, int64_t H, int64_t D,
+                             const void* k_leaf, ta_layout kl, void* k_int, ta_layout nl,
+                             void* ws, size_t ws_bytes, ta_stream_t stream) {
+  return ta_tree_build_ex(dtype, B, S, H, D, k_leaf, kl, k_int, nl, TA_LAYOUT_REFERENCE, ws,
+                          ws_bytes, stream);
+}
+
+extern "C" int ta_tree_build_backward_ex(int32_t dtype, int64_t B, int64_t S, int64_t H,
+                                         int64_t D, const float* dk_int, ta_layout nl,
+                                         void* dk_leaf, ta_layout ol, int32_t node_layout,
+                                         void* ws, size_t ws_bytes, ta_stream_t stream) {
   int rc = check_tree_args(dtype, B, S, H, D);
   if (rc) return rc;
+  if (node_layout != TA_LAYOUT_REFERENCE && node_layout != TA_LAYOUT_TREE)
+    return fail(TA_ERR_INVALID, "unknown node layout %d", node_layout);
   const int es = dtype_size(dtype);
   if ((rc = check_view("dk_int", dk_int, nl, 4, false)) ||
       (rc = check_view("dk_leaf", dk_leaf, ol, es, false)))
@@ -302,6 +331,8 @@ extern "C" int ta_tree_build_backward(int32_t dtype, int64_t B, int64_t S, int64
     p.nodes = (char*)dk_int; p.ns = nl.seq; p.nb = nl.batch; p.nh = nl.head;
     p.count = counts[j];
     p.pos_scale = scales[j];
+    p.tree_layout = node_layout == TA_LAYOUT_TREE;
+    p.log_s = floor_log2(S);
     // gradients of this pass's run averages: produced by pass j+1 (none on the top pass)
     if (j + 1 < np) {
       const int64_t n = counts[j + 1];
@@ -324,4 +355,12 @@ extern "C" int ta_tree_build_backward(int32_t dtype, int64_t B, int64_t S, int64
     if ((rc = check_launch("tree build backward"))) return rc;
   }
   return TA_OK;
+}
+
+extern "C" int ta_tree_build_backward(int32_t dtype, int64_t B, int64_t S, int64_t H, int64_t D,
+                                      const float* dk_int, ta_layout nl, void* dk_leaf,
+                                      ta_layout ol, void* ws, size_t ws_bytes,
+                                      ta_stream_t stream) {
+  return ta_tree_build_backward_ex(dtype, B, S, H, D, dk_int, nl, dk_leaf, ol,
+                                   TA_LAYOUT_REFERENCE, ws, ws_bytes, stream);
 }

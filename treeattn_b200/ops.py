@@ -172,11 +172,24 @@ def branch_prob_stride(num_leaves: int) -> int:
 # tree build
 # ---------------------------------------------------------------------------------------
 
-def tree_build(k_lbhd: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+LAYOUTS = {"reference": L.TA_LAYOUT_REFERENCE, "tree": L.TA_LAYOUT_TREE}
+
+
+def _layout_code(node_layout: str) -> int:
+    try:
+        return LAYOUTS[node_layout]
+    except KeyError:
+        raise ValueError(f"node layout must be 'reference' or 'tree', got {node_layout!r}") from None
+
+
+def tree_build(k_lbhd: torch.Tensor, out: torch.Tensor | None = None,
+               node_layout: str = "reference") -> torch.Tensor:
     """Internal-node keys (S-1, B, H, D) from leaf keys (S, B, H, D) (Haar, input dtype).
 
     The result is allocated head-major, memory (B, H, S-1, D), and returned as a logical
-    (S-1, B, H, D) view: each head's tree is one contiguous block.
+    (S-1, B, H, D) view: each head's tree is one contiguous block. ``node_layout`` "reference"
+    reproduces attn-bench's array (position order, read as a heap by the samplers); "tree"
+    puts every coefficient on the heap node of the subtree it summarises.
     """
     _require_cuda(k_lbhd)
     S, B, H, D = k_lbhd.shape
@@ -188,13 +201,14 @@ def tree_build(k_lbhd: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
     lib = L.load()
     ws_bytes = lib.ta_tree_build_workspace_size(B, S, H, D, dt)
     ws = torch.empty(max(ws_bytes, 1), device=k_lbhd.device, dtype=torch.uint8)
-    L.call("ta_tree_build", dt, B, S, H, D, _ptr(k_lbhd), layout(k_lbhd), _ptr(out), layout(out),
-           _ptr(ws), ws_bytes, _stream(k_lbhd.device))
+    L.call("ta_tree_build_ex", dt, B, S, H, D, _ptr(k_lbhd), layout(k_lbhd), _ptr(out), layout(out),
+           _layout_code(node_layout), _ptr(ws), ws_bytes, _stream(k_lbhd.device))
     _note("tree_build")
     return out
 
 
-def tree_build_backward(dk_int: torch.Tensor, dk_leaf: torch.Tensor) -> torch.Tensor:
+def tree_build_backward(dk_int: torch.Tensor, dk_leaf: torch.Tensor,
+                        node_layout: str = "reference") -> torch.Tensor:
     """dk_leaf (S, B, H, D view, any float dtype) <- transpose of the Haar build of float32 dk_int."""
     _require_cuda(dk_int, dk_leaf)
     if dk_int.dtype != torch.float32:
@@ -203,9 +217,9 @@ def tree_build_backward(dk_int: torch.Tensor, dk_leaf: torch.Tensor) -> torch.Te
     lib = L.load()
     ws_bytes = lib.ta_tree_build_backward_workspace_size(B, S, H, D)
     ws = torch.empty(max(ws_bytes, 1), device=dk_int.device, dtype=torch.uint8)
-    L.call("ta_tree_build_backward", dtype_code(dk_leaf.dtype), B, S, H, D, _ptr(dk_int),
-           layout(dk_int), _ptr(dk_leaf), layout(dk_leaf), _ptr(ws), ws_bytes,
-           _stream(dk_int.device))
+    L.call("ta_tree_build_backward_ex", dtype_code(dk_leaf.dtype), B, S, H, D, _ptr(dk_int),
+           layout(dk_int), _ptr(dk_leaf), layout(dk_leaf), _layout_code(node_layout), _ptr(ws),
+           ws_bytes, _stream(dk_int.device))
     _note("tree_build_backward")
     return dk_leaf
 
