@@ -329,6 +329,49 @@ int ta_exact_backward(const ta_shape* shape, int32_t causal, int64_t query_offse
                       ta_layout dk_layout, float* dv, ta_layout dv_layout, int32_t accumulate,
                       void* workspace, size_t workspace_bytes, ta_stream_t stream);
 
+/* ---- generalised tree: fanout f, leaf blocks of Lb keys -------------------------------- */
+
+/*
+ * No counterpart in the reference (its tree is binary with one key per leaf); BASELINE's
+ * configurations name a fanout and a leaf block. N = leaf_block * fanout^Dp keys; node
+ * (d, j) summarises the keys of blocks [j f^(Dp-d), (j+1) f^(Dp-d)) as mean / 2 (float32,
+ * levels 1..Dp, ta_blocked_summary_rows rows per head, [B*H][rows][D]). Each of the S paths of
+ * a query draws one child per level by Gumbel-max over log_softmax(q . c_children) (causal:
+ * children starting beyond the query's bottom-right-aligned boundary row0 + l + N - row_total
+ * masked), then attends softmax(softmax_scale q . K_blk^T) V_blk over its leaf block (causal:
+ * keys beyond the boundary masked); out = sum_s softmax_s(path log-prob) o_s. At fanout 2,
+ * leaf block 1 this is the reference sampler on the TA_LAYOUT_TREE node keys.
+ * Noise: philox keyed by the GLOBAL (batch, head, query) of the (row/batch/head)_total problem,
+ * element offset + (level * S + s) * f + child, so shards draw exactly what the full call draws;
+ * a call consumes Dp * S * f offsets (rounded up to 4). `gumbels` (Dp, L, B, H, S, f) replaces
+ * it. The backward is deterministic (sorted per leaf block, no float atomics).
+ */
+typedef struct ta_blocked {
+  int32_t fanout;      /* power of two, 2 .. 16 */
+  int32_t leaf_block;  /* power of two, 1 .. 256 */
+  int32_t causal;
+  float softmax_scale; /* leaf-block attention scale (> 0) */
+  int64_t row0, row_total, batch0, batch_total, head0, head_total; /* this call's block */
+} ta_blocked;
+int64_t ta_blocked_summary_rows(int64_t num_leaves, int32_t fanout, int32_t leaf_block);
+int ta_blocked_build(const ta_shape* shape, const ta_blocked* cfg, const void* k,
+                     ta_layout k_layout, float* summaries, ta_stream_t stream);
+int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const ta_rng* rng,
+                           float* out, ta_stream_t stream);
+int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
+                       ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,
+                       ta_layout v_layout, const float* summaries, void* out,
+                       ta_layout out_layout, const ta_rng* rng, const float* gumbels,
+                       int32_t* block, float* weights, ta_stream_t stream);
+size_t ta_blocked_backward_workspace_size(const ta_shape* shape, const ta_blocked* cfg);
+int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
+                        ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,
+                        ta_layout v_layout, const float* summaries, const void* grad_out,
+                        ta_layout grad_out_layout, const int32_t* block, const float* weights,
+                        void* dq, ta_layout dq_layout, void* dk, ta_layout dk_layout, void* dv,
+                        ta_layout dv_layout, void* workspace, size_t workspace_bytes,
+                        ta_stream_t stream);
+
 /* ---- reference-granularity entry points (treeattn_cuda.cpp:479-488) ---------------- */
 
 /*

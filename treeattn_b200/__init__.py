@@ -13,6 +13,7 @@ Public API (drop-in for the TreeAttention reference's hot path):
 """
 
 from . import ops, sharding
+from .blocked import blocked_tree_attention
 from .autograd import (
     CausalTreeAttentionFunction,
     ExactTreeAttentionFunction,
@@ -39,6 +40,7 @@ def has_native_kernels() -> bool:
 __all__ = [
     "hierarchical_attention",
     "tree_attention",
+    "blocked_tree_attention",
     "TreeAttentionFunction",
     "CausalTreeAttentionFunction",
     "ExactTreeAttentionFunction",

@@ -37,6 +37,14 @@ class Shard(ctypes.Structure):
                 ("head0", ctypes.c_int64), ("head_count", ctypes.c_int64)]
 
 
+class Blocked(ctypes.Structure):
+    _fields_ = [("fanout", ctypes.c_int32), ("leaf_block", ctypes.c_int32),
+                ("causal", ctypes.c_int32), ("softmax_scale", ctypes.c_float),
+                ("row0", ctypes.c_int64), ("row_total", ctypes.c_int64),
+                ("batch0", ctypes.c_int64), ("batch_total", ctypes.c_int64),
+                ("head0", ctypes.c_int64), ("head_total", ctypes.c_int64)]
+
+
 class Shape(ctypes.Structure):
     _fields_ = [
         ("batch", ctypes.c_int64),
@@ -85,6 +93,16 @@ SIGNATURES = {
     "ta_branch_prob_stride": (_I32, [_I64]),
     "ta_gumbel_fill_shard": (ctypes.c_int, [_P, ctypes.POINTER(Rng), ctypes.POINTER(Shard), _I64,
                                             _I32, _I32, _P]),
+    "ta_blocked_summary_rows": (ctypes.c_int64, [_I64, _I32, _I32]),
+    "ta_blocked_build": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _P]),
+    "ta_blocked_gumbel_fill": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked),
+                                              ctypes.POINTER(Rng), _P, _P]),
+    "ta_blocked_forward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,
+                                          _P, _L, _P, _P, _L, ctypes.POINTER(Rng), _P, _P, _P, _P]),
+    "ta_blocked_backward_workspace_size": (_SZ, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked)]),
+    "ta_blocked_backward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,
+                                           _P, _L, _P, _P, _L, _P, _P, _P, _L, _P, _L, _P, _L, _P,
+                                           _SZ, _P]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),
