@@ -53,9 +53,15 @@ def parse_args():
     p.add_argument("--batch", type=int, default=WORKLOAD["batch_per_gpu"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--mode", choices=["shard", "sp"], default="shard",
+    p.add_argument("--fanout", type=int, default=2)
+    p.add_argument("--leaf-block", type=int, default=64)
+    p.add_argument("--causal", action="store_true")
+    p.add_argument("--dtype", choices=["bf16", "f16"], default="bf16")
+    p.add_argument("--mode", choices=["shard", "sp", "blocked"], default="shard",
                    help="shard: (batch, head)-sharded headline workload; sp: sequence-parallel "
-                        "causal long context (B=1, S=65536, H=32, d=128, 16 paths unless overridden)")
+                        "causal long context (B=1, S=65536, H=32, d=128, 16 paths unless overridden); "
+                        "blocked: generalised fanout / leaf-block tree (B=4, S=4096, H=16, d=128, "
+                        "fanout 2, leaf block 64, 8 paths: BASELINE's single-B200 config)")
     return p.parse_args()
 
 
@@ -475,6 +481,94 @@ def run_sp(args):
         dist.destroy_process_group()
 
 
+def run_blocked(args):
+    """Generalised tree (fanout, leaf block), one GPU or (batch, head)-sharded ranks."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from treeattn_b200 import ops
+    from treeattn_b200.blocked import blocked_tree_attention
+    from treeattn_b200.sharding import shard_for_rank
+
+    S = args.seq_len if args.seq_len != WORKLOAD["seq_len"] else 4096
+    B = args.batch if args.batch != WORKLOAD["batch_per_gpu"] else 4
+    H, D, P = args.heads, args.head_dim, args.num_samples
+    f, Lb = args.fanout, args.leaf_block
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    sd = 1.0 if dt == torch.bfloat16 else 0.5
+    gen = torch.Generator(device=dev).manual_seed(1000 * rank)
+    q, k, v, go = (torch.randn(B, S, H, D, device=dev, generator=gen).mul(sd).to(dt) for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    shard = shard_for_rank(world * B, H, rank, world, "batch") if world > 1 else None
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        torch.manual_seed(0)
+        out = blocked_tree_attention(q, k, v, args.causal, None, num_samples=P, fanout=f,
+                                     leaf_block=Lb, shard=shard)
+        out.backward(go)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(dev.index)
+    ops.profile_enable(True)
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    ms_step = ms / args.steps
+    if rank == 0:
+        # leaf-block attention FLOPs (QK^T and PV per sampled path; backward 2.5x)
+        leaf_flops = B * S * H * P * Lb * D * 4.0 * 3.5
+        total = sum(t for _, t in prof.values()) or 1.0
+        line = {"metric": "generalised tree attention fwd+bwd tokens/s (fanout, leaf block)",
+                "value": world * B * S / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
+                "data": "synthetic N(0,1) (fp16: N(0,0.5)) q/k/v/grad_out, seeded CUDA generator",
+                "config": {"workload": "stochastic tree attention, generalised tree", "batch_per_gpu": B,
+                           "seq_len": S, "heads": H, "head_dim": D, "num_samples": P, "fanout": f,
+                           "leaf_block": Lb, "causal": args.causal},
+                "leaf_block_tflops": leaf_flops / (ms_step / 1e3) / 1e12,
+                "gpu_launches": int(sum(c for c, _ in prof.values())),
+                "kernels": {k_: {"launches_per_step": c / args.steps, "ms_per_step": t / args.steps,
+                                 "share": t / total} for k_, (c, t) in
+                            sorted(prof.items(), key=lambda x: -x[1][1])},
+                "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     sys.path.insert(0, ROOT)
@@ -482,6 +576,8 @@ def main():
         run_reference(args)
     elif args.mode == "sp":
         run_sp(args)
+    elif args.mode == "blocked":
+        run_blocked(args)
     else:
         run_ours(args)
 

@@ -358,19 +358,30 @@ int ta_blocked_build(const ta_shape* shape, const ta_blocked* cfg, const void* k
                      ta_layout k_layout, float* summaries, ta_stream_t stream);
 int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const ta_rng* rng,
                            float* out, ta_stream_t stream);
+/*
+ * Leaf-block attention on the tensor cores (16-bit inputs, head_dim 64 or 128, leaf block 16..128;
+ * the backward also needs leaf_block >= 32 and leaf_block * head_dim <= 8192): the forward then
+ * takes `path_out` (float32 [B*H][L*S][D], w_s * o_s per path, kept for the backward) and a
+ * workspace of ta_blocked_forward_workspace_size bytes; with path_out NULL (or for other shapes)
+ * everything runs on the CUDA cores. ta_blocked_uses_tensor_cores tells which.
+ */
+int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
+                                     int32_t backward);
+size_t ta_blocked_forward_workspace_size(const ta_shape* shape, const ta_blocked* cfg);
 int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
                        ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,
                        ta_layout v_layout, const float* summaries, void* out,
                        ta_layout out_layout, const ta_rng* rng, const float* gumbels,
-                       int32_t* block, float* weights, ta_stream_t stream);
+                       int32_t* block, float* weights, float* path_out, void* workspace,
+                       size_t workspace_bytes, ta_stream_t stream);
 size_t ta_blocked_backward_workspace_size(const ta_shape* shape, const ta_blocked* cfg);
 int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
                         ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,
                         ta_layout v_layout, const float* summaries, const void* grad_out,
                         ta_layout grad_out_layout, const int32_t* block, const float* weights,
-                        void* dq, ta_layout dq_layout, void* dk, ta_layout dk_layout, void* dv,
-                        ta_layout dv_layout, void* workspace, size_t workspace_bytes,
-                        ta_stream_t stream);
+                        const float* path_out, void* dq, ta_layout dq_layout, void* dk,
+                        ta_layout dk_layout, void* dv, ta_layout dv_layout, void* workspace,
+                        size_t workspace_bytes, ta_stream_t stream);
 
 /* ---- reference-granularity entry points (treeattn_cuda.cpp:479-488) ---------------- */
 

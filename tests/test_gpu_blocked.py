@@ -56,8 +56,17 @@ def test_forward_backward_against_oracle(case, causal):
 
 
 @pytest.mark.parametrize("dtype,tol", [("bf16", 2e-2), ("f16", 5e-3)])
-def test_low_precision_within_tolerance(dtype, tol):
-    B, N, H, D, S, f, Lb = 2, 1024, 2, 128, 8, 4, 64
+@pytest.mark.parametrize("N,D,f,Lb", [
+    (1024, 128, 4, 64),    # tensor-core forward and backward
+    (512, 64, 2, 16),      # tensor-core forward, CUDA-core backward (leaf block 16)
+    (2048, 128, 2, 32),
+    (1024, 64, 2, 64),
+    (2048, 64, 4, 128),
+    (2048, 128, 2, 128),   # tensor-core forward, CUDA-core backward (Lb * D > 8192)
+    (256, 96, 2, 32),      # head_dim 96: CUDA cores throughout
+])
+def test_low_precision_within_tolerance(dtype, tol, N, D, f, Lb):
+    B, H, S = 2, 2, 8
     q, k, v, go = _inputs(B, N, H, D, dtype, 3)
     if dtype == "f16":
         q, k, v, go = (t * 0.5 for t in (q, k, v, go))

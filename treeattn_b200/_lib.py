@@ -97,12 +97,15 @@ SIGNATURES = {
     "ta_blocked_build": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _P]),
     "ta_blocked_gumbel_fill": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked),
                                               ctypes.POINTER(Rng), _P, _P]),
+    "ta_blocked_uses_tensor_cores": (_I32, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _I32]),
+    "ta_blocked_forward_workspace_size": (_SZ, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked)]),
     "ta_blocked_forward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,
-                                          _P, _L, _P, _P, _L, ctypes.POINTER(Rng), _P, _P, _P, _P]),
+                                          _P, _L, _P, _P, _L, ctypes.POINTER(Rng), _P, _P, _P, _P, _P,
+                                          _SZ, _P]),
     "ta_blocked_backward_workspace_size": (_SZ, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked)]),
     "ta_blocked_backward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,
-                                           _P, _L, _P, _P, _L, _P, _P, _P, _L, _P, _L, _P, _L, _P,
-                                           _SZ, _P]),
+                                           _P, _L, _P, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _L,
+                                           _P, _SZ, _P]),
     "ta_tree_build_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "ta_tree_build": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P, _SZ, _P]),
     "ta_tree_build_noalloc": (ctypes.c_int, [_I32, _I64, _I64, _I64, _I64, _P, _L, _P, _L, _P]),

@@ -91,6 +91,12 @@ class BlockedTreeAttentionFunction(torch.autograd.Function):
         out = torch.empty_like(q)
         blk = torch.empty((Lq, B, H, num_samples), device=q.device, dtype=torch.int32)
         w = torch.empty((Lq, B, H, num_samples), device=q.device, dtype=torch.float32)
+        lib = L.load()
+        path_out, ws = None, None
+        if lib.ta_blocked_uses_tensor_cores(ctypes.byref(shape), ctypes.byref(cfg), 0):
+            path_out = torch.empty((B * H, Lq * num_samples, D), device=q.device, dtype=torch.float32)
+            ws_bytes = lib.ta_blocked_forward_workspace_size(ctypes.byref(shape), ctypes.byref(cfg))
+            ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
         rng_p, g_p = None, None
         if gumbels is not None:
             gumbels = gumbels.to(device=q.device, dtype=torch.float32).contiguous()
@@ -101,15 +107,16 @@ class BlockedTreeAttentionFunction(torch.autograd.Function):
         L.call("ta_blocked_forward", ctypes.byref(shape), ctypes.byref(cfg), ops._ptr(qv),
                ops.layout(qv), ops._ptr(kv), ops.layout(kv), ops._ptr(vv), ops.layout(vv),
                ops._ptr(summ), ops._ptr(out), ops.layout(out.transpose(0, 1)), rng_p, g_p,
-               ops._ptr(blk), ops._ptr(w), ops._stream(q.device))
-        ctx.save_for_backward(q, k, v, summ, blk, w)
+               ops._ptr(blk), ops._ptr(w), ops._ptr(path_out), ops._ptr(ws),
+               ws.numel() if ws is not None else 0, ops._stream(q.device))
+        ctx.save_for_backward(q, k, v, summ, blk, w, path_out)
         ctx.cfg, ctx.shape = cfg, shape
         ctx.mark_non_differentiable(blk, w)
         return out, blk, w
 
     @staticmethod
     def backward(ctx, grad_out, _gb, _gw):
-        q, k, v, summ, blk, w = ctx.saved_tensors
+        q, k, v, summ, blk, w, path_out = ctx.saved_tensors
         cfg, shape = ctx.cfg, ctx.shape
         grad_out = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -122,7 +129,8 @@ class BlockedTreeAttentionFunction(torch.autograd.Function):
         L.call("ta_blocked_backward", ctypes.byref(shape), ctypes.byref(cfg), ops._ptr(t(q)),
                ops.layout(t(q)), ops._ptr(t(k)), ops.layout(t(k)), ops._ptr(t(v)), ops.layout(t(v)),
                ops._ptr(summ), ops._ptr(t(grad_out)), ops.layout(t(grad_out)), ops._ptr(blk),
-               ops._ptr(w), ops._ptr(t(dq)), ops.layout(t(dq)), ops._ptr(t(dk)), ops.layout(t(dk)),
+               ops._ptr(w), ops._ptr(path_out), ops._ptr(t(dq)), ops.layout(t(dq)), ops._ptr(t(dk)),
+               ops.layout(t(dk)),
                ops._ptr(t(dv)), ops.layout(t(dv)), ops._ptr(ws), ws_bytes, ops._stream(q.device))
         return dq, dk, dv, None, None, None, None, None, None, None, None
 

@@ -1,0 +1,6 @@
+// Instantiations of the generalised-tree launchers for f32 inputs, fanout 2.
+#include "ta_blocked_impl.cuh"
+
+namespace ta {
+TA_BLK_EPLS(TA_BLK_INSTANTIATE, float, 2)
+}  // namespace ta
