@@ -53,6 +53,7 @@ def parse_args():
     p.add_argument("--batch", type=int, default=WORKLOAD["batch_per_gpu"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-fa2", action="store_true")
     p.add_argument("--fanout", type=int, default=2)
     p.add_argument("--leaf-block", type=int, default=64)
     p.add_argument("--causal", action="store_true")
@@ -300,11 +301,44 @@ def run_ours(args):
         "clocks": clk,
         "e2e": e2e,
     }
+    if world == 1 and not args.no_fa2:
+        line["fa2"] = fa2_reference(q.detach(), k.detach(), v.detach(), go, args)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference(args, budget_s=20.0)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def fa2_reference(q, k, v, go, args):
+    """Dense FlashAttention-2 (flash_attn library, the metric's comparator) fwd+bwd on the
+    same bshd tensors and GPU: tokens/s, CUDA events, same warm-up / step counts."""
+    import torch
+    try:
+        from flash_attn import flash_attn_func
+    except Exception as exc:  # noqa: BLE001 - a comparator only
+        return {"unavailable": f"flash_attn not importable: {exc}"}
+    qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+
+    def step():
+        for t in (qq, kk, vv):
+            t.grad = None
+        flash_attn_func(qq, kk, vv, causal=False).backward(go)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    B, S = q.shape[0], q.shape[1]
+    return {"value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "what": "flash_attn_func dense attention fwd+bwd, same bshd bf16 q/k/v/grad_out, "
+                    "non-causal (library comparator, not this package's path)"}
 
 
 # ---------------------------------------------------------------------------------------
