@@ -110,6 +110,25 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
   const uint32_t jq = (uint32_t)(b * p.H + h) * (uint32_t)p.S;
   const uint32_t Jq = (uint32_t)(p.B * p.H * p.S);
 
+  // Gumbel pair of path s (of this query) at `depth`; its address depends on no decision, so
+  // the walk fetches it one level ahead and its latency overlaps the row gather.
+  auto noise = [&](int s, int depth) -> float2 {
+    if (causal) {
+      const uint32_t jl = jq + (uint32_t)s;
+      if (p.gumbels != nullptr)
+        return *reinterpret_cast<const float2*>(p.gumbels + (((uint64_t)l * p.log_n + depth) * Jq + jl) * 2u);
+      const uint64_t off = p.offset + ((uint64_t)l * p.log_n + depth) * p.offset_step;
+      return make_float2(torch_gumbel(p.seed, off, 2u * jl, p.stride),
+                         torch_gumbel(p.seed, off, 2u * jl + 1u, p.stride));
+    }
+    const uint32_t jm_ = j0 + (uint32_t)s;
+    if (p.gumbels != nullptr)
+      return *reinterpret_cast<const float2*>(p.gumbels + (uint64_t)depth * M + 2u * jm_);
+    const uint64_t off = p.offset + (uint64_t)depth * p.offset_step;
+    return make_float2(torch_gumbel(p.seed, off, 2u * jm_, p.stride),
+                       torch_gumbel(p.seed, off, 2u * jm_ + 1u, p.stride));
+  };
+
   for (int s0 = 0; s0 < p.S; s0 += 4) {
     const int ns = min(4, p.S - s0);
     uint32_t node[4] = {0u, 0u, 0u, 0u};
@@ -128,7 +147,11 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
         }
       }
     }
+    const bool draws = !replay && t4 < ns;
+    float2 g_next = draws && d0 < p.log_n ? noise(s0 + t4, d0) : make_float2(0.0f, 0.0f);
     for (int depth = d0; depth < p.log_n; ++depth) {
+      const float2 g_cur = g_next;
+      if (draws && depth + 1 < p.log_n) g_next = noise(s0 + t4, depth + 1);
       uint4 raw[4][CPL];
       if (depth < p.top_levels) {
 #pragma unroll
@@ -172,28 +195,7 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
           const uint8_t byte = p.packed[(int64_t)jm * p.pbytes + (depth >> 3)];
           dir = (byte >> (depth & 7)) & 1;
         } else {
-          float gl, gr;
-          if (causal) {
-            const uint32_t jl = jq + (uint32_t)(s0 + t4);
-            if (p.gumbels != nullptr) {
-              const float2 gg = *reinterpret_cast<const float2*>(
-                  p.gumbels + (((uint64_t)l * p.log_n + depth) * Jq + jl) * 2u);
-              gl = gg.x;
-              gr = gg.y;
-            } else {
-              const uint64_t off = p.offset + ((uint64_t)l * p.log_n + depth) * p.offset_step;
-              gl = torch_gumbel(p.seed, off, 2u * jl, p.stride);
-              gr = torch_gumbel(p.seed, off, 2u * jl + 1u, p.stride);
-            }
-          } else if (p.gumbels != nullptr) {
-            const float2 gg = *reinterpret_cast<const float2*>(p.gumbels + (uint64_t)depth * M + 2u * jm);
-            gl = gg.x;
-            gr = gg.y;
-          } else {
-            const uint64_t off = p.offset + (uint64_t)depth * p.offset_step;
-            gl = torch_gumbel(p.seed, off, 2u * jm, p.stride);
-            gr = torch_gumbel(p.seed, off, 2u * jm + 1u, p.stride);
-          }
+          const float gl = g_cur.x, gr = g_cur.y;
           dir = (lpr + gr > lpl + gl) ? 1 : 0;
         }
         lp += dir ? lpr : lpl;
