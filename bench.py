@@ -218,32 +218,56 @@ def run_ours(args):
     tokens_step = world * B * S
     value = tokens_step / (ms_step / 1e3)
 
-    # end to end through the public API with host buffers: H2D inputs, D2H output + grads
+    # end to end through the public API with host buffers: every step uploads its inputs from
+    # pinned host memory and downloads its output and gradients. Uploads run on a copy-in
+    # stream into two alternating device buffers, downloads on a copy-out stream, so step i+1's
+    # upload and step i-1's download overlap step i's kernels; the events bracket all of it.
     e2e = None
     if not args.no_e2e:
         hq, hk, hv, hgo = (t.detach().cpu().pin_memory() for t in (q, k, v, go))
         hout, hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(4))
+        bufs = [[torch.empty_like(t) for t in (q, k, v, go)] for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        free = [None, None]  # event: compute done with buffer i
 
-        def step_e2e():
-            dq_ = hq.to(dev, non_blocking=True).requires_grad_(True)
-            dk_ = hk.to(dev, non_blocking=True).requires_grad_(True)
-            dv_ = hv.to(dev, non_blocking=True).requires_grad_(True)
-            g_ = hgo.to(dev, non_blocking=True)
+        def step_e2e(i):
+            buf = bufs[i % 2]
+            with torch.cuda.stream(s_in):
+                if free[i % 2] is not None:
+                    s_in.wait_event(free[i % 2])
+                for dst, src in zip(buf, (hq, hk, hv, hgo)):
+                    dst.copy_(src, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            stream.wait_event(ready)
+            dq_, dk_, dv_ = (t.detach().requires_grad_(True) for t in buf[:3])
             out = ta.tree_attention(dq_, dk_, dv_, False, None, num_samples=P, shard=shard)
-            out.backward(g_)
-            hout.copy_(out.detach(), non_blocking=True)
-            hdq.copy_(dq_.grad, non_blocking=True)
-            hdk.copy_(dk_.grad, non_blocking=True)
-            hdv.copy_(dv_.grad, non_blocking=True)
+            out.backward(buf[3])
+            done = torch.cuda.Event()
+            done.record(stream)
+            free[i % 2] = done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for dst, src in ((hout, out), (hdq, dq_.grad), (hdk, dk_.grad), (hdv, dv_.grad)):
+                    src.record_stream(s_out)
+                    dst.copy_(src.detach(), non_blocking=True)
 
-        for _ in range(max(1, args.warmup)):
-            step_e2e()
+        def drain():
+            fin = torch.cuda.Event()
+            fin.record(s_out)
+            stream.wait_event(fin)
+
+        for i in range(max(1, args.warmup)):
+            step_e2e(i)
+        drain()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            step_e2e()
+        s_in.wait_event(e0)
+        for i in range(args.steps):
+            step_e2e(i)
+        drain()
         e1.record(stream)
         barrier()
         ems = e0.elapsed_time(e1)
