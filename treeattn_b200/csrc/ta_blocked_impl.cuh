@@ -3,6 +3,8 @@
 // ta_blocked_<dtype>_f<fanout>.cu, which split the compile across processes.
 #pragma once
 
+#include <type_traits>
+
 // Generalised tree attention: fanout f, leaf blocks of Lb keys (sm_100a).
 //
 // No counterpart in the reference (its tree is binary with one key per leaf); at f = 2,
@@ -704,6 +706,183 @@ __global__ void __launch_bounds__(256) blk_bwd_key_kernel(const BlkParams p) {
   reinterpret_cast<T*>(p.dk)[key * p.dks + (int64_t)b * p.dkb + (int64_t)h * p.dkh + c] = static_cast<T>(acc);
 }
 
+// ---------------------------------------------------------------------------------------
+// table-lookup walk (tensor-core path): Z = Q_tile C^T for every summary row at once
+// ---------------------------------------------------------------------------------------
+constexpr int kWalkQ = 32;         // queries per CTA
+constexpr int kWalkChunk = 128;    // summary rows per product chunk
+constexpr int kWalkMaxRows = 1024; // summary rows the table holds (levels 1..Dp)
+
+__host__ __device__ inline int walk_rows_pad(int64_t R) { return (int)((R + kWalkChunk - 1) / kWalkChunk) * kWalkChunk; }
+__host__ __device__ inline size_t walk_smem(int64_t R, int D, int S) {
+  return (size_t)kWalkQ * (walk_rows_pad(R) + 4) * 4    // Z table
+         + (size_t)2 * kWalkChunk * (D + 8) * 2          // C chunk, bf16 high and low parts
+         + (size_t)kWalkQ * (D + 8) * 2                  // Q tile
+         + (size_t)kWalkQ * S * 4;                       // path log-probabilities
+}
+
+// The F Gumbels of (level d, path s): the same elements blk_gumbel draws, one philox per
+// 4-vector they share.
+template <int F>
+__device__ __forceinline__ void blk_gumbels_of(const BlkParams& p, int b, int h, int l, int d, int s, float* g) {
+  if (p.gumbels != nullptr) {
+    const float* src = p.gumbels + ((((int64_t)d * p.L + l) * p.B + b) * p.H + h) * (int64_t)p.S * F +
+                       (int64_t)s * F;
+#pragma unroll
+    for (int i = 0; i < F; ++i) g[i] = src[i];
+    return;
+  }
+  const uint64_t sub = ((uint64_t)(p.batch0 + b) * p.head_total + (uint64_t)(p.head0 + h)) *
+                           (uint64_t)p.row_total + (uint64_t)(p.row0 + l);
+  const uint64_t e0 = ((uint64_t)d * p.S + (uint64_t)s) * F;
+  float4 u4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  uint64_t vec = ~0ull;
+#pragma unroll
+  for (int i = 0; i < F; ++i) {
+    const uint64_t e = e0 + i;
+    if ((e >> 2) != vec) {
+      vec = e >> 2;
+      curandStatePhilox4_32_10_t st;
+      curand_init(p.seed, sub, p.offset + 4ull * vec, &st);
+      u4 = _curand_uniform4(st.output);
+    }
+    const uint32_t c = (uint32_t)(e & 3);
+    g[i] = gumbel_from_uniform(c == 0 ? u4.x : c == 1 ? u4.y : c == 2 ? u4.z : u4.w);
+  }
+}
+
+template <typename T, int D, int F>
+__global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
+  constexpr int LD = D + 8;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int RP = walk_rows_pad(p.R);
+  const int ZS = RP + 4;
+  float* s_z = reinterpret_cast<float*>(smraw);                       // [kWalkQ][ZS]
+  uint16_t* s_chi = reinterpret_cast<uint16_t*>(s_z + kWalkQ * ZS);   // [kWalkChunk][LD]
+  uint16_t* s_clo = s_chi + kWalkChunk * LD;
+  uint16_t* s_q = s_clo + kWalkChunk * LD;                            // [kWalkQ][LD]
+  float* s_lp = reinterpret_cast<float*>(s_q + kWalkQ * LD);          // [kWalkQ][S]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lt = (p.L + kWalkQ - 1) / kWalkQ;
+  const int bh = blockIdx.x / lt;
+  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  constexpr int CPR = D * 2 / 16;
+  for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i - r * CPR;
+    if (l0 + r < p.L)
+      cp_async16(s_q + r * LD + c * 8, p.q + ((int64_t)(l0 + r) * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2 + c * 16);
+    else
+      *reinterpret_cast<uint4*>(s_q + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
+  }
+  cp_async_commit();
+  const float* csrc = p.summ + (int64_t)bh * p.R * D;
+  const int m0 = (warp & 1) * 16, nb0 = (warp >> 1) * 32;  // warp: 16 queries x 32 rows of a chunk
+  for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
+    __syncthreads();  // the previous chunk's readers are done
+    for (int i = tid; i < kWalkChunk * D / 2; i += blockDim.x) {
+      const int r = i / (D / 2), c = (i - r * (D / 2)) * 2;
+      float2 v = make_float2(0.f, 0.f);
+      if (r0 + r < p.R) v = *reinterpret_cast<const float2*>(csrc + (int64_t)(r0 + r) * D + c);
+      const uint32_t hi = Mma<T>::pack(v.x, v.y);
+      float2 hf;
+      if constexpr (sizeof(T) == 2 && std::is_same<T, __half>::value) {
+        const __half2 hh = *reinterpret_cast<const __half2*>(&hi);
+        hf = __half22float2(hh);
+      } else {
+        hf = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+      }
+      *reinterpret_cast<uint32_t*>(s_chi + r * LD + c) = hi;
+      *reinterpret_cast<uint32_t*>(s_clo + r * LD + c) = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
+    }
+    cp_async_wait_0();
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+#pragma unroll
+    for (int k0 = 0; k0 < D; k0 += 16) {
+      uint32_t a[4];
+      frag_a(a, s_q, LD, m0, k0, lane);
+#pragma unroll
+      for (int t = 0; t < 4; t += 2) {
+        uint32_t bb[4];
+        frag_b_nk(bb, s_chi, LD, nb0 + t * 8, k0, lane);
+        Mma<T>::run(acc[t], a, bb);
+        Mma<T>::run(acc[t + 1], a, bb + 2);
+        frag_b_nk(bb, s_clo, LD, nb0 + t * 8, k0, lane);
+        Mma<T>::run(acc[t], a, bb);
+        Mma<T>::run(acc[t + 1], a, bb + 2);
+      }
+    }
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = r0 + nb0 + t * 8 + tq * 2;
+      *reinterpret_cast<float2*>(s_z + (m0 + g) * ZS + c) = make_float2(acc[t][0], acc[t][1]);
+      *reinterpret_cast<float2*>(s_z + (m0 + g + 8) * ZS + c) = make_float2(acc[t][2], acc[t][3]);
+    }
+  }
+  __syncthreads();
+  // one thread per (query, path): the walk reads its children's logits from the table
+  for (int i = tid; i < kWalkQ * p.S; i += blockDim.x) {
+    const int qi = i / p.S, s = i - qi * p.S;
+    const int l = l0 + qi;
+    if (l >= p.L) continue;
+    const float* zr = s_z + qi * ZS;
+    const int64_t bnd = blk_boundary(p, l);
+    int64_t j = 0, cspan = p.N;
+    float lp = 0.0f;
+    for (int d = 0; d < p.Dp; ++d) {
+      cspan /= F;
+      const float* zc = zr + p.lvl_off[d + 1] + j * F;
+      float z[F], g[F];
+      float m = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        z[c] = (p.causal && (j * F + c) * cspan > bnd) ? -INFINITY : zc[c];
+        m = fmaxf(m, z[c]);
+      }
+      float se = 0.0f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) se += expf(z[c] - m);
+      const float lse = m + logf(se);
+      blk_gumbels_of<F>(p, b, h, l, d, s, g);
+      int dir = 0;
+      float best = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        const float sc = z[c] > -INFINITY ? (z[c] - lse) + g[c] : -INFINITY;
+        if (sc > best) { best = sc; dir = c; }
+      }
+      float take = 0.0f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) take = c == dir ? z[c] - lse : take;
+      lp += take;
+      j = j * F + dir;
+    }
+    const int64_t o = (((int64_t)l * p.B + b) * p.H + h) * p.S + s;
+    p.blk[o] = (int32_t)j;
+    s_lp[qi * p.S + s] = lp;
+    const int64_t prow = (int64_t)bh * p.P + (int64_t)l * p.S + s;
+    p.keys0[prow] = (uint32_t)j;
+    p.vals0[prow] = (uint32_t)((int64_t)l * p.S + s);
+  }
+  __syncthreads();
+  // path weights: softmax of each query's path log-probabilities, in path order
+  for (int qi = tid; qi < kWalkQ; qi += blockDim.x) {
+    const int l = l0 + qi;
+    if (l >= p.L) continue;
+    float m = -INFINITY;
+    for (int s = 0; s < p.S; ++s) m = fmaxf(m, s_lp[qi * p.S + s]);
+    float z = 0.0f;
+    for (int s = 0; s < p.S; ++s) z += expf(s_lp[qi * p.S + s] - m);
+    const float inv = 1.0f / z;
+    const int64_t o = (((int64_t)l * p.B + b) * p.H + h) * p.S;
+    for (int s = 0; s < p.S; ++s) p.weights[o + s] = expf(s_lp[qi * p.S + s] - m) * inv;
+  }
+}
+
 // out[l,b,h] = sum_s path_out[b*H+h][l*S+s] in path order (tensor-core forward)
 template <typename T>
 __global__ void __launch_bounds__(256) blk_combine_out_kernel(const BlkParams p) {
@@ -916,7 +1095,19 @@ int blk_fwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
     p.sample_only = 1;
     {
       TA_PROFILE("blocked_sample", st);
-      launch();
+      if constexpr (EPL == 2 || EPL == 4) {
+        if (p.R <= kWalkMaxRows) {
+          constexpr int D = 32 * EPL;
+          const size_t wsm = walk_smem(p.R, D, p.S);
+          cudaFuncSetAttribute(blk_walk_mma_kernel<T, D, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm);
+          const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
+          blk_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
+        } else {
+          launch();
+        }
+      } else {
+        launch();
+      }
     }
     int rc = check_launch("blocked sampler");
     if (rc) return rc;
