@@ -751,50 +751,41 @@ __device__ __forceinline__ void blk_gumbels_of(const BlkParams& p, int b, int h,
   }
 }
 
-template <typename T, int D, int F>
-__global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
+// Convert summary rows [r0, r0 + kWalkChunk) of head bh to bf16/fp16 high and low parts in
+// shared memory ([row][d], padded rows; rows past R are zero).
+template <typename T, int D>
+__device__ __forceinline__ void walk_load_chunk(const BlkParams& p, int bh, int r0, uint16_t* s_chi,
+                                                uint16_t* s_clo) {
   constexpr int LD = D + 8;
-  extern __shared__ __align__(16) unsigned char smraw[];
-  const int RP = walk_rows_pad(p.R);
-  const int ZS = RP + 4;
-  float* s_z = reinterpret_cast<float*>(smraw);                       // [kWalkQ][ZS]
-  uint16_t* s_chi = reinterpret_cast<uint16_t*>(s_z + kWalkQ * ZS);   // [kWalkChunk][LD]
-  uint16_t* s_clo = s_chi + kWalkChunk * LD;
-  uint16_t* s_q = s_clo + kWalkChunk * LD;                            // [kWalkQ][LD]
-  float* s_lp = reinterpret_cast<float*>(s_q + kWalkQ * LD);          // [kWalkQ][S]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int lt = (p.L + kWalkQ - 1) / kWalkQ;
-  const int bh = blockIdx.x / lt;
-  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
-  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-  constexpr int CPR = D * 2 / 16;
-  for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
-    const int r = i / CPR, c = i - r * CPR;
-    if (l0 + r < p.L)
-      cp_async16(s_q + r * LD + c * 8, p.q + ((int64_t)(l0 + r) * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2 + c * 16);
-    else
-      *reinterpret_cast<uint4*>(s_q + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
-  }
-  cp_async_commit();
   const float* csrc = p.summ + (int64_t)bh * p.R * D;
+  for (int i = threadIdx.x; i < kWalkChunk * D / 2; i += blockDim.x) {
+    const int r = i / (D / 2), c = (i - r * (D / 2)) * 2;
+    float2 v = make_float2(0.f, 0.f);
+    if (r0 + r < p.R) v = *reinterpret_cast<const float2*>(csrc + (int64_t)(r0 + r) * D + c);
+    const uint32_t hi = Mma<T>::pack(v.x, v.y);
+    float2 hf;
+    if constexpr (std::is_same<T, __half>::value) {
+      hf = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+    } else {
+      hf = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+    }
+    *reinterpret_cast<uint32_t*>(s_chi + r * LD + c) = hi;
+    *reinterpret_cast<uint32_t*>(s_clo + r * LD + c) = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
+  }
+}
+
+// Z[q][r] = q . c_r for the CTA's kWalkQ query rows (s_q, 16-bit) and every summary row, on
+// the tensor cores with c split into high and low parts (a float32-accurate logit table).
+// Waits for the caller's pending cp.async copies (the query rows).
+template <typename T, int D>
+__device__ __forceinline__ void walk_scores(const BlkParams& p, int bh, const uint16_t* s_q,
+                                            uint16_t* s_chi, uint16_t* s_clo, float* s_z, int RP, int ZS) {
+  constexpr int LD = D + 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int m0 = (warp & 1) * 16, nb0 = (warp >> 1) * 32;  // warp: 16 queries x 32 rows of a chunk
   for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
     __syncthreads();  // the previous chunk's readers are done
-    for (int i = tid; i < kWalkChunk * D / 2; i += blockDim.x) {
-      const int r = i / (D / 2), c = (i - r * (D / 2)) * 2;
-      float2 v = make_float2(0.f, 0.f);
-      if (r0 + r < p.R) v = *reinterpret_cast<const float2*>(csrc + (int64_t)(r0 + r) * D + c);
-      const uint32_t hi = Mma<T>::pack(v.x, v.y);
-      float2 hf;
-      if constexpr (sizeof(T) == 2 && std::is_same<T, __half>::value) {
-        const __half2 hh = *reinterpret_cast<const __half2*>(&hi);
-        hf = __half22float2(hh);
-      } else {
-        hf = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
-      }
-      *reinterpret_cast<uint32_t*>(s_chi + r * LD + c) = hi;
-      *reinterpret_cast<uint32_t*>(s_clo + r * LD + c) = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
-    }
+    walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
     cp_async_wait_0();
     __syncthreads();
     float acc[4][4];
@@ -823,6 +814,34 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
       *reinterpret_cast<float2*>(s_z + (m0 + g + 8) * ZS + c) = make_float2(acc[t][2], acc[t][3]);
     }
   }
+}
+
+template <typename T, int D, int F>
+__global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
+  constexpr int LD = D + 8;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int RP = walk_rows_pad(p.R);
+  const int ZS = RP + 4;
+  float* s_z = reinterpret_cast<float*>(smraw);                       // [kWalkQ][ZS]
+  uint16_t* s_chi = reinterpret_cast<uint16_t*>(s_z + kWalkQ * ZS);   // [kWalkChunk][LD]
+  uint16_t* s_clo = s_chi + kWalkChunk * LD;
+  uint16_t* s_q = s_clo + kWalkChunk * LD;                            // [kWalkQ][LD]
+  float* s_lp = reinterpret_cast<float*>(s_q + kWalkQ * LD);          // [kWalkQ][S]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lt = (p.L + kWalkQ - 1) / kWalkQ;
+  const int bh = blockIdx.x / lt;
+  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  constexpr int CPR = D * 2 / 16;
+  for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i - r * CPR;
+    if (l0 + r < p.L)
+      cp_async16(s_q + r * LD + c * 8, p.q + ((int64_t)(l0 + r) * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2 + c * 16);
+    else
+      *reinterpret_cast<uint4*>(s_q + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
+  }
+  cp_async_commit();
+  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS);
   __syncthreads();
   // one thread per (query, path): the walk reads its children's logits from the table
   for (int i = tid; i < kWalkQ * p.S; i += blockDim.x) {
@@ -880,6 +899,210 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
     const float inv = 1.0f / z;
     const int64_t o = (((int64_t)l * p.B + b) * p.H + h) * p.S;
     for (int s = 0; s < p.S; ++s) p.weights[o + s] = expf(s_lp[qi * p.S + s] - m) * inv;
+  }
+}
+
+// Backward of the tree levels as table lookups (tensor-core path), per 32 queries of a head:
+// Z = Q C^T again; per (query, path) thread: delta_s = dO . (w_s o_s), dlp_s = delta_s -
+// w_s sum_t delta_t, and per level the children's coefficients dz = dlp (onehot - softmax(z))
+// (written per path for the summary gradients); per (query, level) thread: the query's
+// coefficient row DZ (paths summed in order); then dq_tree = DZ C on the tensor cores with
+// both operands split into high and low parts.
+__host__ __device__ inline size_t bwd_walk_smem(int64_t R, int D, int S, int DF) {
+  return (size_t)kWalkQ * (walk_rows_pad(R) + 4) * 4    // Z table, then DZ
+         + (size_t)2 * kWalkChunk * (D + 8) * 2          // C chunk high / low
+         + (size_t)2 * kWalkQ * (D + 8) * 2              // Q and dO tiles
+         + (size_t)kWalkQ * S * 4                        // delta, then dlp
+         + (size_t)kWalkQ * S * DF * 4;                  // dz per path
+}
+
+template <typename T, int D, int F>
+__global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p) {
+  constexpr int LD = D + 8;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int RP = walk_rows_pad(p.R);
+  const int ZS = RP + 4;
+  const int DF = p.Dp * F;
+  float* s_z = reinterpret_cast<float*>(smraw);                       // [kWalkQ][ZS]
+  uint16_t* s_chi = reinterpret_cast<uint16_t*>(s_z + kWalkQ * ZS);   // [kWalkChunk][LD]
+  uint16_t* s_clo = s_chi + kWalkChunk * LD;
+  uint16_t* s_q = s_clo + kWalkChunk * LD;                            // [kWalkQ][LD]
+  uint16_t* s_g = s_q + kWalkQ * LD;                                  // [kWalkQ][LD]
+  float* s_dl = reinterpret_cast<float*>(s_g + kWalkQ * LD);          // [kWalkQ][S]
+  float* s_dzp = s_dl + kWalkQ * p.S;                                 // [kWalkQ][S][DF]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lt = (p.L + kWalkQ - 1) / kWalkQ;
+  const int bh = blockIdx.x / lt;
+  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  constexpr int CPR = D * 2 / 16;
+  for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i - r * CPR;
+    if (l0 + r < p.L) {
+      const int64_t l = l0 + r;
+      cp_async16(s_q + r * LD + c * 8, p.q + (l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2 + c * 16);
+      cp_async16(s_g + r * LD + c * 8, p.dout + (l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * 2 + c * 16);
+    } else {
+      *reinterpret_cast<uint4*>(s_q + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(s_g + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  cp_async_commit();
+  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS);
+  __syncthreads();
+  // delta_s = dO_q . (w_s o_s)
+  for (int i = tid; i < kWalkQ * p.S; i += blockDim.x) {
+    const int qi = i / p.S, sp = i - qi * p.S;
+    const int64_t l = l0 + qi;
+    if (l >= p.L) continue;
+    const int64_t prow = (int64_t)bh * p.P + l * p.S + sp;
+    const float4* orow = reinterpret_cast<const float4*>(p.path_out + prow * D);
+    const uint16_t* grow = s_g + qi * LD;
+    float dl = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < D / 4; ++c) {
+      const float4 o = orow[c];
+      dl = fmaf(raw_to_float<T>(grow[4 * c]), o.x, dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 1]), o.y, dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 2]), o.z, dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 3]), o.w, dl);
+    }
+    s_dl[qi * p.S + sp] = dl;
+    p.delta[prow] = dl;
+  }
+  __syncthreads();
+  // dlp and the per-level children's coefficients of every path
+  float dlp_mine[4];
+  int n_mine = 0;
+  for (int i = tid; i < kWalkQ * p.S; i += blockDim.x, ++n_mine) {
+    const int qi = i / p.S, sp = i - qi * p.S;
+    const int64_t l = l0 + qi;
+    float tot = 0.0f;
+    for (int t = 0; t < p.S; ++t) tot += s_dl[qi * p.S + t];
+    float dlp = 0.0f;
+    if (l < p.L) {
+      const int64_t o = ((l * p.B + b) * p.H + h) * p.S + sp;
+      dlp = s_dl[qi * p.S + sp] - p.weights[o] * tot;
+    }
+    if (n_mine < 4) dlp_mine[n_mine] = dlp;
+  }
+  __syncthreads();  // every thread has read delta before dlp overwrites it
+  n_mine = 0;
+  for (int i = tid; i < kWalkQ * p.S; i += blockDim.x, ++n_mine) {
+    const int qi = i / p.S, sp = i - qi * p.S;
+    const int64_t l = l0 + qi;
+    float* dzp = s_dzp + (int64_t)(qi * p.S + sp) * DF;
+    if (l >= p.L) {
+      for (int e = 0; e < DF; ++e) dzp[e] = 0.0f;
+      continue;
+    }
+    float dlp = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dlp = u == n_mine ? dlp_mine[u] : dlp;
+    const int64_t prow = (int64_t)bh * p.P + l * p.S + sp;
+    const int64_t o = ((l * p.B + b) * p.H + h) * p.S + sp;
+    const int64_t blk = p.blk[o];
+    const int64_t bnd = blk_boundary(p, (int)l);
+    const float* zr = s_z + qi * ZS;
+    int64_t pw = 1;
+    for (int t = 0; t < p.Dp; ++t) pw *= F;
+    int64_t j = 0, cspan = p.N;
+    for (int d = 0; d < p.Dp; ++d) {
+      pw /= F;
+      cspan /= F;
+      const int dir = (int)((blk / pw) % F);
+      const float* zc = zr + p.lvl_off[d + 1] + j * F;
+      float z[F], m = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        z[c] = (p.causal && (j * F + c) * cspan > bnd) ? -INFINITY : zc[c];
+        m = fmaxf(m, z[c]);
+      }
+      float se = 0.0f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) se += expf(z[c] - m);
+      const float lse = m + logf(se);
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        const float sm = z[c] > -INFINITY ? expf(z[c] - lse) : 0.0f;
+        const float dz = dlp * ((c == dir ? 1.0f : 0.0f) - sm);
+        dzp[d * F + c] = dz;
+        p.dz_rows[prow * DF + d * F + c] = dz;
+      }
+      j = j * F + dir;
+    }
+    p.keys0[prow] = (uint32_t)blk;
+    p.vals0[prow] = (uint32_t)(l * p.S + sp);
+  }
+  __syncthreads();
+  // DZ: the table region becomes the coefficient rows, summed over paths in order
+  for (int i = tid; i < kWalkQ * ZS; i += blockDim.x) s_z[i] = 0.0f;
+  __syncthreads();
+  for (int i = tid; i < kWalkQ * p.Dp; i += blockDim.x) {
+    const int qi = i / p.Dp, d = i - qi * p.Dp;
+    const int64_t l = l0 + qi;
+    if (l >= p.L) continue;
+    int64_t pw = 1;
+    for (int t = 0; t < p.Dp - d; ++t) pw *= F;  // blocks under a level-d node
+    float* dzr = s_z + qi * ZS + p.lvl_off[d + 1];
+    const int64_t o = ((l * p.B + b) * p.H + h) * p.S;
+    for (int sp = 0; sp < p.S; ++sp) {
+      const int64_t jd = p.blk[o + sp] / pw;  // the path's node at level d
+      const float* dzp = s_dzp + (int64_t)(qi * p.S + sp) * DF + d * F;
+#pragma unroll
+      for (int c = 0; c < F; ++c) dzr[jd * F + c] += dzp[c];
+    }
+  }
+  // dq_tree = DZ C: warp w owns queries [16 (w & 1), +16) x columns [(w >> 1) D / 4, +D / 4)
+  constexpr int NTW = D / 32;
+  const int m0 = (warp & 1) * 16, n0 = (warp >> 1) * (D / 4);
+  const int g = lane >> 2, tq = lane & 3;
+  float acc[NTW][4];
+#pragma unroll
+  for (int t = 0; t < NTW; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+  for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
+    __syncthreads();  // DZ complete / previous chunk consumed
+    walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
+    __syncthreads();
+#pragma unroll 2
+    for (int k0 = 0; k0 < kWalkChunk; k0 += 16) {
+      uint32_t ahi[4], alo[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = m0 + g + (u & 1) * 8;
+        const int col = r0 + k0 + tq * 2 + (u >> 1) * 8;
+        const float2 v = *reinterpret_cast<const float2*>(s_z + row * ZS + col);
+        ahi[u] = Mma<T>::pack(v.x, v.y);
+        float2 hf;
+        if constexpr (std::is_same<T, __half>::value) {
+          hf = __half22float2(*reinterpret_cast<const __half2*>(&ahi[u]));
+        } else {
+          hf = make_float2(__uint_as_float(ahi[u] << 16), __uint_as_float(ahi[u] & 0xffff0000u));
+        }
+        alo[u] = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
+      }
+#pragma unroll
+      for (int t = 0; t < NTW; t += 2) {
+        uint32_t bh_[4], bl_[4];
+        frag_b_kn(bh_, s_chi, LD, n0 + t * 8, k0, lane);
+        frag_b_kn(bl_, s_clo, LD, n0 + t * 8, k0, lane);
+        Mma<T>::run(acc[t], ahi, bh_);
+        Mma<T>::run(acc[t + 1], ahi, bh_ + 2);
+        Mma<T>::run(acc[t], ahi, bl_);
+        Mma<T>::run(acc[t + 1], ahi, bl_ + 2);
+        Mma<T>::run(acc[t], alo, bh_);
+        Mma<T>::run(acc[t + 1], alo, bh_ + 2);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int64_t l = l0 + m0 + g + u * 8;
+    if (l >= p.L) continue;
+    float* dst = p.dq_tree + ((l * p.B + b) * p.H + h) * D + n0;
+#pragma unroll
+    for (int t = 0; t < NTW; ++t)
+      *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(acc[t][2 * u], acc[t][2 * u + 1]);
   }
 }
 
@@ -1133,9 +1356,22 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
   const bool mma = p.path_out != nullptr;
   {
     TA_PROFILE("blocked_bwd_query", st);
-    const unsigned grid = (unsigned)(lt * p.B * p.H);
-    const size_t sm = kBlkWarps * wbytes;
-    blk_bwd_query_kernel<T, EPL, F><<<grid, kBlkWarps * 32, sm, st>>>(p);
+    bool done = false;
+    if constexpr (sizeof(T) == 2 && (EPL == 2 || EPL == 4)) {
+      constexpr int D = 32 * EPL;
+      const size_t wsm = bwd_walk_smem(p.R, D, p.S, p.Dp * F);
+      if (mma && wsm <= 220 * 1024 && p.S * kWalkQ <= 4 * 256 && p.Dp * F <= kDFMax) {
+        cudaFuncSetAttribute(blk_bwd_walk_mma_kernel<T, D, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm);
+        const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
+        blk_bwd_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
+        done = true;
+      }
+    }
+    if (!done) {
+      const unsigned grid = (unsigned)(lt * p.B * p.H);
+      const size_t sm = kBlkWarps * wbytes;
+      blk_bwd_query_kernel<T, EPL, F><<<grid, kBlkWarps * 32, sm, st>>>(p);
+    }
   }
   int rc = check_launch("blocked backward (queries)");
   if (rc) return rc;
