@@ -367,6 +367,13 @@ int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const t
  */
 int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
                                      int32_t backward);
+/*
+ * Process-wide choice of the tensor-core forward: 1 = tcgen05 with TMEM accumulators
+ * (default), 0 = mma.sync. Returns the previous setting. The last 4 bytes of the forward
+ * workspace's final 256-byte slot hold the tcgen05 kernel's status after a call (0 = ok, 1 = a
+ * bounded wait expired; the results of that call are then invalid).
+ */
+int32_t ta_blocked_set_tcgen05(int32_t enable);
 size_t ta_blocked_forward_workspace_size(const ta_shape* shape, const ta_blocked* cfg);
 int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
                        ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,

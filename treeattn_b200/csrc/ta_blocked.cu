@@ -127,6 +127,16 @@ extern "C" int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* c
   return check_launch("blocked gumbel fill");
 }
 
+namespace {
+int g_use_tcgen05 = 1;  // leaf-block forward on tcgen05 (1) or mma.sync (0)
+}
+
+extern "C" int32_t ta_blocked_set_tcgen05(int32_t enable) {
+  const int32_t old = g_use_tcgen05;
+  g_use_tcgen05 = enable ? 1 : 0;
+  return old;
+}
+
 extern "C" int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
                                                int32_t backward) {
   BlkParams p;
@@ -165,6 +175,8 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
     const BlkWs w = blk_fwd_ws(p);
     if (!ws || ws_bytes < w.total) return fail(TA_ERR_WORKSPACE, "blocked forward workspace too small");
     p.path_out = path_out;
+    p.status = (int32_t*)((char*)ws + w.dc);
+    p.use_tcgen05 = g_use_tcgen05;
     p.keys0 = (uint32_t*)((char*)ws + w.keys[0]);
     p.vals0 = (uint32_t*)((char*)ws + w.vals[0]);
     sp = blk_sort_params(p, (char*)ws, w.keys, w.vals, w.hist);

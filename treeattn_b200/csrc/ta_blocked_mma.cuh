@@ -93,6 +93,7 @@ struct BlkMmaParams {
   int32_t B, H, L, N, S, nb, causal;
   int64_t P, row0, row_total;
   float scale;
+  int32_t* status;         // tensor-core wait status (0 = ok), forward
 };
 
 template <int LB, int D>
