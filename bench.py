@@ -6,7 +6,7 @@
 One step = one forward + backward pass of the attn-bench kernel contract
 ``tree_attention(q, k, v)`` on bshd bf16 tensors: Haar tree build from k, fused Gumbel-max
 path sampling + softmax + value gather, deterministic backward (dq, dk, dv) and the
-transposed tree build. Workload (BASELINE.json metric "S=16k, d=128 bf16"): B=1 per GPU,
+transposed tree build. Workload (the headline metric "S=16k, d=128 bf16"): B=1 per GPU,
 S=16384, H=16, d=128, 8 sampled paths per query, reference tree semantics (binary tree, one
 token per leaf). Inputs q, k, v, grad_out ~ N(0, 1) from a seeded CUDA generator.
 
@@ -62,7 +62,7 @@ def parse_args():
                    help="shard: (batch, head)-sharded headline workload; sp: sequence-parallel "
                         "causal long context (B=1, S=65536, H=32, d=128, 16 paths unless overridden); "
                         "blocked: generalised fanout / leaf-block tree (B=4, S=4096, H=16, d=128, "
-                        "fanout 2, leaf block 64, 8 paths: BASELINE's single-B200 config)")
+                        "fanout 2, leaf block 64, 8 paths: the single-B200 benchmark config)")
     return p.parse_args()
 
 

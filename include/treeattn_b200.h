@@ -332,7 +332,7 @@ int ta_exact_backward(const ta_shape* shape, int32_t causal, int64_t query_offse
 /* ---- generalised tree: fanout f, leaf blocks of Lb keys -------------------------------- */
 
 /*
- * No counterpart in the reference (its tree is binary with one key per leaf); BASELINE's
+ * No counterpart in the reference (its tree is binary with one key per leaf); the benchmark
  * configurations name a fanout and a leaf block. N = leaf_block * fanout^Dp keys; node
  * (d, j) summarises the keys of blocks [j f^(Dp-d), (j+1) f^(Dp-d)) as mean / 2 (float32,
  * levels 1..Dp, ta_blocked_summary_rows rows per head, [B*H][rows][D]). Each of the S paths of

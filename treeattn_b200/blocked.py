@@ -1,6 +1,6 @@
 """Generalised tree attention: fanout f, leaf blocks of Lb keys (no reference counterpart).
 
-BASELINE's configurations name a fanout and a leaf block ("fanout 4, leaf block 128"); the
+The benchmark configurations name a fanout and a leaf block ("fanout 4, leaf block 128"); the
 reference's tree is binary with one key per leaf. At fanout 2, leaf block 1 this mode is the
 reference sampler on the tree-correct node layout (``node_layout="tree"``). Semantics, noise
 and the deterministic backward are described in ``include/treeattn_b200.h``
