@@ -712,6 +712,77 @@ __global__ void __launch_bounds__(kFixWarps * 32) bwd_fixup_kernel(const BwdPara
   }
 }
 
+// One warp per chunk (no block barriers: most chunks own only a few short-span cut nodes):
+// the owner of a cut node finds the span with ballots and sums the span's partial rows in
+// chunk order after its own, lanes over columns (float4), 16 rows in flight.
+constexpr int kFixWarpsPerBlock = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kFixWarpsPerBlock * 32) bwd_fixup_warp_kernel(const BwdParams p, int64_t nchunks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t chunk = (int64_t)blockIdx.x * kFixWarpsPerBlock + (threadIdx.x >> 5);
+  if (chunk >= nchunks) return;  // whole warp
+  const int ln = p.log_n;
+  const int seg = (int)(chunk / p.chunks_per_seg);
+  const int64_t cis = chunk - (int64_t)seg * p.chunks_per_seg;
+  const int64_t seg_end = (int64_t)(seg + 1) * p.chunks_per_seg;
+  const int b = seg / p.H, h = seg - (seg / p.H) * p.H;
+  const int64_t stride = (int64_t)(ln + 1) * 2;
+  const uint8_t* flg = p.flags;
+  const int64_t base_node = ((int64_t)1 << ln) - 1;
+  uint32_t key = 0;
+  bool have_key = false;
+  for (int d = 0; d <= ln; ++d) {
+    if (flg[chunk * stride + 2 * d + 1] == 0) continue;  // not the owner of a cut node
+    if (!have_key) {
+      const int64_t i_last = min((cis + 1) * (int64_t)p.chunk, p.P) - 1;
+      key = p.keys[p.sorted_buf][(int64_t)seg * p.P + i_last];
+      have_key = true;
+    }
+    // the node spans chunk+1 .. c_end: chunks flagged "through" followed by one "ends here"
+    int64_t c_end = chunk + 1;
+    for (int64_t c0 = chunk + 1; c0 < seg_end; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const bool ends = c < seg_end && flg[c * stride + 2 * d] != 2;
+      const unsigned m = __ballot_sync(0xffffffffu, ends);
+      if (m) {
+        c_end = c0 + __ffs(m) - 1;
+        break;
+      }
+    }
+    const int64_t node = d < ln ? heap_node(d, key, ln) : (int64_t)key + base_node - (p.N - 1);
+    for (int c4 = lane * 4; c4 < p.D; c4 += 128) {
+      float4 tot = *reinterpret_cast<const float4*>(p.partial + (chunk * stride + 2 * d + 1) * p.D + c4);
+      int64_t c = chunk + 1;
+      for (; c + 16 <= c_end + 1; c += 16) {
+        float4 v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          v[u] = *reinterpret_cast<const float4*>(p.partial + ((c + u) * stride + 2 * d) * p.D + c4);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) { tot.x += v[u].x; tot.y += v[u].y; tot.z += v[u].z; tot.w += v[u].w; }
+      }
+      for (; c <= c_end; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(p.partial + (c * stride + 2 * d) * p.D + c4);
+        tot.x += v.x; tot.y += v.y; tot.z += v.z; tot.w += v.w;
+      }
+      const float tv[4] = {tot.x, tot.y, tot.z, tot.w};
+      if (d < ln) {
+        char* row = p.dk + ((int64_t)b * p.dkb + (int64_t)h * p.dkh + node * p.dks) *
+                               (p.dk_f32 ? 4 : (int64_t)sizeof(T));
+        if (p.dk_f32) *reinterpret_cast<float4*>(reinterpret_cast<float*>(row) + c4) = tot;
+        else for (int e = 0; e < 4; ++e) reinterpret_cast<T*>(row)[c4 + e] = static_cast<T>(tv[e]);
+      } else if (p.dv_f32) {
+        char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * 4;
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(row) + c4) = tot;
+      } else {
+        char* row = p.dv + ((int64_t)b * p.dvb + (int64_t)h * p.dvh + node * p.dvs) * (int64_t)sizeof(T);
+        for (int e = 0; e < 4; ++e) reinterpret_cast<T*>(row)[c4 + e] = static_cast<T>(tv[e]);
+      }
+    }
+  }
+}
+
 }  // namespace ta
 #include "ta_backward_mma.cuh"
 namespace ta {
@@ -773,7 +844,11 @@ int run_rest(BwdParams& p, cudaStream_t st) {
       const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
       {
         TA_PROFILE("bwd_fixup", st);
-        bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
+        if (p.D % 4 == 0)
+          bwd_fixup_warp_kernel<T><<<(unsigned)((nchunks_total + kFixWarpsPerBlock - 1) / kFixWarpsPerBlock),
+                                     kFixWarpsPerBlock * 32, 0, st>>>(p, nchunks_total);
+        else
+          bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
       }
       return check_launch("backward fix-up");
     }
@@ -790,7 +865,11 @@ int run_rest(BwdParams& p, cudaStream_t st) {
   if ((rc = check_launch("backward node pass"))) return rc;
   {
     TA_PROFILE("bwd_fixup", st);
-    bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
+    if (p.D % 4 == 0)
+          bwd_fixup_warp_kernel<T><<<(unsigned)((nchunks_total + kFixWarpsPerBlock - 1) / kFixWarpsPerBlock),
+                                     kFixWarpsPerBlock * 32, 0, st>>>(p, nchunks_total);
+        else
+          bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
   }
   return check_launch("backward fix-up");
 }
