@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
           float kf[EPC];
           E::unpack(raw[u][i], kf);
 #pragma unroll
-          for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(gl[u], kf[e], acc[i * EPC + e]);
+          for (int e = 0; e < EPC; e += 2) ffma2(acc[i * EPC + e], acc[i * EPC + e + 1], gl[u], kf[e], kf[e + 1]);
         }
       }
     }
