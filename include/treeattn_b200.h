@@ -261,6 +261,15 @@ int ta_backward_coef(const ta_shape* shape, const void* q, ta_layout q_layout, c
                      int32_t dv_dtype, void* workspace, size_t workspace_bytes,
                      ta_stream_t stream);
 
+/*
+ * Process-wide size of the tensor-core node pass's ranges (bf16, head_dim % 32 == 0): each CTA
+ * reduces `chunks` consecutive 128-path chunks of a head, carrying open nodes between them, and
+ * only nodes cut by a range boundary go through the fix-up. 0 (default) derives it from the
+ * shape (about 1184 ranges, at most 32 chunks each); values above 32 are clamped. The
+ * summation order, and so the low bits of dK / dV, depend on it. Returns the previous setting.
+ */
+int32_t ta_backward_set_node_range(int32_t chunks);
+
 /* ---- causal mode (A9) ------------------------------------------------------------- */
 
 /*

@@ -353,3 +353,38 @@ def test_backward_bf16_tensor_core_node_pass(L, N, B, H, D, S):
     dq2, dk2, dv2 = ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S,
                                  dk_dtype=torch.float32)
     assert torch.equal(dk, dk2) and torch.equal(dv, dv2) and torch.equal(dq, dq2)
+
+
+@pytest.mark.parametrize("range_chunks", [1, 3, 32])
+@pytest.mark.parametrize("L,N,B,H,D,S", [(2048, 2048, 1, 2, 128, 8), (1000, 64, 2, 1, 64, 3),
+                                         (512, 8192, 1, 1, 256, 8)])
+def test_node_pass_ranges_carry_open_nodes(range_chunks, L, N, B, H, D, S):
+    """The tensor-core node pass walks ranges of 128-path chunks and carries nodes that stay
+    open between chunks (deep trees: many nodes span several chunks; shallow trees: every
+    node does). Every range size matches the oracle and is bitwise repeatable."""
+    from treeattn_b200 import _lib
+
+    lib = _lib.load()
+    torch.manual_seed(L + N + D)
+    q = torch.randn(L, B, H, D, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(N - 1, B, H, D, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(N, B, H, D, device=DEV, dtype=torch.bfloat16)
+    go = torch.randn(L, B, H, D, device=DEV, dtype=torch.bfloat16)
+    torch.manual_seed(3)
+    res = ops.forward(q, k, v, S)
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    rq, rk, rv = O.backward(f(q), f(k), f(v), f(go), res.leaf.cpu().numpy().astype(np.int64),
+                            res.weights.cpu().numpy())
+    old = lib.ta_backward_set_node_range(range_chunks)
+    try:
+        outs = [ops.backward(q, k, v, go, res.leaf, res.weights, res.branch_prob, S,
+                             dk_dtype=torch.float32,
+                             dv=torch.empty(N, B, H, D, device=DEV, dtype=torch.float32))
+                for _ in range(2)]
+    finally:
+        lib.ta_backward_set_node_range(old)
+    dq, dk, dv = outs[0]
+    np.testing.assert_allclose(f(dk), rk, atol=2e-4, rtol=2e-4)
+    np.testing.assert_allclose(f(dv), rv, atol=2e-4, rtol=2e-4)
+    np.testing.assert_allclose(f(dq), rq, atol=2e-2, rtol=1e-2)
+    assert all(torch.equal(a, b) for a, b in zip(outs[0], outs[1]))

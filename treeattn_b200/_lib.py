@@ -98,6 +98,7 @@ SIGNATURES = {
     "ta_blocked_gumbel_fill": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked),
                                               ctypes.POINTER(Rng), _P, _P]),
     "ta_blocked_set_tcgen05": (_I32, [_I32]),
+    "ta_backward_set_node_range": (_I32, [_I32]),
     "ta_blocked_uses_tensor_cores": (_I32, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _I32]),
     "ta_blocked_forward_workspace_size": (_SZ, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked)]),
     "ta_blocked_forward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,

@@ -134,8 +134,18 @@ struct BwdLayout {
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+namespace {
+int32_t g_node_range_chunks = 0;  // 0: chunks per node-pass range follow from the shape
+}
+
+extern "C" int32_t ta_backward_set_node_range(int32_t chunks) {
+  const int32_t old = g_node_range_chunks;
+  g_node_range_chunks = chunks < 0 ? 0 : chunks;
+  return old;
+}
+
 static int chunk_of(const ta_shape* s) {
-  return use_mma_node_pass(s->dtype, s->head_dim) ? kChunkMma : kChunk;
+  return use_mma_node_pass(s->dtype, s->head_dim, floor_log2(s->num_leaves)) ? kChunkMma : kChunk;
 }
 
 static BwdLayout bwd_layout(const ta_shape* s) {
@@ -242,6 +252,7 @@ static int bwd_setup(const ta_shape* shape, const void* q, ta_layout ql, const v
   p.chunk = chunk_of(shape);
   p.chunks_per_seg = (int32_t)((p.P + p.chunk - 1) / p.chunk);
   p.max_logit = shape->max_logit;
+  p.node_range_chunks = g_node_range_chunks;
   if (p.log_n > 30) return fail(TA_ERR_UNSUPPORTED, "tree too deep");
   return TA_OK;
 }

@@ -65,13 +65,38 @@ struct BwdParams {
   int32_t chunk;       // sorted paths per node-pass chunk
   int32_t coef_mode;   // sig holds final per-level coefficients, dlp holds value weights
   int32_t dv_f32;      // dv written as float32 (else input dtype)
+  int32_t node_range_chunks;  // tensor-core node pass: chunks per CTA range (0 = from the shape)
 };
 
-// The tensor-core node pass serves bf16 inputs whose head_dim is a multiple of 32 (<= 256).
-inline bool use_mma_node_pass(int32_t dtype, int64_t D) {
-  return dtype == TA_BF16 && D % 32 == 0 && D <= 256 && D / 32 != 5 && D / 32 != 6 && D / 32 != 7;
+constexpr int kChunkMma = 128;      // paths per tensor-core node-pass chunk (one per thread)
+constexpr int kMTile = 32;          // G rows per MMA pass (two m16 tiles)
+constexpr int kGK = 2 * kChunkMma;  // K of the product: high | low coefficient halves
+constexpr int kGStride = kGK + 8;   // padded row (elements) of the G tile
+constexpr int kMaxLev = 31;
+
+__host__ __device__ inline int mma_row_stride(int D) { return D + 8; }  // padded Q/dO rows
+// Shared memory of one tensor-core node-pass CTA for head_dim D and a tree of 2^ln leaves.
+__host__ __device__ inline size_t mma_node_smem(int D, int ln) {
+  const int lev = ln + 1;
+  return (size_t)2 * kChunkMma * mma_row_stride(D) * 2  // q, dO rows (bf16)
+         + (size_t)kMTile * kGStride * 2                 // G tile (bf16)
+         + (size_t)lev * kChunkMma * 4                   // coefficients [level][path]
+         + (size_t)2 * lev * D * 4                       // carried node rows, two parities
+         + (size_t)kChunkMma * 4 * 3                     // keys, shared depths, query rows
+         + (size_t)kMTile * 4 * 2                        // tile rows: run key, level
+         + (size_t)4 * kMaxLev * 4                       // run-start masks [warp][level]
+         + (size_t)kMaxLev * 4 * 2                       // rows per level, row offsets
+         + (size_t)2 * kMaxLev * 4                       // carried-node origin, two parities
+         + (size_t)4 * kMaxLev * 4 + 64;                 // per-warp run prefixes
 }
-constexpr int kChunkMma = 128;
+constexpr size_t kMaxBlockSmem = 227 * 1024;
+
+// The tensor-core node pass serves bf16 inputs whose head_dim is a multiple of 32 (<= 256)
+// and whose CTA fits the shared-memory limit.
+inline bool use_mma_node_pass(int32_t dtype, int64_t D, int ln) {
+  return dtype == TA_BF16 && D % 32 == 0 && D <= 256 && D / 32 != 5 && D / 32 != 6 && D / 32 != 7 &&
+         mma_node_smem((int)D, ln) <= kMaxBlockSmem;
+}
 
 // radix-sort kernels (ta_backward.cu)
 __global__ void sort_hist_kernel(const BwdParams p, int src, int shift);
@@ -841,14 +866,20 @@ int run_rest(BwdParams& p, cudaStream_t st) {
         }
       }
       if ((rc = check_launch("backward node pass"))) return rc;
-      const int64_t nchunks_total = (int64_t)p.B * p.H * p.chunks_per_seg;
+      // the node pass cuts nodes only at range boundaries: the fix-up's chunks are the ranges
+      int range_chunks, ranges_per_seg;
+      node_mma_ranges(p, range_chunks, ranges_per_seg);
+      BwdParams pf = p;
+      pf.chunk = range_chunks * kChunkMma;
+      pf.chunks_per_seg = ranges_per_seg;
+      const int64_t nranges_total = (int64_t)p.B * p.H * ranges_per_seg;
       {
         TA_PROFILE("bwd_fixup", st);
         if (p.D % 4 == 0)
-          bwd_fixup_warp_kernel<T><<<(unsigned)((nchunks_total + kFixWarpsPerBlock - 1) / kFixWarpsPerBlock),
-                                     kFixWarpsPerBlock * 32, 0, st>>>(p, nchunks_total);
+          bwd_fixup_warp_kernel<T><<<(unsigned)((nranges_total + kFixWarpsPerBlock - 1) / kFixWarpsPerBlock),
+                                     kFixWarpsPerBlock * 32, 0, st>>>(pf, nranges_total);
         else
-          bwd_fixup_kernel<T><<<(unsigned)nchunks_total, kFixWarps * 32, 0, st>>>(p);
+          bwd_fixup_kernel<T><<<(unsigned)nranges_total, kFixWarps * 32, 0, st>>>(pf);
       }
       return check_launch("backward fix-up");
     }
