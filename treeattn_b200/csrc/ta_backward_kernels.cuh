@@ -82,7 +82,7 @@ __host__ __device__ inline size_t mma_node_smem(int D, int ln) {
          + (size_t)kMTile * kGStride * 2                 // G tile (bf16)
          + (size_t)lev * kChunkMma * 4                   // coefficients [level][path]
          + (size_t)2 * lev * D * 4                       // carried node rows, two parities
-         + (size_t)kChunkMma * 4 * 3                     // keys, shared depths, query rows
+         + (size_t)2 * kChunkMma * 4                     // query rows of two sub-chunks
          + (size_t)kMTile * 4 * 2                        // tile rows: run key, level
          + (size_t)4 * kMaxLev * 4                       // run-start masks [warp][level]
          + (size_t)kMaxLev * 4 * 2                       // rows per level, row offsets

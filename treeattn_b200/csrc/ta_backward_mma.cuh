@@ -61,7 +61,7 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int n) {
 // NT = n8 tiles per warp (D / 32)
 template <int NT>
 __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdParams p, int range_chunks,
-                                                                   int ranges_per_seg) {
+                                                                      int ranges_per_seg) {
   using T = __nv_bfloat16;
   extern __shared__ __align__(16) unsigned char s_mma[];
   const int D = p.D;
@@ -72,10 +72,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
   T* s_G = s_g + kMmaChunk * RS;
   float* s_co = reinterpret_cast<float*>(s_G + kMTile * kGStride);   // [lev][path]
   float* s_carry = s_co + lev * kMmaChunk;                            // [2][lev][D]
-  uint32_t* s_key = reinterpret_cast<uint32_t*>(s_carry + 2 * lev * D);
-  int* s_sd = reinterpret_cast<int*>(s_key + kMmaChunk);
-  uint32_t* s_l = reinterpret_cast<uint32_t*>(s_sd + kMmaChunk);     // query row of each path
-  uint32_t* s_rkey = s_l + kMmaChunk;                                // [kMTile] run keys of a tile
+  uint32_t* s_l = reinterpret_cast<uint32_t*>(s_carry + 2 * lev * D);  // [2][path] query rows
+  uint32_t* s_rkey = s_l + 2 * kMmaChunk;                            // [kMTile] run keys of a tile
   int* s_rlev = reinterpret_cast<int*>(s_rkey + kMTile);             // [kMTile] levels of a tile
   uint32_t* s_mask = reinterpret_cast<uint32_t*>(s_rlev + kMTile);   // [4][kMaxLev]
   int* s_runs = reinterpret_cast<int*>(s_mask + 4 * kMaxLev);       // runs per level
@@ -84,6 +82,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
   int* s_wpre = s_pre + 2 * kMaxLev;  // [4][kMaxLev]: runs of level d in earlier path warps
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // path of this thread; the upper half (tid >= 128) writes the low coefficient halves
+  const int pt = tid & (kMmaChunk - 1), upper = tid >> 7;
   const int64_t range = blockIdx.x;
   const int seg = (int)(range / ranges_per_seg);
   const int rr = (int)(range - (int64_t)seg * ranges_per_seg);
@@ -104,72 +104,89 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
   const char* gbase = p.dout + ((int64_t)b * p.gb + (int64_t)h * p.gh) * 2;
   const int cpr = D * 2 / 16;  // 16-byte pieces per row
   const int nsig4 = p.sig_stride / 4;
+  const int h4 = (nsig4 + 1) / 2;  // the lower half stores levels [0, 4 h4), the upper the rest
+  const int sig_lo = upper ? h4 : 0, sig_hi = upper ? nsig4 : h4;
 
-  // gather the rows of a sub-chunk's n paths (query rows in s_l) into dst; rows past n are zero
+  // gather the rows of a sub-chunk's n paths (query rows in sl) into dst; rows past n are zero
   // (each thread copies one 16-byte column piece of every rows_per_it-th row)
   const int rows_per_it = kMmaThreads / cpr, gc = tid % cpr, gr0 = tid / cpr;
-  auto gather_rows = [&](T* dst, const char* src, int64_t stride_el, int n) {
+  auto gather_rows = [&](T* dst, const uint32_t* sl, const char* src, int64_t stride_el, int n) {
     if (gr0 < rows_per_it) {
       for (int r = gr0; r < n; r += rows_per_it)
-        cp_async16(reinterpret_cast<char*>(dst + r * RS) + gc * 16, src + (int64_t)s_l[r] * stride_el * 2 + gc * 16);
+        cp_async16(reinterpret_cast<char*>(dst + r * RS) + gc * 16, src + (int64_t)sl[r] * stride_el * 2 + gc * 16);
       if (n < kMmaChunk)
         for (int r = gr0; r < kMmaChunk; r += rows_per_it)
           if (r >= n) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst + r * RS) + gc * 16) = make_uint4(0, 0, 0, 0);
     }
     cp_async_commit();  // committed even when empty: the wait counts stay fixed
   };
-  // a path's per-level coefficients: loaded into registers early, stored to s_co later
-  float4 sg[8];
+  // a path's per-level coefficients (this half's levels): registers first, s_co later
+  float4 sg[4];
   float c_dl = 0.0f, c_w = 0.0f;
   auto load_coef = [&](uint32_t pl) {
     const float4* sg4 = reinterpret_cast<const float4*>(p.sig + ((int64_t)seg * p.P + pl) * p.sig_stride);
 #pragma unroll
-    for (int d4 = 0; d4 < 8; ++d4)
-      if (d4 < nsig4) sg[d4] = __ldg(sg4 + d4);
+    for (int i = 0; i < 4; ++i)
+      if (sig_lo + i < sig_hi) sg[i] = __ldg(sg4 + sig_lo + i);
     c_dl = p.dlp[(int64_t)seg * p.P + pl];
-    if (!p.coef_mode) {
+    if (!p.coef_mode && !upper) {
       const uint32_t l = pl / (uint32_t)p.S, s = pl - l * (uint32_t)p.S;
       c_w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
     }
   };
   auto store_coef = [&](uint32_t key) {
 #pragma unroll
-    for (int d4 = 0; d4 < 8; ++d4) {
-      if (d4 >= nsig4) break;
-      const float vv[4] = {sg[d4].x, sg[d4].y, sg[d4].z, sg[d4].w};
+    for (int i = 0; i < 4; ++i) {
+      if (sig_lo + i >= sig_hi) break;
+      const float vv[4] = {sg[i].x, sg[i].y, sg[i].z, sg[i].w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int d = 4 * d4 + u;
+        const int d = 4 * (sig_lo + i) + u;
         if (d < ln)
-          s_co[d * kMmaChunk + tid] = p.coef_mode ? vv[u] : (((key >> (ln - 1 - d)) & 1u) ? -vv[u] : vv[u]) * c_dl;
+          s_co[d * kMmaChunk + pt] = p.coef_mode ? vv[u] : (((key >> (ln - 1 - d)) & 1u) ? -vv[u] : vv[u]) * c_dl;
       }
     }
-    s_co[ln * kMmaChunk + tid] = p.coef_mode ? c_dl : c_w;
+    if (!upper) s_co[ln * kMmaChunk + pt] = p.coef_mode ? c_dl : c_w;
   };
   auto shared_depths = [&](uint32_t a, uint32_t c) -> int {
     const uint32_t x = a ^ c;
     return x == 0 ? ln + 1 : ln - (32 - __clz(x)) + 1;
   };
+  // the records one sub-chunk needs, loaded a sub-chunk ahead: this thread's path (key,
+  // position), the key before a warp's first path, and the keys around the sub-chunk
+  struct Rec {
+    uint32_t key, pl, wprev, key0, keyl, prev, next;
+  };
+  auto load_rec = [&](int64_t i0, int n, Rec& r) {
+    r.key = 0; r.pl = 0; r.wprev = 0;
+    if (pt < n) {
+      r.key = keys[i0 + pt];
+      r.pl = vals[i0 + pt];
+      if (lane == 0 && pt > 0) r.wprev = keys[i0 + pt - 1];
+    }
+    r.key0 = keys[i0];
+    r.keyl = keys[i0 + n - 1];
+    r.prev = i0 > 0 ? keys[i0 - 1] : 0u;
+    r.next = i0 + n < p.P ? keys[i0 + n] : 0u;
+  };
 
-  // prologue: the first sub-chunk's records, rows and coefficients
+  // prologue: the first sub-chunk's records, rows and coefficients; a zero G tile
   const int64_t range_i0 = (int64_t)c_first * kMmaChunk;
-  uint32_t my_key = 0, my_pl = 0;
+  Rec cur;
   {
     const int n = (int)min((int64_t)kMmaChunk, p.P - range_i0);
-    if (tid < n) {
-      my_key = keys[range_i0 + tid];
-      my_pl = vals[range_i0 + tid];
-      s_key[tid] = my_key;
-      s_l[tid] = my_pl / (uint32_t)p.S;
-    }
+    load_rec(range_i0, n, cur);
+    if (tid < n) s_l[tid] = cur.pl / (uint32_t)p.S;
     if (tid < kMaxLev) s_pre[tid] = 1;  // at the range start, every open node began before it
     if (tid < 2 * lev) flg[tid] = 0;
+    for (int idx = tid; idx < kMTile * kGStride / 8; idx += kMmaThreads)
+      reinterpret_cast<uint4*>(s_G)[idx] = make_uint4(0, 0, 0, 0);
     __syncthreads();
-    gather_rows(s_q, qbase, p.qs, n);
-    gather_rows(s_g, gbase, p.gs, n);
-    if (tid < n) {
-      load_coef(my_pl);
-      store_coef(my_key);
+    gather_rows(s_q, s_l, qbase, p.qs, n);
+    gather_rows(s_g, s_l, gbase, p.gs, n);
+    if (pt < n) {
+      load_coef(cur.pl);
+      store_coef(cur.key);
     }
   }
 
@@ -178,30 +195,29 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
     const int n = (int)min((int64_t)kMmaChunk, p.P - i0);
     const int64_t i1 = i0 + kMmaChunk;
     const int n1 = j + 1 < cnt ? (int)min((int64_t)kMmaChunk, p.P - i1) : 0;
-    uint32_t nkey = 0, npl = 0;
-    if (tid < n1) {  // the next sub-chunk's records, consumed after the dK product
-      nkey = keys[i1 + tid];
-      npl = vals[i1 + tid];
-    }
+    Rec nxt;  // the next sub-chunk's records, consumed after this one's dK product
+    if (n1 > 0) load_rec(i1, n1, nxt);
     const float* carry_in = s_carry + (j & 1) * lev * D;
     float* carry_out = s_carry + ((j + 1) & 1) * lev * D;
     const int* pre_in = s_pre + (j & 1) * kMaxLev;
     int* pre_out = s_pre + ((j + 1) & 1) * kMaxLev;
+    uint32_t* sl_next = s_l + ((j + 1) & 1) * kMmaChunk;
 
     // run structure: path i opens a new node at level d iff d >= sd(i)
-    const bool has_prev = i0 > 0;
-    const uint32_t prev_key = has_prev ? keys[i0 - 1] : 0u;
-    const bool has_next = i0 + n < p.P;
-    const uint32_t next_key = has_next ? keys[i0 + n] : 0u;
+    const bool has_prev = i0 > 0, has_next = i0 + n < p.P;
+    uint32_t pk = __shfl_up_sync(0xffffffffu, cur.key, 1);  // key of the path before pt
+    if (lane == 0) pk = pt > 0 ? cur.wprev : cur.prev;
     int my_sd = ln + 2;  // no new node anywhere (past the chunk)
-    if (tid < n) my_sd = tid == 0 ? 0 : shared_depths(s_key[tid - 1], my_key);
+    if (pt < n) my_sd = pt == 0 ? 0 : shared_depths(pk, cur.key);
     if (tid < kMmaChunk) {
-      s_sd[tid] = my_sd;
       for (int d = 0; d <= ln; ++d) {
         const uint32_t m = __ballot_sync(0xffffffffu, my_sd <= d);
         if (lane == 0) s_mask[warp * kMaxLev + d] = m;
       }
     }
+    const int open_sd = has_prev ? shared_depths(cur.prev, cur.key0) : 0;  // levels < open_sd began earlier
+    const int cont_sd = has_next ? shared_depths(cur.keyl, cur.next) : 0;
+    const bool last_sub = j + 1 == cnt;
     __syncthreads();
     if (warp == 0) {  // lane d: runs of level d, per-warp prefixes, first row of the level
       int runs = 0;
@@ -222,46 +238,38 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
       if (lane < ln) s_off[lane] = incl - x;
       if (lane == ln) s_off[ln] = 0;
     }
-    const int open_sd = has_prev ? shared_depths(prev_key, s_key[0]) : 0;  // levels < open_sd began earlier
-    const int cont_sd = has_next ? shared_depths(s_key[n - 1], next_key) : 0;
-    const bool last_sub = j + 1 == cnt;
+    if (tid < n1) sl_next[tid] = nxt.pl / (uint32_t)p.S;
+    cp_async_wait_1();  // this sub-chunk's q rows
     __syncthreads();
     const int dk_rows = s_off[ln - 1] + s_runs[ln - 1];
     const int dv_rows = s_runs[ln];
+    const uint32_t le_mask = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+    const int pw = pt >> 5;
 
     // per pass (dK rows with q, then dV rows with dO), tiles of kMTile rows
     for (int pass = 0; pass < 2; ++pass) {
-      cp_async_wait_1();  // pass 0: this sub-chunk's q rows; pass 1: its dO rows
-      __syncthreads();
       const int rows = pass == 0 ? dk_rows : dv_rows;
       const T* s_b = pass == 0 ? s_q : s_g;
       for (int t0 = 0; t0 < rows; t0 += kMTile) {
-        // G tile: zero, then scatter each path's coefficients (high | low)
-        for (int idx = tid; idx < kMTile * kGStride / 8; idx += kMmaThreads)
-          reinterpret_cast<uint4*>(s_G)[idx] = make_uint4(0, 0, 0, 0);
-        __syncthreads();
-        // (dK: threads t and t + 128 take path t's even and odd levels; dV: threads < 128)
-        const int pt = tid & (kMmaChunk - 1);
-        if (pt < n && (pass == 0 || tid < kMmaChunk)) {
-          const int pw = pt >> 5, pln = pt & 31;
-          const uint32_t le_mask = pln == 31 ? 0xffffffffu : ((2u << pln) - 1u);
-          const uint32_t pkey = s_key[pt];
-          const int psd = s_sd[pt];
-          const int dlo = pass == 0 ? (tid >> 7) : ln, dhi = pass == 0 ? ln : ln + 1;
-          for (int d = dlo; d < dhi; d += 2) {
+        // G tile: each thread writes its path's entries (high half: column pt, low half:
+        // column 128 + pt) and clears the same entries after the product, so the tile is
+        // zero again without a block-wide fill
+        uint32_t wrote = 0;
+        if (pt < n) {
+          const int dlo = pass == 0 ? 0 : ln, dhi = pass == 0 ? ln : ln + 1;
+          for (int d = dlo; d < dhi; ++d) {
             // run index of path pt at level d: set bits of level d up to and including it
             const int r = s_wpre[pw * kMaxLev + d] + __popc(s_mask[pw * kMaxLev + d] & le_mask);
             const int row = s_off[d] + r - 1 - t0;
             if (row >= 0 && row < kMTile) {
-              if (psd <= d) {  // this path opens the run: its key names the row's node
-                s_rkey[row] = pkey;
+              if (!upper && my_sd <= d) {  // this path opens the run: its key names the row's node
+                s_rkey[row] = cur.key;
                 s_rlev[row] = d;
               }
               const float c = s_co[d * kMmaChunk + pt];
               const T hi = __float2bfloat16_rn(c);
-              const T lo = __float2bfloat16_rn(c - __bfloat162float(hi));
-              s_G[row * kGStride + pt] = hi;
-              s_G[row * kGStride + kMmaChunk + pt] = lo;
+              s_G[row * kGStride + upper * kMmaChunk + pt] = upper ? __float2bfloat16_rn(c - __bfloat162float(hi)) : hi;
+              wrote |= 1u << row;
             }
           }
         }
@@ -291,90 +299,93 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
         // boundary goes to the partial buffer (slot 2d: began before the range, slot 2d+1:
         // continues past it) for the fix-up; every other node is final.
         const int g = lane >> 2, t = lane & 3;
-        {
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int row = t0 + mt * 16 + g + half * 8;
-            if (row >= rows) continue;
-            const int d = s_rlev[row - t0];
-            const int r = row - s_off[d];
-            const uint32_t key = s_rkey[row - t0];
-            const uint32_t pre = key >> (ln - d);
-            const bool open_in = r == 0 && d < open_sd;
-            const bool cont = r == s_runs[d] - 1 && d < cont_sd;
-            const bool before = open_in && pre_in[d] != 0;  // the node began before the range
-            const bool add_carry = open_in && j > 0;
-            const bool carry = cont && !last_sub;
-            float* pdst = nullptr;
-            if (!carry) {
-              if (before) pdst = part + (int64_t)(2 * d) * D;
-              else if (cont) pdst = part + (int64_t)(2 * d + 1) * D;
-            }
+        for (int half = 0; half < 2; ++half) {
+          const int row = t0 + mt * 16 + g + half * 8;
+          if (row >= rows) continue;
+          const int d = s_rlev[row - t0];
+          const int r = row - s_off[d];
+          const uint32_t key = s_rkey[row - t0];
+          const uint32_t pre = key >> (ln - d);
+          const bool open_in = r == 0 && d < open_sd;
+          const bool cont = r == s_runs[d] - 1 && d < cont_sd;
+          const bool before = open_in && pre_in[d] != 0;  // the node began before the range
+          const bool add_carry = open_in && j > 0;
+          const bool carry = cont && !last_sub;
+          float* pdst = nullptr;
+          if (!carry) {
+            if (before) pdst = part + (int64_t)(2 * d) * D;
+            else if (cont) pdst = part + (int64_t)(2 * d + 1) * D;
+          }
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const int c = n0 + nt * 8 + 2 * t;
-              float2 v = make_float2(acc[nt][half * 2], acc[nt][half * 2 + 1]);
-              if (add_carry) {
-                const float2 cv = *reinterpret_cast<const float2*>(carry_in + d * D + c);
-                v.x = cv.x + v.x;
-                v.y = cv.y + v.y;
-              }
-              if (carry) {
-                *reinterpret_cast<float2*>(carry_out + d * D + c) = v;
-              } else if (pdst != nullptr) {
-                *reinterpret_cast<float2*>(pdst + c) = v;
-              } else if (d < ln) {
-                const int64_t node = ((int64_t)1 << d) - 1 + pre;
-                char* rowp = dkb + node * p.dks * dk_es;
-                if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = v;
-                else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(v.x, v.y);
-              } else {
-                const int64_t leaf = (int64_t)pre + base_node - K;
-                if (p.dv_f32)
-                  *reinterpret_cast<float2*>(reinterpret_cast<float*>(dvb + leaf * p.dvs * 4) + c) = v;
-                else
-                  *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
-                      __floats2bfloat162_rn(v.x, v.y);
-              }
+          for (int nt = 0; nt < NT; ++nt) {
+            const int c = n0 + nt * 8 + 2 * t;
+            float2 v = make_float2(acc[nt][half * 2], acc[nt][half * 2 + 1]);
+            if (add_carry) {
+              const float2 cv = *reinterpret_cast<const float2*>(carry_in + d * D + c);
+              v.x = cv.x + v.x;
+              v.y = cv.y + v.y;
             }
-            if ((warp & 3) == 0 && t == 0) {
-              if (carry) pre_out[d] = before ? 1 : 0;
-              else if (before) flg[2 * d] = cont ? 2 : 1;
-              else if (cont) flg[2 * d + 1] = 1;
+            if (carry) {
+              *reinterpret_cast<float2*>(carry_out + d * D + c) = v;
+            } else if (pdst != nullptr) {
+              *reinterpret_cast<float2*>(pdst + c) = v;
+            } else if (d < ln) {
+              const int64_t node = ((int64_t)1 << d) - 1 + pre;
+              char* rowp = dkb + node * p.dks * dk_es;
+              if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = v;
+              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(v.x, v.y);
+            } else {
+              const int64_t leaf = (int64_t)pre + base_node - K;
+              if (p.dv_f32)
+                *reinterpret_cast<float2*>(reinterpret_cast<float*>(dvb + leaf * p.dvs * 4) + c) = v;
+              else
+                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
+                    __floats2bfloat162_rn(v.x, v.y);
             }
           }
+          if ((warp & 3) == 0 && t == 0) {
+            if (carry) pre_out[d] = before ? 1 : 0;
+            else if (before) flg[2 * d] = cont ? 2 : 1;
+            else if (cont) flg[2 * d + 1] = 1;
+          }
         }
-        __syncthreads();  // G tile reused by the next tile or pass
+        // the dO rows must have landed before the dV pass: wait with the last dK tile's barrier
+        if (pass == 0 && t0 + kMTile >= rows) cp_async_wait_0();
+        __syncthreads();  // G tile, run keys and levels reused by the next tile or pass
+        while (wrote) {
+          const int row = __ffs(wrote) - 1;
+          wrote &= wrote - 1;
+          s_G[row * kGStride + upper * kMmaChunk + pt] = __float2bfloat16_rn(0.0f);
+        }
       }
       if (pass == 0) {  // s_q is free: gather the next sub-chunk's q rows behind the dV product
-        if (tid < n1) s_l[tid] = npl / (uint32_t)p.S;
-        __syncthreads();
-        if (n1 > 0) gather_rows(s_q, qbase, p.qs, n1);
+        if (n1 > 0) gather_rows(s_q, sl_next, qbase, p.qs, n1);
         else cp_async_commit();
-        if (tid < n1) load_coef(npl);
+        if (pt < n1) load_coef(nxt.pl);
       }
     }
 
     // unreached nodes: gaps between consecutive runs, and the head's two ends
-    const int64_t zrow_dk = p.dks * dk_es, zrow_dv = p.dvs * dv_es;
-    auto zero_node = [&](int d, int64_t pf) {
-      if (d < ln) {
-        char* rowp = dkb + (((int64_t)1 << d) - 1 + pf) * zrow_dk;
-        for (int c = 0; c < D; c += 2) {
-          if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-          else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+    if (tid < n) {
+      const int64_t zrow_dk = p.dks * dk_es, zrow_dv = p.dvs * dv_es;
+      auto zero_node = [&](int d, int64_t pf) {
+        if (d < ln) {
+          char* rowp = dkb + (((int64_t)1 << d) - 1 + pf) * zrow_dk;
+          for (int c = 0; c < D; c += 2) {
+            if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
+            else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+          }
+        } else {
+          char* rowp = dvb + (pf + base_node - K) * zrow_dv;
+          for (int c = 0; c < D; c += 2) {
+            if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
+            else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+          }
         }
-      } else {
-        char* rowp = dvb + (pf + base_node - K) * zrow_dv;
-        for (int c = 0; c < D; c += 2) {
-          if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-          else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
-        }
-      }
-    };
-    if (tid < n) {  // path i (> 0) opening a run at level d leaves a gap after the previous run
-      const uint32_t pk = tid > 0 ? s_key[tid - 1] : prev_key;
-      if (tid > 0 || has_prev) {
+      };
+      const uint32_t my_key = cur.key;
+      if (tid > 0 || has_prev) {  // path i opening a run at level d leaves a gap after the previous run
         if (my_key - pk > 1u) {
           const int sd = tid > 0 ? my_sd : shared_depths(pk, my_key);
           for (int d = sd; d <= ln; ++d) {
@@ -393,17 +404,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
         }
       }
     }
-    if (j + 1 == cnt) break;
-    // s_g is free: gather the next sub-chunk's dO rows behind its dK product
-    gather_rows(s_g, gbase, p.gs, n1);
-    __syncthreads();  // every read of this sub-chunk's keys and coefficients is done
-    my_key = nkey;
-    my_pl = npl;
-    if (tid < n1) {
-      s_key[tid] = my_key;
-      store_coef(my_key);
-    }
-    __syncthreads();
+    if (last_sub) break;
+    // s_g is free: gather the next sub-chunk's dO rows behind its dK product. The s_co reads
+    // of this sub-chunk ended before the last tile's barrier; the next run-structure barrier
+    // publishes the new coefficients.
+    gather_rows(s_g, sl_next, gbase, p.gs, n1);
+    cur = nxt;
+    if (pt < n1) store_coef(cur.key);
   }
 }
 
