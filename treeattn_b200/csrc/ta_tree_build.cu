@@ -77,9 +77,17 @@ __global__ void __launch_bounds__(kTreeThreads) haar_fwd_kernel(const TreeParams
 
   float stack[LV][EPC];
   float cur[EPC];
+  // rows are loaded a batch at a time, all loads of a batch issued before its math
+  constexpr int BATCH = RUN < 16 ? RUN : 16;
 #pragma unroll
-  for (int i = 0; i < RUN; ++i) {
-    E::unpack(ld16_stream(src + (c0 + i) * p.ss * (int64_t)sizeof(T)), cur);
+  for (int i0 = 0; i0 < RUN; i0 += BATCH) {
+  uint4 rows[BATCH];
+#pragma unroll
+  for (int u = 0; u < BATCH; ++u) rows[u] = ld16_stream(src + (c0 + i0 + u) * p.ss * (int64_t)sizeof(T));
+#pragma unroll
+  for (int u = 0; u < BATCH; ++u) {
+    const int i = i0 + u;
+    E::unpack(rows[u], cur);
 #pragma unroll
     for (int l = 0; l < LV; ++l) {
       if (((i >> l) & 1) == 0) {
@@ -99,6 +107,7 @@ __global__ void __launch_bounds__(kTreeThreads) haar_fwd_kernel(const TreeParams
       st16(nodes + node_row(p, pos) * p.ns * (int64_t)sizeof(T), E::pack(diff));
     }
   }
+  }
   if (p.write_dst) {
     char* dst = p.dst + ((int64_t)b * p.db + (int64_t)h * p.dh) * sizeof(T) + v * 16;
     st16(dst + run * p.ds * (int64_t)sizeof(T), E::pack(cur));
@@ -108,8 +117,9 @@ __global__ void __launch_bounds__(kTreeThreads) haar_fwd_kernel(const TreeParams
 // backward: expand one run of 2^LV entries from the gradient of its average.
 // src = float32 gradients of run averages (NULL on the top pass: zero), dst = float32
 // gradients of the pass input entries (or dtype dk_leaf on pass 0 when OUT_T != float).
+constexpr int kTreeBwdThreads = 128;
 template <typename OUT_T, int LV>
-__global__ void __launch_bounds__(kTreeThreads) haar_bwd_kernel(const TreeParams p) {
+__global__ void __launch_bounds__(kTreeBwdThreads) haar_bwd_kernel(const TreeParams p) {
   using E = Elem<OUT_T>;
   constexpr int RUN = 1 << LV;
   const int64_t runs = p.count >> LV;
@@ -126,7 +136,12 @@ __global__ void __launch_bounds__(kTreeThreads) haar_bwd_kernel(const TreeParams
 
   const char* nodes = p.nodes + ((int64_t)b * p.nb + (int64_t)h * p.nh) * 4 + v * 16;
   float g[LV + 1][4];
-  float dstk[LV][4];
+  // the diff at position c0 + m (m = 1 .. RUN-1) is used once, by the left child at level
+  // ctz(m): load all of them before any math
+  float dpre[RUN][4];
+#pragma unroll
+  for (int m = 1; m < RUN; ++m)
+    Elem<float>::unpack(ld16_stream(nodes + node_row(p, (c0 + m) * p.pos_scale) * p.ns * 4), dpre[m]);
   if (p.src != nullptr) {
     const char* src = p.src + ((int64_t)b * p.sb + (int64_t)h * p.sh) * 4 + v * 16;
     Elem<float>::unpack(ld16_stream(src + run * p.ss * 4), g[LV]);
@@ -142,14 +157,12 @@ __global__ void __launch_bounds__(kTreeThreads) haar_bwd_kernel(const TreeParams
 #pragma unroll
     for (int l = LV - 1; l >= 0; --l) {
       if (l > top) continue;
-      if ((i >> l) & 1) {  // right child: parent's diff was loaded for the left sibling
+      if ((i >> l) & 1) {  // right child: the parent's diff sits at position i
 #pragma unroll
-        for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] - dstk[l][e]) * 0.5f;
-      } else {  // left child: load the parent's diff at position i + 2^l
-        const int64_t pos = (c0 + i + (1 << l)) * p.pos_scale;
-        Elem<float>::unpack(ld16_stream(nodes + node_row(p, pos) * p.ns * 4), dstk[l]);
+        for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] - dpre[i][e]) * 0.5f;
+      } else {  // left child: the parent's diff sits at position i + 2^l
 #pragma unroll
-        for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] + dstk[l][e]) * 0.5f;
+        for (int e = 0; e < 4; ++e) g[l][e] = (g[l + 1][e] + dpre[i + (1 << l)][e]) * 0.5f;
       }
     }
     char* out = dst + (c0 + i) * p.ds * (int64_t)sizeof(OUT_T);
@@ -182,13 +195,13 @@ template <typename OUT_T>
 static void launch_haar_bwd(int lv, const TreeParams& p, cudaStream_t st) {
   TA_PROFILE("tree_build_bwd", st);
   const int64_t total = (int64_t)p.B * (p.count >> lv) * p.H * p.vecs;
-  const unsigned grid = (unsigned)((total + kTreeThreads - 1) / kTreeThreads);
+  const unsigned grid = (unsigned)((total + kTreeBwdThreads - 1) / kTreeBwdThreads);
   switch (lv) {
-    case 1: haar_bwd_kernel<OUT_T, 1><<<grid, kTreeThreads, 0, st>>>(p); break;
-    case 2: haar_bwd_kernel<OUT_T, 2><<<grid, kTreeThreads, 0, st>>>(p); break;
-    case 3: haar_bwd_kernel<OUT_T, 3><<<grid, kTreeThreads, 0, st>>>(p); break;
-    case 4: haar_bwd_kernel<OUT_T, 4><<<grid, kTreeThreads, 0, st>>>(p); break;
-    default: haar_bwd_kernel<OUT_T, 5><<<grid, kTreeThreads, 0, st>>>(p); break;
+    case 1: haar_bwd_kernel<OUT_T, 1><<<grid, kTreeBwdThreads, 0, st>>>(p); break;
+    case 2: haar_bwd_kernel<OUT_T, 2><<<grid, kTreeBwdThreads, 0, st>>>(p); break;
+    case 3: haar_bwd_kernel<OUT_T, 3><<<grid, kTreeBwdThreads, 0, st>>>(p); break;
+    case 4: haar_bwd_kernel<OUT_T, 4><<<grid, kTreeBwdThreads, 0, st>>>(p); break;
+    default: haar_bwd_kernel<OUT_T, 5><<<grid, kTreeBwdThreads, 0, st>>>(p); break;
   }
 }
 
