@@ -253,6 +253,14 @@ static int bwd_setup(const ta_shape* shape, const void* q, ta_layout ql, const v
   p.chunks_per_seg = (int32_t)((p.P + p.chunk - 1) / p.chunk);
   p.max_logit = shape->max_logit;
   p.node_range_chunks = g_node_range_chunks;
+  p.qtable_levels = 0;
+  if (shape->dtype == TA_BF16 && p.nchunks % 2 == 0 && p.nchunks <= 16 && p.log_n >= 4) {
+    const int tl = p.log_n < kQTableLevels ? p.log_n : kQTableLevels;
+    if ((size_t)kBwdGroups * p.S * 4 + qtable_smem(tl, p.nchunks * 16, p.nchunks * 8) <= 200 * 1024) {
+      p.qtable_levels = tl;
+      p.top_levels = 0;
+    }
+  }
   if (p.log_n > 30) return fail(TA_ERR_UNSUPPORTED, "tree too deep");
   return TA_OK;
 }

@@ -66,7 +66,22 @@ struct BwdParams {
   int32_t coef_mode;   // sig holds final per-level coefficients, dlp holds value weights
   int32_t dv_f32;      // dv written as float32 (else input dtype)
   int32_t node_range_chunks;  // tensor-core node pass: chunks per CTA range (0 = from the shape)
+  int32_t qtable_levels;      // query pass: top levels reduced on the tensor cores (0 = none)
 };
+
+// Query pass, bf16 with head_dim a multiple of 16 (at most 128): the dq contributions of the
+// top kQTableLevels levels of a CTA's 64 queries are one dense product
+//     dq_top[64 x D] = C[64 x nodes] * K_top[nodes x D],  C[l][n] = sum of l's coefficients at n,
+// run with mma.sync (C split into bf16 high and low parts, K exact in bf16); the deeper
+// levels keep the per-lane row gathers.
+constexpr int kQTableLevels = 7;
+__host__ __device__ inline int qtable_cstride(int tl, int D) {
+  const int a = (1 << tl) + 8, b = D + 4;  // C rows, then dq_top rows, in one region
+  return a > b ? a : b;
+}
+__host__ __device__ inline size_t qtable_smem(int tl, int row_bytes, int D) {
+  return (size_t)(1 << tl) * (row_bytes + 16) + (size_t)64 * qtable_cstride(tl, D) * 4;
+}
 
 constexpr int kChunkMma = 128;      // paths per tensor-core node-pass chunk (one per thread)
 constexpr int kMTile = 32;          // G rows per MMA pass (two m16 tiles)
@@ -126,8 +141,15 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
   const unsigned gmask = 0xFu << (threadIdx.x & 28);
   const int row_bytes = p.nchunks * 16;
   const int top_rows = (1 << p.top_levels) - 1;
+  const int tlq = p.qtable_levels;
   char* s_tree = reinterpret_cast<char*>(smem);
-  float* s_dlp = reinterpret_cast<float*>(s_tree + (size_t)top_rows * row_bytes) + g * p.S;
+  // table mode: K_top rows (padded by 16 bytes) then the C / dq_top region
+  const int kts = row_bytes + 16;
+  const int cstride = qtable_cstride(tlq, p.nchunks * 8);
+  float* s_C = reinterpret_cast<float*>(s_tree + (size_t)(1 << tlq) * kts);
+  char* s_after = tlq > 0 ? s_tree + qtable_smem(tlq, row_bytes, p.nchunks * 8)
+                          : s_tree + (size_t)top_rows * row_bytes;
+  float* s_dlp = reinterpret_cast<float*>(s_after) + g * p.S;
 
   const uint32_t K = (uint32_t)p.N - 1u;
   const uint32_t base_node = (1u << p.log_n) - 1u;
@@ -144,10 +166,22 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
     cp_async_wait_0();
     __syncthreads();
   }
-  if (l >= p.L) return;  // whole group leaves together (no block barrier follows)
+  if (tlq > 0) {  // K_top rows 0 .. 2^tlq - 2 (padded stride), then one zero row
+    const int rows = (1 << tlq) - 1, ppr = row_bytes >> 4;
+    for (int i = threadIdx.x; i < rows * ppr; i += kBwdThreads) {
+      const int r = i / ppr, c = i - r * ppr;
+      cp_async16(s_tree + r * kts + c * 16, kbase + (uint64_t)r * kstride + c * 16);
+    }
+    cp_async_commit();
+    for (int c = threadIdx.x; c < ppr; c += kBwdThreads)
+      *reinterpret_cast<uint4*>(s_tree + rows * kts + c * 16) = make_uint4(0, 0, 0, 0);
+  }
+  // groups past the last query stay until the table product's barriers are done
+  const bool active = l < p.L;
+  if (tlq == 0 && !active) return;
 
   // g_s = dO . v[leaf_s]
-  if (!p.coef_mode) {
+  if (active && !p.coef_mode) {
     uint4 graw[CPL];
     const char* grow = p.dout + ((int64_t)l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * sizeof(T);
 #pragma unroll
@@ -181,7 +215,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
     }
   }
   __syncwarp(gmask);
-  if (!p.coef_mode) {
+  if (active && !p.coef_mode) {
     // dlp_s = w_s (g_s - sum_t w_t g_t)
     float wg = 0.0f;
     for (int s = 0; s < p.S; ++s) wg = fmaf(p.weights[j0 + s], s_dlp[s], wg);
@@ -201,12 +235,89 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
   float acc[NE];
 #pragma unroll
   for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && CPL <= 4) {
+    if (tlq > 0) {
+      // C row of this query: lane t4 adds the levels d = t4 (mod 4), paths in order
+      float* crow = s_C + g * cstride;
+      for (int c = t4; c < (1 << tlq); c += 4) crow[c] = 0.0f;
+      __syncwarp(gmask);
+      if (active) {
+        for (int s = 0; s < p.S; ++s) {
+          const uint32_t bits = p.coef_mode ? p.keys[0][path0 + s] : (uint32_t)p.leaf[j0 + s] + K - base_node;
+          const float dlp = p.coef_mode ? 1.0f : s_dlp[s];
+          const float* sig = p.sig + (path0 + s) * p.sig_stride;
+          for (int d = t4; d < tlq; d += 4) {
+            const uint32_t node = (1u << d) - 1u + (bits >> (p.log_n - d));
+            const float sgn = (!p.coef_mode && ((bits >> (p.log_n - 1 - d)) & 1u)) ? -1.0f : 1.0f;
+            crow[node] += sgn * __ldg(sig + d) * dlp;
+          }
+        }
+      }
+      cp_async_wait_0();
+      __syncthreads();
+      // dq_top: warp w takes query rows [16 (w % 4), +16) and column half w / 4
+      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      const int mt = warp & 3, gq = lane >> 2, tq = lane & 3;
+      const int D = p.nchunks * 8, ntiles = D / 16;
+      const int n0 = (warp >> 2) * (D / 2);
+      const T* s_kt = reinterpret_cast<const T*>(s_tree);
+      const int kre = kts / 2;  // padded row in elements
+      float dacc[2 * CPL][4];
+#pragma unroll
+      for (int nt = 0; nt < 2 * CPL; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dacc[nt][e] = 0.0f;
+      auto split = [](float2 x, uint32_t& hi, uint32_t& lo) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x.x, x.y);
+        const __nv_bfloat162 r = __floats2bfloat162_rn(x.x - __bfloat162float(h.x), x.y - __bfloat162float(h.y));
+        hi = *reinterpret_cast<const uint32_t*>(&h);
+        lo = *reinterpret_cast<const uint32_t*>(&r);
+      };
+      for (int nb = 0; nb < (1 << tlq) / 16; ++nb) {
+        const float* c0 = s_C + (mt * 16 + gq) * cstride + nb * 16 + 2 * tq;
+        const float* c1 = c0 + 8 * cstride;
+        uint32_t ahi[4], alo[4];
+        split(*reinterpret_cast<const float2*>(c0), ahi[0], alo[0]);
+        split(*reinterpret_cast<const float2*>(c1), ahi[1], alo[1]);
+        split(*reinterpret_cast<const float2*>(c0 + 8), ahi[2], alo[2]);
+        split(*reinterpret_cast<const float2*>(c1 + 8), ahi[3], alo[3]);
+#pragma unroll
+        for (int nt = 0; nt < 2 * CPL; ++nt) {
+          if (nt < ntiles) {
+            uint32_t bfr[2];
+            ldsm_x2_trans(bfr, s_kt + (nb * 16 + (lane & 15)) * kre + n0 + nt * 8);
+            mma_bf16(dacc[nt], ahi, bfr);
+            mma_bf16(dacc[nt], alo, bfr);
+          }
+        }
+      }
+      __syncthreads();  // C reads done: the region takes dq_top [64][D + 4]
+#pragma unroll
+      for (int nt = 0; nt < 2 * CPL; ++nt) {
+        if (nt < ntiles) {
+          const int col = n0 + nt * 8 + 2 * tq;
+          *reinterpret_cast<float2*>(s_C + (mt * 16 + gq) * cstride + col) = make_float2(dacc[nt][0], dacc[nt][1]);
+          *reinterpret_cast<float2*>(s_C + (mt * 16 + gq + 8) * cstride + col) = make_float2(dacc[nt][2], dacc[nt][3]);
+        }
+      }
+      __syncthreads();
+      if (!active) return;
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        const int c = i * 4 + t4;
+        if (c < p.nchunks) {
+#pragma unroll
+          for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = s_C[g * cstride + c * EPC + e];
+        }
+      }
+    }
+  }
   for (int s = 0; s < p.S; ++s) {
     // coefficient mode: the records were written by the caller (before the sort)
     const uint32_t bits = p.coef_mode ? p.keys[0][path0 + s] : (uint32_t)p.leaf[j0 + s] + K - base_node;
     const float dlp = p.coef_mode ? 1.0f : s_dlp[s];
     const float* sig = p.sig + (path0 + s) * p.sig_stride;
-    for (int d0 = 0; d0 < p.log_n; d0 += DU) {
+    for (int d0 = tlq; d0 < p.log_n; d0 += DU) {
       uint4 raw[DU][CPL];
       float gl[DU];
 #pragma unroll
@@ -819,7 +930,8 @@ template <typename T, int CPL>
 void launch_query(const BwdParams& p, cudaStream_t st) {
   const int ltiles = (p.L + kBwdGroups - 1) / kBwdGroups;
   const size_t smem = (size_t)kBwdGroups * p.S * 4 +
-                      (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16;
+                      (p.qtable_levels > 0 ? qtable_smem(p.qtable_levels, p.nchunks * 16, p.nchunks * 8)
+                                           : (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(bwd_query_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   TA_PROFILE("bwd_query", st);
