@@ -66,17 +66,25 @@ def _log_softmax_masked(z: np.ndarray, valid: np.ndarray) -> np.ndarray:
     return (zz - m - np.log(np.exp(zz - m).sum(-1, keepdims=True))).astype(np.float32)
 
 
-def sample_blocks(q, summ, gumbels, num_samples, fanout, leaf_block, num_keys, causal):
+def _boundary(L, num_keys, query_start, total_queries):
+    """Causal boundary of queries [query_start, query_start + L) of ``total_queries``."""
+    total = L if total_queries is None else total_queries
+    return query_start + np.arange(L) + num_keys - total
+
+
+def sample_blocks(q, summ, gumbels, num_samples, fanout, leaf_block, num_keys, causal,
+                  query_start=0, total_queries=None):
     """Sampled leaf block (L, B, H, S) and path log-probability (float32).
 
-    gumbels: (Dp, L, B, H, S, f) float32.
+    gumbels: (Dp, L, B, H, S, f) float32. ``q`` may be the slice [query_start, +L) of
+    ``total_queries`` queries (the causal boundary is that of the full call).
     """
     L, B, H, D = q.shape
     dp = len(summ)
     S = num_samples
     j = np.zeros((L, B, H, S), dtype=np.int64)
     lp = np.zeros((L, B, H, S), dtype=np.float32)
-    boundary = np.arange(L) + num_keys - L
+    boundary = _boundary(L, num_keys, query_start, total_queries)
     for d in range(dp):
         child = summ[d]                                   # level d+1: (f^(d+1), B, H, D)
         idx = j[..., None] * fanout + np.arange(fanout)   # (L,B,H,S,f)
@@ -97,7 +105,8 @@ def sample_blocks(q, summ, gumbels, num_samples, fanout, leaf_block, num_keys, c
     return j, lp
 
 
-def leaf_block_attention(q, k, v, blk, leaf_block, softmax_scale, causal):
+def leaf_block_attention(q, k, v, blk, leaf_block, softmax_scale, causal, query_start=0,
+                         total_queries=None):
     """o_s = softmax(scale q . K_blk) V_blk per path: (L, B, H, S, D) float32, and P."""
     L, B, H, D = q.shape
     N = k.shape[0]
@@ -109,7 +118,7 @@ def leaf_block_attention(q, k, v, blk, leaf_block, softmax_scale, causal):
     vr = v[keys, bi, hi].astype(np.float32)
     a = np.float32(softmax_scale) * np.einsum("lbhd,lbhskd->lbhsk", q.astype(np.float32), kr)
     if causal:
-        boundary = np.arange(L) + N - L
+        boundary = _boundary(L, N, query_start, total_queries)
         a = np.where(keys <= boundary[:, None, None, None, None], a, -np.inf)
     m = a.max(-1, keepdims=True)
     e = np.exp(a - m)
@@ -117,13 +126,19 @@ def leaf_block_attention(q, k, v, blk, leaf_block, softmax_scale, causal):
     return np.einsum("lbhsk,lbhskd->lbhsd", p, vr).astype(np.float32), p
 
 
-def forward(q, k, v, gumbels, num_samples, fanout, leaf_block, causal=False, softmax_scale=None):
-    """dict(out (L,B,H,D), weights (L,B,H,S), block (L,B,H,S)); q/k/v (seq, B, H, D) float32."""
+def forward(q, k, v, gumbels, num_samples, fanout, leaf_block, causal=False, softmax_scale=None,
+            query_start=0, total_queries=None, summ=None):
+    """dict(out (L,B,H,D), weights (L,B,H,S), block (L,B,H,S)); q/k/v (seq, B, H, D) float32.
+
+    ``q`` / ``gumbels`` may cover the query slice [query_start, +L) of ``total_queries`` (large
+    problems are checked a slice at a time); ``summ`` reuses precomputed ``summaries``.
+    """
     D = q.shape[-1]
     scale = D ** -0.5 if softmax_scale is None else softmax_scale
-    summ = summaries(k, fanout, leaf_block)
-    blk, lp = sample_blocks(q, summ, gumbels, num_samples, fanout, leaf_block, k.shape[0], causal)
-    o, _ = leaf_block_attention(q, k, v, blk, leaf_block, scale, causal)
+    summ = summaries(k, fanout, leaf_block) if summ is None else summ
+    blk, lp = sample_blocks(q, summ, gumbels, num_samples, fanout, leaf_block, k.shape[0], causal,
+                            query_start, total_queries)
+    o, _ = leaf_block_attention(q, k, v, blk, leaf_block, scale, causal, query_start, total_queries)
     m = lp.max(-1, keepdims=True)
     e = np.exp(lp - m)
     w = (e / e.sum(-1, keepdims=True)).astype(np.float32)
@@ -131,9 +146,11 @@ def forward(q, k, v, gumbels, num_samples, fanout, leaf_block, causal=False, sof
     return dict(out=out, weights=w, block=blk, log_prob=lp)
 
 
-def forward_torch(q, k, v, block, fanout, leaf_block, causal=False, softmax_scale=None):
+def forward_torch(q, k, v, block, fanout, leaf_block, causal=False, softmax_scale=None,
+                  query_start=0, total_queries=None):
     """Differentiable torch (CPU, float64-capable) restatement given the sampled blocks, for
-    gradients: returns out (L, B, H, D). The path of block b is its base-f digits."""
+    gradients: returns out (L, B, H, D). The path of block b is its base-f digits. ``q`` may
+    be the query slice [query_start, +L) of ``total_queries``."""
     import torch
 
     L, B, H, D = q.shape
@@ -144,7 +161,7 @@ def forward_torch(q, k, v, block, fanout, leaf_block, causal=False, softmax_scal
     S = blk.shape[-1]
     bi = torch.arange(B)[None, :, None, None, None]
     hi = torch.arange(H)[None, None, :, None, None]
-    boundary = torch.arange(L) + N - L
+    boundary = torch.as_tensor(_boundary(L, N, query_start, total_queries))
     lp = torch.zeros(L, B, H, S, dtype=q.dtype)
     for d in range(dp):
         n = fanout ** (d + 1)

@@ -248,6 +248,24 @@ def forward(q, k, v, gumbels, num_samples, max_logit=MAX_LOGIT):
 # A8: analytic backward  (_autograd.py:707-860)
 # --------------------------------------------------------------------------------------
 
+def _scatter_rows(dst: np.ndarray, rows: np.ndarray, coef: np.ndarray, src: np.ndarray) -> None:
+    """dst[rows[l,b,h,s], b, h] += coef[l,b,h,s] * src[l,b,h] (repeated rows summed, float64).
+
+    Per (b, h) this is a sparse (rows x L) matrix times src, so scipy's sparse product does the
+    scatter: the same totals as np.add.at up to summation order, fast at 10^6 paths.
+    """
+    from scipy import sparse
+
+    L, B, H, S = rows.shape
+    T = dst.shape[0]
+    lidx = np.broadcast_to(np.arange(L)[:, None], (L, S)).ravel()
+    for b in range(B):
+        for h in range(H):
+            m = sparse.csr_matrix((coef[:, b, h].astype(np.float64).ravel(),
+                                   (rows[:, b, h].ravel(), lidx)), shape=(T, L))
+            dst[:, b, h] += m @ src[:, b, h].astype(np.float64)
+
+
 def backward(q, k, v, grad_out, leaf, w, max_logit=MAX_LOGIT):
     """Analytic gradients of the stochastic forward (Gumbels are constants).
 
@@ -267,11 +285,8 @@ def backward(q, k, v, grad_out, leaf, w, max_logit=MAX_LOGIT):
     g = np.einsum("lbhd,lbhsd->lbhs", do32, vg, dtype=np.float32)
     dlp = (w * (g - (w * g).sum(-1, keepdims=True))).astype(np.float32)
 
-    bidx = np.broadcast_to(np.arange(B)[None, :, None, None], leaf.shape)
-    hidx = np.broadcast_to(np.arange(H)[None, None, :, None], leaf.shape)
     dv = np.zeros((N, B, H, D), dtype=np.float64)
-    contrib = w[..., None].astype(np.float64) * do32[:, :, :, None, :]
-    np.add.at(dv, (leaf_c, bidx, hidx), contrib)
+    _scatter_rows(dv, leaf_c, w, do32)
 
     dq = np.zeros((L, B, H, D), dtype=np.float64)
     dk = np.zeros((max(K, 1), B, H, D), dtype=np.float64)
@@ -284,7 +299,7 @@ def backward(q, k, v, grad_out, leaf, w, max_logit=MAX_LOGIT):
         sgn = np.where(bit == 0, 1.0, -1.0)
         gl = sgn * (1.0 / (1.0 + np.exp(sgn * s.astype(np.float64)))) * dlp
         dq += (gl[..., None] * kn).sum(axis=-2)
-        np.add.at(dk, (node, bidx, hidx), gl[..., None] * q32[:, :, :, None, :])
+        _scatter_rows(dk, node, gl, q32)
         node = 2 * node + 1 + bit
     return dq.astype(np.float32), dk[:K].astype(np.float32), dv.astype(np.float32)
 
@@ -327,6 +342,31 @@ def adapter_forward_backward(q_bshd, k_bshd, v_bshd, grad_out_bshd, gumbels, num
     t = lambda x: np.ascontiguousarray(np.transpose(x, (1, 0, 2, 3)))  # noqa: E731
     return dict(out=t(round_to_dtype(fw["out"], dtype)), dq=t(dq), dk=t(dk), dv=t(dv),
                 weights=fw["weights"], leaf=fw["leaf"])
+
+
+def adapter_forward_backward_given_leaves(q_bshd, k_bshd, v_bshd, grad_out_bshd, leaf, dtype="f32",
+                                          max_logit=MAX_LOGIT):
+    """``adapter_forward_backward`` along given sampled leaves (L,B,H,S) instead of noise.
+
+    The path log-probabilities are replayed from the leaves' direction bits
+    (_autograd.py:260-314), so out and dq/dk/dv are the reference's values for exactly those
+    paths. Used to check values independently of near-tie decisions at large sizes.
+    """
+    q = np.transpose(q_bshd, (1, 0, 2, 3))
+    k = np.transpose(k_bshd, (1, 0, 2, 3))
+    v = np.transpose(v_bshd, (1, 0, 2, 3))
+    k_int = haar_internal_node_keys(k, dtype)
+    leaf = np.asarray(leaf, np.int64)
+    rl, lp = replay_paths(q, k_int, path_bits_from_leaf(leaf, v.shape[0]), max_logit)
+    assert np.array_equal(rl, leaf)
+    w = softmax_log_probs(lp)
+    out = weighted_value_sum(v, leaf, w)
+    do = np.transpose(grad_out_bshd, (1, 0, 2, 3))
+    dq, dk_int, dv = backward(q, k_int, v, do, leaf, w, max_logit)
+    dk = haar_internal_node_keys_backward(dk_int)
+    t = lambda x: np.ascontiguousarray(np.transpose(x, (1, 0, 2, 3)))  # noqa: E731
+    return dict(out=t(round_to_dtype(out, dtype)), dq=t(dq), dk=t(dk), dv=t(dv), weights=w,
+                k_int=k_int)
 
 
 # --------------------------------------------------------------------------------------

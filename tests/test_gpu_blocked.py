@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from oracle import blocked_oracle as BO
+from tests.tolerance import assert_within
 from treeattn_b200 import _lib as L
 from treeattn_b200 import blocked as TB
 from treeattn_b200.sharding import shard_for_rank
@@ -80,9 +81,9 @@ def test_low_precision_within_tolerance(dtype, tol, N, D, f, Lb):
     q64, k64, v64 = (sb(t).requires_grad_(True) for t in (q, k, v))
     ref = BO.forward_torch(q64, k64, v64, blk.cpu().numpy(), f, Lb, causal=True)
     ref.backward(sb(go))
-    assert (sb(out) - ref.detach()).abs().max().item() < tol
-    for mine, want in ((qq.grad, q64.grad), (kk.grad, k64.grad), (vv.grad, v64.grad)):
-        assert (sb(mine) - want).abs().max().item() < tol * 2
+    assert_within(sb(out).numpy(), ref.detach().numpy(), dtype, "out", atol=tol)
+    for name, mine, want in (("dq", qq.grad, q64.grad), ("dk", kk.grad, k64.grad), ("dv", vv.grad, v64.grad)):
+        assert_within(sb(mine).numpy(), want.numpy(), dtype, name, atol=tol)
 
 
 def test_in_kernel_noise_equals_dumped_noise_and_backward_is_deterministic():
