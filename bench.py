@@ -136,6 +136,10 @@ def algorithmic_bytes(kernel: str, B, S, H, D, P, elt, launches_per_step):
     table = {
         # read q, k_int, v; write out; write leaf + weight per path
         "fwd_fused": 4 * rows + 8 * paths,
+        # the walk alone: read q, k_int; write leaf + weight per path
+        "fwd_walk": 2 * rows + 8 * paths,
+        # read v, leaf + weight per path; write out
+        "value_sum": 2 * rows + 8 * paths,
         # read q, dO, k_int, v, leaf + weight; write dq
         "bwd_query": 5 * rows + 8 * paths,
         # read q, dO per path-sorted chunk; write dk (float32) and dv

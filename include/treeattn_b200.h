@@ -270,6 +270,17 @@ int ta_backward_coef(const ta_shape* shape, const void* q, ta_layout q_layout, c
  */
 int32_t ta_backward_set_node_range(int32_t chunks);
 
+/*
+ * Process-wide choice of how the non-causal samplers (ta_forward, ta_sample_paths,
+ * ta_replay_paths) form the per-level logits q . k_node for 16-bit inputs with head_dim a
+ * multiple of 32: 1 (default) = m16n8k16 tensor-core products over a warp's eight queries
+ * (exact 16-bit products, float32 sums), 0 = float32 FMA chains on the CUDA cores. The two
+ * sum in different orders, so a decision whose scores tie to within float32 rounding may
+ * differ. Returns the previous setting. (No reference counterpart: the reference's kernels are
+ * scalar.)
+ */
+int32_t ta_forward_set_tensor_dots(int32_t enable);
+
 /* ---- causal mode (A9) ------------------------------------------------------------- */
 
 /*
@@ -378,11 +389,23 @@ int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cf
                                      int32_t backward);
 /*
  * Process-wide choice of the tensor-core forward: 1 = tcgen05 with TMEM accumulators
- * (default), 0 = mma.sync. Returns the previous setting. The last 4 bytes of the forward
- * workspace's final 256-byte slot hold the tcgen05 kernel's status after a call (0 = ok, 1 = a
- * bounded wait expired; the results of that call are then invalid).
+ * (default), 0 = mma.sync. Returns the previous setting.
  */
 int32_t ta_blocked_set_tcgen05(int32_t enable);
+/*
+ * Every mbarrier wait of the tcgen05 forward is bounded (default 1 s). A CTA whose wait
+ * expires records it in a process-wide status word in mapped host memory, waits for its
+ * issued MMA, frees its TMEM and returns; that call's results are invalid. The word is read
+ * without a device synchronisation: ta_blocked_status returns it (1 = an expired wait since
+ * it was last cleared; `clear` != 0 resets it), and the next ta_blocked_forward /
+ * ta_blocked_backward returns TA_ERR_CUDA (clearing it) instead of running. The word is set
+ * once the failing kernel has run: synchronise its stream first for a definite answer.
+ * ta_blocked_set_tc_wait_ns sets the bound in nanoseconds (0 = the 1 s default; returns the
+ * previous bound); short bounds exist for testing the status path.
+ * (No reference counterpart: the reference has no tensor-core kernels.)
+ */
+int32_t ta_blocked_status(int32_t clear);
+uint64_t ta_blocked_set_tc_wait_ns(uint64_t ns);
 size_t ta_blocked_forward_workspace_size(const ta_shape* shape, const ta_blocked* cfg);
 int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, const void* q,
                        ta_layout q_layout, const void* k, ta_layout k_layout, const void* v,

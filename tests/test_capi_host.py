@@ -133,3 +133,29 @@ def test_tree_aware_accounting():
     assert f < from_dense / 100
     assert tb.bwd_flops(1, 16384, 16, 128, False, 8) > f
     assert tb.compulsory_bytes(1, 16384, 16, 128) == 12 * 16384 * 16 * 128 * 2
+
+
+def test_library_sources_have_no_blocking_calls():
+    """The attn-bench contract forbids host synchronisation in the hot path: no kernel-path
+    source calls a synchronising CUDA API. Allowed: the profiler's collection call
+    (ta_profile_collect, off the hot path) and the one-time pinned allocation of the tcgen05
+    status word."""
+    csrc = os.path.join(ROOT, "treeattn_b200", "csrc")
+    banned = re.compile(r"\b(cudaDeviceSynchronize|cudaStreamSynchronize|cudaMemcpy|cudaMemcpy2D|"
+                        r"cudaMemset|cudaMalloc|cudaFree|cudaStreamWaitEvent|cudaEventSynchronize)\s*\(")
+    allowed = {("ta_capi.cu", "cudaEventSynchronize")}
+    found = []
+    for name in sorted(os.listdir(csrc)):
+        text = open(os.path.join(csrc, name)).read()
+        text = re.sub(r"//[^\n]*", "", text)
+        for m in banned.finditer(text):
+            if (name, m.group(1)) not in allowed:
+                found.append((name, m.group(1)))
+    assert not found, found
+
+
+def test_blocked_status_word_readable_without_a_gpu():
+    lib = _lib.load()
+    assert lib.ta_blocked_status(0) == 0
+    old = lib.ta_blocked_set_tc_wait_ns(5)
+    assert lib.ta_blocked_set_tc_wait_ns(old) == 5

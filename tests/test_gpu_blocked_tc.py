@@ -37,3 +37,31 @@ def test_tcgen05_forward_matches_mma_sync(dtype, B, N, H, D, S, f, Lb, causal):
     assert torch.equal(blk_tc, blk_ms) and torch.equal(w_tc, w_ms)  # same walk
     tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
     assert (out_tc.float() - out_ms.float()).abs().max().item() < tol
+
+
+def test_expired_wait_is_reported_by_the_next_call():
+    """A 1 ns bound makes the tcgen05 forward's first mbarrier wait expire (the MMA cannot
+    finish that fast). The CTA records it in the host-visible status word, drains its MMA under
+    the normal bound and frees its TMEM; the next blocked call raises instead of running, and
+    once reported the status is clear again. Nothing waits on a flag that is never set."""
+    lib = L.load()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q, k, v = (torch.randn(1, 1024, 2, 128, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    lib.ta_blocked_status(1)
+    old_tc = lib.ta_blocked_set_tcgen05(1)
+    old = lib.ta_blocked_set_tc_wait_ns(1)
+    try:
+        TB.blocked_tree_attention(q, k, v, False, None, num_samples=8, fanout=2, leaf_block=64)
+        torch.cuda.synchronize()
+    finally:
+        lib.ta_blocked_set_tc_wait_ns(old)
+    try:
+        assert lib.ta_blocked_status(0) == 1
+        with pytest.raises(L.TreeAttnError, match="expired"):
+            TB.blocked_tree_attention(q, k, v, False, None, num_samples=8, fanout=2, leaf_block=64)
+        assert lib.ta_blocked_status(0) == 0
+        out = TB.blocked_tree_attention(q, k, v, False, None, num_samples=8, fanout=2, leaf_block=64)
+        torch.cuda.synchronize()
+        assert torch.isfinite(out).all() and lib.ta_blocked_status(0) == 0
+    finally:
+        lib.ta_blocked_set_tcgen05(old_tc)

@@ -98,7 +98,10 @@ SIGNATURES = {
     "ta_blocked_gumbel_fill": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked),
                                               ctypes.POINTER(Rng), _P, _P]),
     "ta_blocked_set_tcgen05": (_I32, [_I32]),
+    "ta_blocked_status": (_I32, [_I32]),
+    "ta_blocked_set_tc_wait_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "ta_backward_set_node_range": (_I32, [_I32]),
+    "ta_forward_set_tensor_dots": (_I32, [_I32]),
     "ta_blocked_uses_tensor_cores": (_I32, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _I32]),
     "ta_blocked_forward_workspace_size": (_SZ, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked)]),
     "ta_blocked_forward": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked), _P, _L, _P, _L,

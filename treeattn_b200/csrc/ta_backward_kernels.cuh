@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
   const int top_rows = (1 << p.top_levels) - 1;
   const int tlq = p.qtable_levels;
   char* s_tree = reinterpret_cast<char*>(smem);
+  const uint32_t s_tree_sa = (uint32_t)__cvta_generic_to_shared(s_tree);
   // table mode: K_top rows (padded by 16 bytes) then the C / dq_top region
   const int kts = row_bytes + 16;
   const int cstride = qtable_cstride(tlq, p.nchunks * 8);
@@ -325,11 +326,11 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
         const int d = min(d0 + u, p.log_n - 1);
         const uint32_t node = (1u << d) - 1u + (bits >> (p.log_n - d));
         if (d < p.top_levels) {
-          const char* krow = s_tree + node * (uint32_t)row_bytes;
+          const uint32_t krow = s_tree_sa + node * (uint32_t)row_bytes;
 #pragma unroll
           for (int i = 0; i < CPL; ++i) {
             const int c = i * 4 + t4;
-            raw[u][i] = c < p.nchunks ? lds16(krow + c * 16) : make_uint4(0, 0, 0, 0);
+            raw[u][i] = c < p.nchunks ? lds16_sa(krow + c * 16) : make_uint4(0, 0, 0, 0);
           }
         } else {
           const char* krow = kbase + (uint64_t)node * kstride;

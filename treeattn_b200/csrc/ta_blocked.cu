@@ -2,6 +2,9 @@
 // noise dump. Kernels and launchers: ta_blocked_impl.cuh; per-(dtype, fanout) instantiations:
 // ta_blocked_<dtype>_f<fanout>.cu; tensor-core leaf-block kernels: ta_blocked_mma_<dtype>.cu.
 
+#include <atomic>
+#include <mutex>
+
 #include "ta_blocked_impl.cuh"
 
 namespace ta {
@@ -129,12 +132,55 @@ extern "C" int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* c
 
 namespace {
 int g_use_tcgen05 = 1;  // leaf-block forward on tcgen05 (1) or mma.sync (0)
+std::atomic<uint64_t> g_tc_wait_ns{kTcWaitNs};
+std::mutex g_tc_status_mu;
+int32_t* g_tc_status = nullptr;  // mapped, portable pinned host word (process-wide, sticky)
+
+// The status word the tcgen05 kernels write on an expired wait: host memory the GPU writes
+// through its mapping, so the host reads it without a device synchronisation.
+int32_t* tc_status_word() {
+  std::lock_guard<std::mutex> lk(g_tc_status_mu);
+  if (g_tc_status == nullptr) {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 256, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    *(volatile int32_t*)h = 0;
+    g_tc_status = (int32_t*)h;
+  }
+  return g_tc_status;
 }
+
+int32_t take_tc_status() {
+  if (g_tc_status == nullptr) return 0;
+  return __atomic_exchange_n(g_tc_status, 0, __ATOMIC_SEQ_CST);
+}
+
+// An earlier tensor-core forward whose bounded wait expired left invalid results: report it
+// from the next blocked call (the flag is cleared when reported).
+int check_tc_status() {
+  if (take_tc_status() != 0)
+    return fail(TA_ERR_CUDA, "an earlier tcgen05 leaf-block forward gave up on an expired "
+                             "mbarrier wait; its results are invalid");
+  return TA_OK;
+}
+}  // namespace
 
 extern "C" int32_t ta_blocked_set_tcgen05(int32_t enable) {
   const int32_t old = g_use_tcgen05;
   g_use_tcgen05 = enable ? 1 : 0;
   return old;
+}
+
+extern "C" uint64_t ta_blocked_set_tc_wait_ns(uint64_t ns) {
+  return g_tc_wait_ns.exchange(ns == 0 ? kTcWaitNs : ns);
+}
+
+extern "C" int32_t ta_blocked_status(int32_t clear) {
+  if (g_tc_status == nullptr) return 0;
+  if (clear) return take_tc_status();
+  return *(volatile int32_t*)g_tc_status;
 }
 
 extern "C" int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
@@ -157,8 +203,9 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
                                   float* weights, float* path_out, void* ws, size_t ws_bytes,
                                   ta_stream_t stream) {
   BlkParams p;
-  int rc = blk_setup(shape, cfg, p);
+  int rc = check_tc_status();
   if (rc) return rc;
+  if ((rc = blk_setup(shape, cfg, p))) return rc;
   if ((rc = blk_views(shape, p, q, ql, k, kl, v, vl))) return rc;
   if ((rc = check_view("out", out, ol, dtype_size(shape->dtype), false))) return rc;
   if (!block || !weights || (p.R > 0 && !summaries))
@@ -175,8 +222,17 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
     const BlkWs w = blk_fwd_ws(p);
     if (!ws || ws_bytes < w.total) return fail(TA_ERR_WORKSPACE, "blocked forward workspace too small");
     p.path_out = path_out;
-    p.status = (int32_t*)((char*)ws + w.dc);
     p.use_tcgen05 = g_use_tcgen05;
+    if (p.use_tcgen05) {
+      int32_t* word = tc_status_word();
+      void* dword = nullptr;
+      if (word == nullptr || cudaHostGetDevicePointer(&dword, word, 0) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TA_ERR_CUDA, "cannot map the tcgen05 status word");
+      }
+      p.status = (volatile int32_t*)dword;
+      p.wait_ns = g_tc_wait_ns.load();
+    }
     p.keys0 = (uint32_t*)((char*)ws + w.keys[0]);
     p.vals0 = (uint32_t*)((char*)ws + w.vals[0]);
     sp = blk_sort_params(p, (char*)ws, w.keys, w.vals, w.hist);
@@ -200,8 +256,9 @@ extern "C" int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg,
                                    ta_layout dkl, void* dv, ta_layout dvl, void* ws,
                                    size_t ws_bytes, ta_stream_t stream) {
   BlkParams p;
-  int rc = blk_setup(shape, cfg, p);
+  int rc = check_tc_status();
   if (rc) return rc;
+  if ((rc = blk_setup(shape, cfg, p))) return rc;
   if ((rc = blk_views(shape, p, q, ql, k, kl, v, vl))) return rc;
   const int es = dtype_size(shape->dtype);
   if ((rc = check_view("grad_out", grad_out, gl, es, false)) || (rc = check_view("dq", dq, dql, es, false)) ||

@@ -82,7 +82,8 @@ struct BlkParams {
   float* delta;          // [B*H][P]
   float* dq_tree;        // [L][B][H][D] float32 tree part of dq
   float* dq_path;        // [B*H][P][D]
-  int32_t* status;       // tensor-core wait status word (forward workspace)
+  volatile int32_t* status;  // tensor-core wait status word (mapped host memory)
+  uint64_t wait_ns;          // bound of one tensor-core mbarrier wait
   int32_t use_tcgen05;   // leaf-block forward on tcgen05 (else mma.sync)
 };
 
@@ -1246,6 +1247,7 @@ static BlkMmaParams blk_mma_params(const BlkParams& p) {
   m.B = p.B; m.H = p.H; m.L = p.L; m.N = p.N; m.S = p.S; m.nb = p.nb; m.causal = p.causal;
   m.P = p.P; m.row0 = p.row0; m.row_total = p.row_total; m.scale = p.scale;
   m.status = p.status;
+  m.wait_ns = p.wait_ns;
   return m;
 }
 
@@ -1270,7 +1272,7 @@ template <typename T, int LB, int D>
 static void launch_attn_fwd_tc(const BlkMmaParams& m, unsigned grid, cudaStream_t st) {
   constexpr size_t smem = blk_tc_fwd_smem<LB, D>();
   cudaFuncSetAttribute(blk_attn_fwd_tc_kernel<T, LB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  blk_attn_fwd_tc_kernel<T, LB, D><<<grid, kTcRows, smem, st>>>(m, m.status);
+  blk_attn_fwd_tc_kernel<T, LB, D><<<grid, kTcRows, smem, st>>>(m);
 }
 
 template <typename T>
@@ -1279,7 +1281,6 @@ void attn_fwd_mma(const BlkParams& p, cudaStream_t st) {
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.nb);
   if (p.use_tcgen05 && p.status != nullptr) {
     TA_PROFILE("blocked_attn_tc", st);
-    cudaMemsetAsync(p.status, 0, sizeof(int32_t), st);
     if (p.D == 64) {
       switch (p.Lb) {
         case 16: launch_attn_fwd_tc<T, 16, 64>(m, grid, st); break;
@@ -1485,7 +1486,6 @@ static BlkWs blk_fwd_ws(const BlkParams& p) {
   w.keys[0] = take(HB * p.P * 4); w.keys[1] = take(HB * p.P * 4);
   w.vals[0] = take(HB * p.P * 4); w.vals[1] = take(HB * p.P * 4);
   w.hist = take(HB * kRadix * tiles * 4);
-  w.dc = take(256);  // tensor-core status word
   w.total = off;
   return w;
 }

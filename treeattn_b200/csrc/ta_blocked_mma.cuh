@@ -93,7 +93,8 @@ struct BlkMmaParams {
   int32_t B, H, L, N, S, nb, causal;
   int64_t P, row0, row_total;
   float scale;
-  int32_t* status;         // tensor-core wait status (0 = ok), forward
+  volatile int32_t* status;  // tensor-core wait status (0 = ok), mapped host memory
+  uint64_t wait_ns;          // bound of one tensor-core mbarrier wait
 };
 
 template <int LB, int D>

@@ -16,8 +16,9 @@
 // descriptor: start >> 4 in [0,14), leading-byte offset >> 4 in [16,30), stride-byte offset
 // >> 4 in [32,46), version 1 in [46,48), layout type in [61,64) = 0 for no swizzle; instruction
 // descriptor: D format [4,6), A / B format [7,10) / [10,13), A / B major [15] / [16],
-// N >> 3 [17,23), M >> 4 [24,29)). Every mbarrier wait is bounded: on expiry the kernel records
-// an error code in the status word and stops issuing work.
+// N >> 3 [17,23), M >> 4 [24,29)). Every mbarrier wait is bounded: the CTA agrees on a
+// failure (__syncthreads_or), records it in the host-visible status word, waits once more
+// (bounded by kTcWaitNs) for the MMA it had issued, frees its TMEM and returns.
 #pragma once
 
 #include "ta_blocked_mma.cuh"
@@ -26,7 +27,7 @@ namespace ta {
 
 constexpr int kTcRows = 128;         // pairs per tile = MMA M = TMEM lanes
 constexpr int kTcCols = 256;         // TMEM columns allocated per CTA (S: Lb, O: D)
-constexpr uint64_t kTcWaitNs = 1000000000ull;  // an mbarrier wait gives up after 1 s
+constexpr uint64_t kTcWaitNs = 1000000000ull;  // default bound of one mbarrier wait: 1 s
 
 // Shared memory per CTA, at least 80 KB so that no more than two CTAs share an SM: their two
 // 256-column TMEM allocations then always fit the SM's 512 columns and tcgen05.alloc never
@@ -77,21 +78,30 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Wait for the mbarrier phase `parity`, at most kTcWaitNs; false if it never completed. The
+// Wait for the mbarrier phase `parity`, at most `limit_ns`; false if it never completed. The
 // warp is reconverged on return (the next tcgen05.ld is .sync.aligned).
-__device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity) {
+__device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = global_ns();
   bool done = false;
   while (!done) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, P1;\n\t}\n"
-        : "=r"(ok)
-        : "r"(mbar), "r"(parity)
-        : "memory");
+    if (limit_ns >= 1000) {  // try_wait may suspend the thread for a while before it answers
+      asm volatile(
+          "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+          "selp.b32 %0, 1, 0, P1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(mbar), "r"(parity)
+          : "memory");
+    } else {  // sub-microsecond bounds (tests of the status path) poll without suspending
+      asm volatile(
+          "{\n\t.reg .pred P1;\n\tmbarrier.test_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+          "selp.b32 %0, 1, 0, P1;\n\t}\n"
+          : "=r"(ok)
+          : "r"(mbar), "r"(parity)
+          : "memory");
+    }
     done = ok != 0;
-    if (!done && global_ns() - t0 > kTcWaitNs) break;
+    if (!done && global_ns() - t0 > limit_ns) break;
   }
   __syncwarp();
   return __all_sync(0xffffffffu, done);
@@ -120,7 +130,7 @@ __device__ __forceinline__ uint32_t kmaj_off(int r, int c, int cols) {
 }
 
 template <typename T, int LB, int D>
-__global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaParams p, int32_t* status) {
+__global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaParams p) {
   static_assert(LB % 16 == 0 && D % 16 == 0 && LB + D <= kTcCols, "tile shape");
   extern __shared__ __align__(128) unsigned char tc_smem[];
   unsigned char* s_q0 = tc_smem;                      // 2 x [128 x D] K-major
@@ -218,7 +228,8 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
                idS, kk > 0 ? 1u : 0u);
       tc_commit(mbar);
     }
-    if (!tc_wait(mbar, phase)) { failed = true; break; }
+    // the whole CTA leaves together when any warp's wait expired
+    if (__syncthreads_or(!tc_wait(mbar, phase, p.wait_ns))) { failed = true; break; }
     phase ^= 1u;
     tc_fence_after();
     // row max, then P = exp(s - max) (16-bit, K-major) and the row sum; the S row is read from
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
                idO, kk > 0 ? 1u : 0u);
       tc_commit(mbar);
     }
-    if (!tc_wait(mbar, phase)) { failed = true; break; }
+    if (__syncthreads_or(!tc_wait(mbar, phase, p.wait_ns))) { failed = true; break; }
     phase ^= 1u;
     tc_fence_after();
     // O row: every lane executes the same tcgen05.ld; only valid rows store
@@ -313,7 +324,14 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
     tc_fence_after();
   }
   cp_async_wait_0();
-  if (failed && tid == 0) atomicExch(status, 1);
+  if (failed) {
+    // let the MMA issued before the expired wait finish before its TMEM is freed
+    tc_wait(mbar, phase, kTcWaitNs);
+    if (tid == 0) {
+      *p.status = 1;
+      __threadfence_system();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

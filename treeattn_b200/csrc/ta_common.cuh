@@ -154,6 +154,67 @@ __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, const uint
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
+__device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+template <typename T> struct Mma16;
+template <> struct Mma16<__nv_bfloat16> {
+  __device__ __forceinline__ static void mma(float* c, const uint32_t* a, const uint32_t* b) { mma_bf16(c, a, b); }
+};
+template <> struct Mma16<__half> {
+  __device__ __forceinline__ static void mma(float* c, const uint32_t* a, const uint32_t* b) { mma_f16(c, a, b); }
+};
+
+__device__ __forceinline__ uint32_t word_of(const uint4& u, int j) {
+  return j == 0 ? u.x : (j == 1 ? u.y : (j == 2 ? u.z : u.w));
+}
+
+// Four dot products per query on the tensor cores, for a warp of eight 4-lane groups (one
+// query per group). Lane t of group g holds 16-byte chunks t, t+4, ... of its query's row
+// (`qv`) and of the four node rows its query's four paths visit (`kv[path]`). One m16n8k16
+// product per 16 features and pair of paths: A rows = (path pair, query) node rows, B columns
+// = the eight queries, both taking their k positions from the same (chunk, word) of each lane,
+// so row (query g, path t) times column g is the wanted dot (the other 7 columns are unused).
+// The wanted entries of group g sit on lane g/2 of that group; four shuffles hand path t's
+// logit to lane t. Products of 16-bit values are exact; sums accumulate in float32.
+template <typename T, int CPL>
+__device__ __forceinline__ float mma_path_dots(const uint4 (&qv)[CPL], const uint4 (&kv)[4][CPL],
+                                               int t4, unsigned gmask) {
+  // two accumulator sets (even / odd 16-feature steps) halve the dependent MMA chain
+  float d01[2][4] = {}, d23[2][4] = {};
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t b[2] = {word_of(qv[i], 2 * half), word_of(qv[i], 2 * half + 1)};
+      const uint32_t a01[4] = {word_of(kv[0][i], 2 * half), word_of(kv[1][i], 2 * half),
+                               word_of(kv[0][i], 2 * half + 1), word_of(kv[1][i], 2 * half + 1)};
+      const uint32_t a23[4] = {word_of(kv[2][i], 2 * half), word_of(kv[3][i], 2 * half),
+                               word_of(kv[2][i], 2 * half + 1), word_of(kv[3][i], 2 * half + 1)};
+      Mma16<T>::mma(d01[half], a01, b);
+      Mma16<T>::mma(d23[half], a23, b);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    d01[0][e] += d01[1][e];
+    d23[0][e] += d23[1][e];
+  }
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int odd = g & 1;
+  const int src = (lane & ~3) | (g >> 1);
+  const float p0 = __shfl_sync(gmask, odd ? d01[0][1] : d01[0][0], src, 32);
+  const float p1 = __shfl_sync(gmask, odd ? d01[0][3] : d01[0][2], src, 32);
+  const float p2 = __shfl_sync(gmask, odd ? d23[0][1] : d23[0][0], src, 32);
+  const float p3 = __shfl_sync(gmask, odd ? d23[0][3] : d23[0][2], src, 32);
+  return t4 == 0 ? p0 : (t4 == 1 ? p1 : (t4 == 2 ? p2 : p3));
+}
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
@@ -163,6 +224,20 @@ __device__ __forceinline__ uint4 ld16_stream(const void* p) {
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
+  return r;
+}
+// Bring the line holding `p` into L1 ahead of its load (no register is written).
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+// 16-byte load from a shared-memory address (explicit state space, so it always issues as a
+// shared-memory load).
+__device__ __forceinline__ uint4 lds16_sa(uint32_t saddr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(saddr));
   return r;
 }
 __device__ __forceinline__ uint4 lds16(const void* p) {
@@ -215,6 +290,22 @@ __device__ __forceinline__ void log_sigmoid_pair(float x, float& left, float& ri
   const float t = log1pf(expf(-fabsf(x)));
   left = fminf(0.0f, x) - t;
   right = fminf(0.0f, -x) - t;
+}
+
+// The same pair, also returning e = exp(-|x|).
+__device__ __forceinline__ void log_sigmoid_pair_e(float x, float& left, float& right, float& e) {
+  e = expf(-fabsf(x));
+  const float t = log1pf(e);
+  left = fminf(0.0f, x) - t;
+  right = fminf(0.0f, -x) - t;
+}
+
+// σ(-sgn x) for the direction taken (sgn = +1 for direction 0): the probability of the branch
+// not taken, exp(min(0, ±x)) / (1 + e) with e = exp(-|x|), i.e. 1 / (1 + e) when the branch not
+// taken has the non-negative argument and e / (1 + e) otherwise.
+__device__ __forceinline__ float branch_not_taken_prob(float x, int dir, float e) {
+  const bool big = dir ? (x >= 0.0f) : (x <= 0.0f);  // argument of the branch not taken >= 0
+  return (big ? 1.0f : e) / (1.0f + e);
 }
 
 __device__ __forceinline__ float clamp_logit(float x, float m) {

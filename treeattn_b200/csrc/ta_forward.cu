@@ -18,6 +18,9 @@
 
 #include <stdio.h>
 
+#include <atomic>
+#include <type_traits>
+
 #include "ta_common.cuh"
 #include "ta_rng.cuh"
 
@@ -56,11 +59,105 @@ struct FwdParams {
   const int32_t* corrected;  // kCausalTail: levels the prefix kernel already sampled, per query
 };
 
+// After the walk: the paths' log-probabilities and leaves of this group's query sit in
+// s_lp / s_leaf. Writes weights (softmax over the paths, or the raw log-probabilities in the
+// sample-only modes), leaves, packed direction bits and out = sum_s w_s v[leaf_s].
 template <typename T, int CPL>
-__global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
+__device__ __forceinline__ void fwd_finish(const FwdParams& p, bool active, int l, int b, int h,
+                                           int t4, unsigned gmask, float* s_lp,
+                                           const int32_t* s_leaf, uint32_t j0, bool replay,
+                                           bool value_sum = true) {
   using E = Elem<T>;
   constexpr int EPC = E::EPC;
-  constexpr int NE = CPL * EPC;  // elements of a row held by one lane
+  constexpr int NE = CPL * EPC;
+  const uint32_t K = (uint32_t)p.N - 1u;
+  __syncwarp(gmask);
+  if (!active) return;  // past the last tensor-core product: idle groups stop here
+  if (p.mode == kSampleOnly || p.mode == kReplay) {
+    for (int s = t4; s < p.S; s += 4) {
+      p.weights[j0 + s] = s_lp[s];
+      p.leaf[j0 + s] = s_leaf[s];
+    }
+  } else {
+    // softmax over the S paths: lp - logsumexp(lp), exp
+    float m = -INFINITY;
+    for (int s = t4; s < p.S; s += 4) m = fmaxf(m, s_lp[s]);
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 1, 4));
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 2, 4));
+    float sum = 0.0f;
+    for (int s = 0; s < p.S; ++s) sum += expf(s_lp[s] - m);  // same order on every lane
+    const float lse = m + logf(sum);
+    __syncwarp(gmask);
+    for (int s = t4; s < p.S; s += 4) {
+      const float w = expf(s_lp[s] - lse);
+      s_lp[s] = w;
+      if (p.weights) p.weights[j0 + s] = w;
+      if (p.leaf) p.leaf[j0 + s] = s_leaf[s];
+    }
+    __syncwarp(gmask);
+  }
+  if (p.packed != nullptr && !replay) {
+    const int64_t base_node = ((int64_t)1 << p.log_n) - 1;
+    for (int s = t4; s < p.S; s += 4) {
+      const uint32_t bits = (uint32_t)((int64_t)s_leaf[s] + K - base_node);
+      for (int pb = 0; pb < p.pbytes; ++pb) {
+        uint32_t byte = 0;
+        for (int d = pb * 8; d < min(p.log_n, pb * 8 + 8); ++d)
+          byte |= ((bits >> (p.log_n - 1 - d)) & 1u) << (d & 7);
+        p.packed[(int64_t)(j0 + s) * p.pbytes + pb] = (uint8_t)byte;
+      }
+    }
+  }
+  if ((p.mode != kFull && p.mode != kCausalTail) || !value_sum) return;
+
+  // out[l,b,h] = sum_s w_s v[leaf_s]
+  float acc[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
+  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
+  const uint32_t vstride = (uint32_t)(p.vs * (int64_t)sizeof(T));
+  // rows are fetched four paths at a time (all loads in flight together), then summed in
+  // path order
+  for (int s0 = 0; s0 < p.S; s0 += 4) {
+    uint4 vr[4][CPL];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int s = s0 + t < p.S ? s0 + t : p.S - 1;
+      int32_t lf = s_leaf[s];
+      lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+      const char* vrow = vbase + (uint64_t)(uint32_t)lf * vstride;
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        const int c = i * 4 + t4;
+        vr[t][i] = c < p.nchunks ? ldg16(vrow + c * 16) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      if (s0 + t >= p.S) break;
+      const float w = s_lp[s0 + t];
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        float vf[EPC];
+        E::unpack(vr[t][i], vf);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w, vf[e], acc[i * EPC + e]);
+      }
+    }
+  }
+  char* orow = p.out + ((int64_t)l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = i * 4 + t4;
+    if (c < p.nchunks) st16(orow + c * 16, E::pack(acc + i * EPC));
+  }
+}
+
+// MMA: the per-level dot products of the four paths in flight run as m16n8k16 tensor-core
+// products over the warp's eight queries (mma_path_dots); 16-bit inputs with head_dim a
+// multiple of 32 and non-causal modes only (every lane of a warp walks the same levels).
+template <typename T, int CPL, bool MMA>
+__global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
   extern __shared__ float smem[];
 
   const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
@@ -70,7 +167,10 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
   const int h = bh - b * p.H;
   const int g = threadIdx.x >> 2;
   const int t4 = threadIdx.x & 3;
-  const int l = lt * kFwdGroups + g;
+  const bool active = lt * kFwdGroups + g < p.L;
+  // the tensor-core dot needs every lane of the warp: an idle group walks the last query
+  // and stores nothing
+  const int l = active ? lt * kFwdGroups + g : p.L - 1;
   const unsigned gmask = 0xFu << (threadIdx.x & 28);
   const int row_bytes = p.nchunks * 16;
   const int top_rows = (1 << p.top_levels) - 1;
@@ -84,7 +184,7 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
     cp_async_wait_0();
     __syncthreads();
   }
-  if (l >= p.L) return;  // whole group leaves together
+  if (!MMA && !active) return;  // whole group leaves together
 
   const uint32_t K = (uint32_t)p.N - 1u;
   const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
@@ -174,34 +274,59 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
           }
         }
       }
-      float dot[4];
+      float mine;
+      if constexpr (MMA) {
+        mine = mma_path_dots<T, CPL>(qraw, raw, t4, 0xffffffffu);
+      } else {
+        float dot[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        dot[t] = 0.0f;
+        for (int t = 0; t < 4; ++t) {
+          dot[t] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) dot[t] = Dot<T>::chunk(qraw[i], raw[t][i], dot[t]);
+          for (int i = 0; i < CPL; ++i) dot[t] = Dot<T>::chunk(qraw[i], raw[t][i], dot[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          dot[t] += __shfl_xor_sync(gmask, dot[t], 1, 4);
+          dot[t] += __shfl_xor_sync(gmask, dot[t], 2, 4);
+        }
+        mine = t4 == 0 ? dot[0] : (t4 == 1 ? dot[1] : (t4 == 2 ? dot[2] : dot[3]));
       }
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        dot[t] += __shfl_xor_sync(gmask, dot[t], 1, 4);
-        dot[t] += __shfl_xor_sync(gmask, dot[t], 2, 4);
-      }
-      const float mine = t4 == 0 ? dot[0] : (t4 == 1 ? dot[1] : (t4 == 2 ? dot[2] : dot[3]));
-      float lpl, lpr;
-      log_sigmoid_pair(clamp_logit(mine, p.max_logit), lpl, lpr);
+      const float x = clamp_logit(mine, p.max_logit);
       int dir = 0;
       if (t4 < ns) {
         if (replay) {
           const uint8_t byte = p.packed[(int64_t)jm * p.pbytes + (depth >> 3)];
           dir = (byte >> (depth & 7)) & 1;
         } else {
+          // The reference's decision lpr + gr > lpl + gl (ties left). Since lpl - lpr = x
+          // exactly in real arithmetic, it is gr - gl > x unless the two sides are within
+          // float32 rounding of each other; only then are the log-sigmoids evaluated here,
+          // so the next level's row address does not wait for them.
           const float gl = g_cur.x, gr = g_cur.y;
-          dir = (lpr + gr > lpl + gl) ? 1 : 0;
+          const float diff = gr - gl;
+          const float guard = 1e-5f * (fabsf(x) + fabsf(gl) + fabsf(gr) + 2.0f);
+          if (fabsf(diff - x) > guard) {
+            dir = diff > x ? 1 : 0;
+          } else {
+            float a, b;
+            log_sigmoid_pair(x, a, b);
+            dir = (b + gr > a + gl) ? 1 : 0;
+          }
         }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int d = __shfl_sync(gmask, dir, t, 4);
+        node[t] = 2u * node[t] + 1u + (uint32_t)d;
+      }
+      // log-probability bookkeeping, off the walk's dependency chain
+      float lpl, lpr, e;
+      log_sigmoid_pair_e(x, lpl, lpr, e);
+      if (t4 < ns) {
         lp += dir ? lpr : lpl;
-        if (sig_row0 != nullptr) {
-          // σ(-sgn s) = exp(log-prob of the branch not taken)
-          const float sv = expf(dir ? lpl : lpr);
+        if (sig_row0 != nullptr && active) {
+          const float sv = branch_not_taken_prob(x, dir, e);
           const int slot = depth & 3;
           sig4[0] = slot == 0 ? sv : sig4[0];
           sig4[1] = slot == 1 ? sv : sig4[1];
@@ -213,11 +338,6 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
           }
         }
       }
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int d = __shfl_sync(gmask, dir, t, 4);
-        node[t] = 2u * node[t] + 1u + (uint32_t)d;
-      }
     }
     if (t4 < ns) {
       const uint32_t nm = t4 == 0 ? node[0] : (t4 == 1 ? node[1] : (t4 == 2 ? node[2] : node[3]));
@@ -225,116 +345,215 @@ __global__ void __launch_bounds__(kFwdThreads) fwd_kernel(const FwdParams p) {
       s_leaf[s0 + t4] = (int32_t)(nm - K);
     }
   }
-  __syncwarp(gmask);
-
-  if (p.mode == kSampleOnly || p.mode == kReplay) {
-    for (int s = t4; s < p.S; s += 4) {
-      p.weights[j0 + s] = s_lp[s];
-      p.leaf[j0 + s] = s_leaf[s];
-    }
-  } else {
-    // softmax over the S paths: lp - logsumexp(lp), exp
-    float m = -INFINITY;
-    for (int s = t4; s < p.S; s += 4) m = fmaxf(m, s_lp[s]);
-    m = fmaxf(m, __shfl_xor_sync(gmask, m, 1, 4));
-    m = fmaxf(m, __shfl_xor_sync(gmask, m, 2, 4));
-    float sum = 0.0f;
-    for (int s = 0; s < p.S; ++s) sum += expf(s_lp[s] - m);  // same order on every lane
-    const float lse = m + logf(sum);
-    __syncwarp(gmask);
-    for (int s = t4; s < p.S; s += 4) {
-      const float w = expf(s_lp[s] - lse);
-      s_lp[s] = w;
-      if (p.weights) p.weights[j0 + s] = w;
-      if (p.leaf) p.leaf[j0 + s] = s_leaf[s];
-    }
-    __syncwarp(gmask);
-  }
-  if (p.packed != nullptr && !replay) {
-    const int64_t base_node = ((int64_t)1 << p.log_n) - 1;
-    for (int s = t4; s < p.S; s += 4) {
-      const uint32_t bits = (uint32_t)((int64_t)s_leaf[s] + K - base_node);
-      for (int pb = 0; pb < p.pbytes; ++pb) {
-        uint32_t byte = 0;
-        for (int d = pb * 8; d < min(p.log_n, pb * 8 + 8); ++d)
-          byte |= ((bits >> (p.log_n - 1 - d)) & 1u) << (d & 7);
-        p.packed[(int64_t)(j0 + s) * p.pbytes + pb] = (uint8_t)byte;
-      }
-    }
-  }
-  if (p.mode != kFull && p.mode != kCausalTail) return;
-
-  // out[l,b,h] = sum_s w_s v[leaf_s]
-  float acc[NE];
-#pragma unroll
-  for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
-  const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-  const uint32_t vstride = (uint32_t)(p.vs * (int64_t)sizeof(T));
-  for (int s = 0; s < p.S; ++s) {
-    const float w = s_lp[s];
-    int32_t lf = s_leaf[s];
-    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-    const char* vrow = vbase + (uint64_t)(uint32_t)lf * vstride;
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      const int c = i * 4 + t4;
-      if (c < p.nchunks) {
-        float vf[EPC];
-        E::unpack(ldg16(vrow + c * 16), vf);
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w, vf[e], acc[i * EPC + e]);
-      }
-    }
-  }
-  char* orow = p.out + ((int64_t)l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T);
-#pragma unroll
-  for (int i = 0; i < CPL; ++i) {
-    const int c = i * 4 + t4;
-    if (c < p.nchunks) st16(orow + c * 16, E::pack(acc + i * EPC));
-  }
+  fwd_finish<T, CPL>(p, active, l, b, h, t4, gmask, s_lp, s_leaf, j0, replay);
 }
 
-// out = sum_s w_s v[clamp(leaf_s)] for externally supplied leaves / weights.
+// Streamlined non-causal sampler (kFull / kSampleOnly) for the common case: 16-bit inputs,
+// head_dim a multiple of 32 (every lane holds CPL whole 16-byte chunks), a multiple of 4
+// paths, noise prefilled by ta_gumbel_fill. Same decomposition and results as fwd_kernel,
+// with the per-level work cut to what the walk needs: unconditional row loads, the four
+// paths' logits as tensor-core products (mma_path_dots), the decision from the sign of
+// (g_R - g_L) - s with an exact fallback near ties, one ballot for the group's four
+// directions, and the log-probability bookkeeping off the dependency chain.
 template <typename T, int CPL>
-__global__ void __launch_bounds__(kFwdThreads) value_sum_kernel(const FwdParams p) {
-  using E = Elem<T>;
-  constexpr int EPC = E::EPC;
-  constexpr int NE = CPL * EPC;
+__global__ void __launch_bounds__(kFwdThreads, 2) fwd_fast_kernel(const FwdParams p) {
+  constexpr int RB = CPL * 64;  // row bytes
+  extern __shared__ float smem[];
   const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
   const int bh = blockIdx.x / ltiles;
   const int lt = blockIdx.x - bh * ltiles;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
+  const int lane = threadIdx.x & 31;
   const int g = threadIdx.x >> 2;
   const int t4 = threadIdx.x & 3;
-  const int l = lt * kFwdGroups + g;
+  const bool active = lt * kFwdGroups + g < p.L;
+  const int l = active ? lt * kFwdGroups + g : p.L - 1;
+  const unsigned gmask = 0xFu << (threadIdx.x & 28);
+  const int top_rows = (1 << p.top_levels) - 1;
+  char* s_tree = reinterpret_cast<char*>(smem);
+  float* s_lp = reinterpret_cast<float*>(s_tree + (size_t)top_rows * RB) + g * p.S;
+  int32_t* s_leaf = reinterpret_cast<int32_t*>(s_lp - g * p.S + kFwdGroups * p.S) + g * p.S;
+  const char* kbase = p.k + ((int64_t)b * p.kb + (int64_t)h * p.kh) * sizeof(T);
+  const uint32_t kstride = (uint32_t)(p.ks * (int64_t)sizeof(T));
+  {
+    constexpr int PPR = RB / 16;
+    const int total = top_rows * PPR;
+    for (int i = threadIdx.x; i < total; i += kFwdThreads) {
+      const int r = i / PPR, c = i - r * PPR;
+      cp_async16(s_tree + r * RB + c * 16, kbase + (uint64_t)r * kstride + c * 16);
+    }
+    cp_async_commit();
+    cp_async_wait_0();
+    __syncthreads();
+  }
+  const uint32_t K = (uint32_t)p.N - 1u;
+  const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
+  float* sig_row0 = p.sig ? p.sig + (((int64_t)b * p.H + h) * p.P + (int64_t)l * p.S) * p.sig_stride
+                          : nullptr;
+  uint4 qraw[CPL];
+  {
+    const char* qrow = p.q + ((int64_t)l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * sizeof(T) + t4 * 16;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) qraw[i] = ldg16(qrow + i * 64);
+  }
+  const uint64_t M = 2ull * (uint64_t)p.L * p.B * p.H * p.S;  // one depth of noise
+  const uint32_t s_row0 = (uint32_t)__cvta_generic_to_shared(s_tree) + t4 * 16;
+  const char* k_row0 = kbase + t4 * 16;
+  for (int s0 = 0; s0 < p.S; s0 += 4) {
+    uint32_t node[4] = {0u, 0u, 0u, 0u};
+    float lp = 0.0f;
+    float sig4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float* gp = p.gumbels + 2ull * (j0 + s0 + t4);
+    // the noise addresses depend on no decision: each level's pair is requested two levels
+    // before the walk reaches it
+    float2 g_next = __ldg(reinterpret_cast<const float2*>(gp));
+    float2 g_next2 = p.log_n > 1 ? __ldg(reinterpret_cast<const float2*>(gp + M)) : make_float2(0.0f, 0.0f);
+    uint4 raw[4][CPL];
+    // the rows of level `depth` (all four paths' nodes are known to every lane of the group)
+    auto load_rows = [&](int depth) {
+      if (depth < p.top_levels) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t row = s_row0 + node[t] * (uint32_t)RB;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) raw[t][i] = lds16_sa(row + i * 64);
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const char* row = k_row0 + (uint64_t)node[t] * kstride;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) raw[t][i] = ldg16(row + i * 64);
+        }
+      }
+    };
+    load_rows(0);
+    for (int depth = 0; depth < p.log_n; ++depth) {
+      const float2 g_cur = g_next;
+      g_next = g_next2;
+      if (depth + 2 < p.log_n) g_next2 = __ldg(reinterpret_cast<const float2*>(gp + (uint64_t)(depth + 2) * M));
+      const float x = clamp_logit(mma_path_dots<T, CPL>(qraw, raw, t4, 0xffffffffu), p.max_logit);
+      // the reference's lpr + gr > lpl + gl (ties left) is gr - gl > x (lpl - lpr = x) unless
+      // the two sides are within float32 rounding of each other; only then evaluate it as is
+      const float gl = g_cur.x, gr = g_cur.y;
+      const float diff = gr - gl;
+      const float guard = 1e-5f * (fabsf(x) + fabsf(gl) + fabsf(gr) + 2.0f);
+      int dir;
+      if (fabsf(diff - x) > guard) {
+        dir = diff > x ? 1 : 0;
+      } else {
+        float a, c;
+        log_sigmoid_pair(x, a, c);
+        dir = (c + gr > a + gl) ? 1 : 0;
+      }
+      const uint32_t bits = __ballot_sync(0xffffffffu, dir) >> (lane & 28);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) node[t] = 2u * node[t] + 1u + ((bits >> t) & 1u);
+      // the next level's rows are requested before this level's bookkeeping runs
+      if (depth + 1 < p.log_n) load_rows(depth + 1);
+      float lpl, lpr, e;
+      log_sigmoid_pair_e(x, lpl, lpr, e);
+      lp += dir ? lpr : lpl;
+      if (sig_row0 != nullptr) {
+        const float sv = branch_not_taken_prob(x, dir, e);
+        const int slot = depth & 3;
+        sig4[0] = slot == 0 ? sv : sig4[0];
+        sig4[1] = slot == 1 ? sv : sig4[1];
+        sig4[2] = slot == 2 ? sv : sig4[2];
+        sig4[3] = slot == 3 ? sv : sig4[3];
+        if ((slot == 3 || depth == p.log_n - 1) && active) {
+          float* dst = sig_row0 + (int64_t)(s0 + t4) * p.sig_stride + (depth & ~3);
+          *reinterpret_cast<float4*>(dst) = make_float4(sig4[0], sig4[1], sig4[2], sig4[3]);
+        }
+      }
+    }
+    const uint32_t nm = t4 == 0 ? node[0] : (t4 == 1 ? node[1] : (t4 == 2 ? node[2] : node[3]));
+    s_lp[s0 + t4] = lp;
+    s_leaf[s0 + t4] = (int32_t)(nm - K);
+    if (p.mode == kFull) {
+      // the value rows the final sum gathers: start pulling them into L2 now
+      const char* vrow = p.v + ((int64_t)(nm - K) * p.vs + (int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
+      prefetch_l2(vrow);
+      if (RB > 128) prefetch_l2(vrow + 128);
+    }
+  }
+  // out is summed by value_gather_kernel, launched next at a higher occupancy than this walk
+  fwd_finish<T, CPL>(p, active, l, b, h, t4, gmask, s_lp, s_leaf, j0, false, false);
+}
+
+// out = sum_s w_s v[clamp(leaf_s)] from leaves / weights in HBM (after the sampler, or supplied
+// by the caller). Eight lanes per query, each holding C8 16-byte chunks of the row, four paths'
+// rows in flight at a time; the sum runs in path order, as in the fused finish, so both give
+// the same bits. Few registers: many warps per SM hide the gathers' latency.
+constexpr int kGatherThreads = 256;
+constexpr int kGatherQueries = kGatherThreads / 8;
+
+template <typename T, int C8>
+__global__ void __launch_bounds__(kGatherThreads, 4) value_gather_kernel(const FwdParams p) {
+  using E = Elem<T>;
+  constexpr int EPC = E::EPC;
+  const int ltiles = (p.L + kGatherQueries - 1) / kGatherQueries;
+  const int bh = blockIdx.x / ltiles;
+  const int lt = blockIdx.x - bh * ltiles;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int g = threadIdx.x >> 3;
+  const int t8 = threadIdx.x & 7;
+  const int l = lt * kGatherQueries + g;
   if (l >= p.L) return;
   const uint32_t j0 = (uint32_t)(((int64_t)l * p.B + b) * p.H + h) * (uint32_t)p.S;
-  float acc[NE];
+  float acc[C8 * EPC];
 #pragma unroll
-  for (int e = 0; e < NE; ++e) acc[e] = 0.0f;
+  for (int e = 0; e < C8 * EPC; ++e) acc[e] = 0.0f;
   const char* vbase = p.v + ((int64_t)b * p.vb + (int64_t)h * p.vh) * sizeof(T);
-  for (int s = 0; s < p.S; ++s) {
-    const float w = p.weights[j0 + s];
-    int64_t lf = p.leaf[j0 + s];
-    lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
-    const char* vrow = vbase + lf * p.vs * (int64_t)sizeof(T);
+  const uint32_t vstride = (uint32_t)(p.vs * (int64_t)sizeof(T));
+  for (int s0 = 0; s0 < p.S; s0 += 4) {
+    uint4 vr[4][C8];
+    float w[4];
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      const int c = i * 4 + t4;
-      if (c < p.nchunks) {
+    for (int t = 0; t < 4; ++t) {
+      const int s = s0 + t < p.S ? s0 + t : p.S - 1;
+      w[t] = s0 + t < p.S ? p.weights[j0 + s] : 0.0f;
+      int32_t lf = p.leaf[j0 + s];
+      lf = lf < 0 ? 0 : (lf >= p.N ? p.N - 1 : lf);
+      const char* vrow = vbase + (uint64_t)(uint32_t)lf * vstride;
+#pragma unroll
+      for (int i = 0; i < C8; ++i) {
+        const int c = i * 8 + t8;
+        vr[t][i] = c < p.nchunks ? ldg16(vrow + c * 16) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      if (s0 + t >= p.S) break;
+#pragma unroll
+      for (int i = 0; i < C8; ++i) {
         float vf[EPC];
-        E::unpack(ldg16(vrow + c * 16), vf);
+        E::unpack(vr[t][i], vf);
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w, vf[e], acc[i * EPC + e]);
+        for (int e = 0; e < EPC; ++e) acc[i * EPC + e] = fmaf(w[t], vf[e], acc[i * EPC + e]);
       }
     }
   }
   char* orow = p.out + ((int64_t)l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh) * sizeof(T);
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) {
-    const int c = i * 4 + t4;
+  for (int i = 0; i < C8; ++i) {
+    const int c = i * 8 + t8;
     if (c < p.nchunks) st16(orow + c * 16, E::pack(acc + i * EPC));
+  }
+}
+
+template <typename T>
+static void launch_value_gather(const FwdParams& p, cudaStream_t st) {
+  const int ltiles = (p.L + kGatherQueries - 1) / kGatherQueries;
+  const dim3 grid((unsigned)(ltiles * p.B * p.H));
+  TA_PROFILE("value_sum", st);
+  switch ((p.nchunks + 7) / 8) {
+    case 1: value_gather_kernel<T, 1><<<grid, kGatherThreads, 0, st>>>(p); break;
+    case 2: value_gather_kernel<T, 2><<<grid, kGatherThreads, 0, st>>>(p); break;
+    case 3: value_gather_kernel<T, 3><<<grid, kGatherThreads, 0, st>>>(p); break;
+    default: value_gather_kernel<T, 4><<<grid, kGatherThreads, 0, st>>>(p); break;
   }
 }
 
@@ -445,22 +664,74 @@ int check_shape(const ta_shape* s, bool need_pow2) {
   return TA_OK;
 }
 
+namespace {
+int g_tensor_dots = 1;  // forward dot products on mma.sync where the shape allows
+}
+
+template <typename T, int CPL, bool MMA>
+static void launch_fwd_kernel(const FwdParams& p, dim3 grid, size_t smem, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_set{0};  // per device: the attribute is set once
+  if (smem > 48 * 1024) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+      cudaFuncSetAttribute(fwd_kernel<T, CPL, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kTreeSmemBudget + kFwdGroups * 256 * 8);
+      attr_set.fetch_or(bit);
+    }
+  }
+  fwd_kernel<T, CPL, MMA><<<grid, kFwdThreads, smem, st>>>(p);
+}
+
+template <typename T, int CPL>
+static void launch_fast_kernel(const FwdParams& p, dim3 grid, size_t smem, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_set{0};
+  if (smem > 48 * 1024) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+      cudaFuncSetAttribute(fwd_fast_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kTreeSmemBudget + kFwdGroups * 256 * 8);
+      attr_set.fetch_or(bit);
+    }
+  }
+  fwd_fast_kernel<T, CPL><<<grid, kFwdThreads, smem, st>>>(p);
+}
+
 template <typename T, int CPL>
 static void launch_fwd(const FwdParams& p, cudaStream_t st, bool value_only) {
   const int ltiles = (p.L + kFwdGroups - 1) / kFwdGroups;
   const dim3 grid((unsigned)(ltiles * p.B * p.H));
   if (value_only) {
-    TA_PROFILE("value_sum", st);
-    value_sum_kernel<T, CPL><<<grid, kFwdThreads, 0, st>>>(p);
+    launch_value_gather<T>(p, st);
     return;
   }
   const size_t smem = (size_t)kFwdGroups * p.S * 8 +
                       (size_t)((1 << p.top_levels) - 1) * p.nchunks * 16;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(fwd_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (g_tensor_dots && p.nchunks == 4 * CPL && p.mode != kCausalTail) {
+      if (CPL <= 4 && (p.mode == kFull || p.mode == kSampleOnly) && p.gumbels != nullptr &&
+          p.S % 4 == 0 && p.weights != nullptr && p.leaf != nullptr) {
+        {
+          TA_PROFILE(p.mode == kFull ? "fwd_walk" : "sample_paths", st);
+          launch_fast_kernel<T, (CPL <= 4 ? CPL : 4)>(p, grid, smem, st);
+        }
+        if (p.mode == kFull) launch_value_gather<T>(p, st);
+        return;
+      }
+    }
+  }
   TA_PROFILE(p.mode == kFull ? "fwd_fused" : p.mode == kSampleOnly ? "sample_paths"
              : p.mode == kCausalTail ? "causal_tail" : "replay_paths", st);
-  fwd_kernel<T, CPL><<<grid, kFwdThreads, smem, st>>>(p);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (g_tensor_dots && p.nchunks == 4 * CPL && p.mode != kCausalTail) {
+      launch_fwd_kernel<T, CPL, true>(p, grid, smem, st);
+      return;
+    }
+  }
+  launch_fwd_kernel<T, CPL, false>(p, grid, smem, st);
 }
 
 template <typename T>
@@ -694,6 +965,12 @@ extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, const ta_shar
       (float*)out, (uint32_t)local, sd, rng->seed,
       rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
   return check_launch("gumbel fill (shard)");
+}
+
+extern "C" int32_t ta_forward_set_tensor_dots(int32_t enable) {
+  const int32_t old = g_tensor_dots;
+  g_tensor_dots = enable ? 1 : 0;
+  return old;
 }
 
 extern "C" int32_t ta_branch_prob_stride(int64_t num_leaves) {
