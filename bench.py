@@ -15,8 +15,9 @@ every rank runs its own batch element with no data-path collective (weak scaling
 timed region is bracketed by barriers and the max over ranks is reported.
 
 ``--impl reference`` times the CPU oracle (numpy restatement of the reference, forked over
-all host cores by head) on a bounded sample of the same workload and extrapolates to a full
-step. Rank 0 prints one JSON line.
+all host cores by head) over whole steps of a subset of the heads (every query, the full
+tree), sized so that the run takes a few minutes; throughput is quoted for the full config.
+Rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -54,15 +55,19 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-fa2", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the config-3 (head-sharded generalised tree) and config-4 "
+                        "(sequence-parallel causal) records of the default line")
     p.add_argument("--fanout", type=int, default=2)
     p.add_argument("--leaf-block", type=int, default=64)
     p.add_argument("--causal", action="store_true")
     p.add_argument("--dtype", choices=["bf16", "f16"], default="bf16")
-    p.add_argument("--mode", choices=["shard", "sp", "blocked"], default="shard",
+    p.add_argument("--mode", choices=["shard", "sp", "blocked", "sweep"], default="shard",
                    help="shard: (batch, head)-sharded headline workload; sp: sequence-parallel "
                         "causal long context (B=1, S=65536, H=32, d=128, 16 paths unless overridden); "
                         "blocked: generalised fanout / leaf-block tree (B=4, S=4096, H=16, d=128, "
-                        "fanout 2, leaf block 64, 8 paths: the single-B200 benchmark config)")
+                        "fanout 2, leaf block 64, 8 paths: the single-B200 benchmark config); "
+                        "sweep: the attn-bench-style sweep of config 5 against FA2")
     return p.parse_args()
 
 
@@ -150,6 +155,166 @@ def algorithmic_bytes(kernel: str, B, S, H, D, P, elt, launches_per_step):
         "tree_build_bwd": (B * S * H * D * 4 + rows) / max(1, launches_per_step),
     }
     return table.get(kernel)
+
+
+# ---------------------------------------------------------------------------------------
+# shared timing helpers
+# ---------------------------------------------------------------------------------------
+def _barrier(world, dev):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+
+def _timed(step, steps, warmup, world, dev):
+    """`warmup` untimed steps, then `steps` steps bracketed by barrier + synchronize and timed
+    with CUDA events on the current stream; the max over ranks, in ms per step."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        step()
+    _barrier(world, dev)
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    _barrier(world, dev)
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    return ms / steps
+
+
+def _fa2_ms(shape, dtype, causal, steps, warmup, world, dev, sd=1.0):
+    """Dense FlashAttention-2 fwd+bwd (flash_attn library, a comparator) on this rank's bshd
+    shape; max over ranks in ms per step, or None when flash_attn is not importable."""
+    import torch
+    try:
+        from flash_attn import flash_attn_func
+    except Exception:  # noqa: BLE001 - a comparator only
+        return None
+    g = torch.Generator(device=dev).manual_seed(7)
+    q, k, v, go = (torch.randn(*shape, device=dev, generator=g).mul(sd).to(dtype) for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        flash_attn_func(q, k, v, causal=causal).backward(go)
+
+    return _timed(step, steps, warmup, world, dev)
+
+
+def _kernels(prof, steps):
+    total = sum(t for _, t in prof.values()) or 1.0
+    return {k_: {"launches_per_step": c / steps, "ms_per_step": t / steps, "share": t / total}
+            for k_, (c, t) in sorted(prof.items(), key=lambda x: -x[1][1])}
+
+
+def record_c3(args, world, rank, dev):
+    """B=8, S=8192, H=32, d=64, fp16 N(0, 0.5), fanout 4, leaf block 128,
+    8 paths, causal; the fixed global problem is head-sharded over the ranks (strong scaling,
+    no collective: rank r runs heads [r H/N, (r+1) H/N) with that slice of the global noise)."""
+    import torch
+    from treeattn_b200 import ops
+    from treeattn_b200.blocked import blocked_tree_attention
+    from treeattn_b200.sharding import shard_for_rank
+
+    B, S, H, D, P, f, Lb = 8, 8192, 32, 64, 8, 4, 128
+    if H % world:
+        return {"skipped": f"H={H} not divisible by {world} ranks"}
+    shard = shard_for_rank(B, H, rank, world, "head") if world > 1 else None
+    hl = H // world
+    gen = torch.Generator(device=dev).manual_seed(3000 + rank)
+    q, k, v, go = (torch.randn(B, S, hl, D, device=dev, generator=gen).mul(0.5).to(torch.float16)
+                   for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        torch.manual_seed(0)
+        blocked_tree_attention(q, k, v, True, None, num_samples=P, fanout=f, leaf_block=Lb,
+                               shard=shard).backward(go)
+
+    ops.profile_enable(True)
+    ms = _timed(step, args.steps, args.warmup, world, dev)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    fa2 = None if args.no_fa2 else _fa2_ms((B, S, hl, D), torch.float16, True, args.steps,
+                                            args.warmup, world, dev, 0.5)
+    rec = {"config": {"workload": "generalised tree (fanout 4, leaf block 128), causal", "batch": B,
+                      "seq_len": S, "heads": H, "head_dim": D, "num_samples": P, "fanout": f,
+                      "leaf_block": Lb, "dtype": "f16", "data": "N(0, 0.5)",
+                      "parallelism": f"head-sharded x{world} ({hl} heads per GPU), no collective"},
+           "scaling": "strong", "value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps)}
+    if fa2 is not None:
+        rec["fa2"] = {"value": B * S / (fa2 / 1e3), "unit": "tokens/s", "ms_per_step": fa2,
+                      "what": "flash_attn_func dense causal fwd+bwd on each rank's head slice"}
+    return rec
+
+
+def record_c4(args, world, rank, dev):
+    """B=1, S=65536, H=32, d=128, bf16, 16 paths, causal; the sequence is
+    split evenly over the ranks (sequence parallel, strong scaling); one rank runs the plain
+    causal op."""
+    import torch
+    from treeattn_b200 import ops
+    import treeattn_b200 as ta
+    from treeattn_b200.sequence_parallel import sp_tree_attention
+
+    B, S, H, D, P = 1, 65536, 32, 128, 16
+    n = S // world
+    gen = torch.Generator(device=dev).manual_seed(4000)
+    full = [torch.randn(B, S, H, D, device=dev, generator=gen).to(torch.bfloat16) for _ in range(4)]
+    sl = slice(rank * n, (rank + 1) * n)
+    q, k, v, go = (t[:, sl].contiguous() for t in full)
+    del full
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        torch.manual_seed(0)
+        if world > 1:
+            out = sp_tree_attention(q, k, v, True, num_samples=P)
+        else:
+            out = ta.tree_attention(q, k, v, True, None, num_samples=P)
+        out.backward(go)
+
+    ops.profile_enable(True)
+    ms = _timed(step, args.steps, args.warmup, world, dev)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    rec = {"config": {"workload": "stochastic tree attention, causal (exact prefix + corrected "
+                                  "sampler)", "batch": B, "seq_len": S, "heads": H, "head_dim": D,
+                      "num_samples": P, "dtype": "bf16",
+                      "parallelism": f"sequence-parallel x{world}: NCCL all-gather of K/V, "
+                                     "reduce-scatter of dK/dV" if world > 1 else "one GPU"},
+           "scaling": "strong", "value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps)}
+    if world == 1 and not args.no_fa2:
+        fa2 = _fa2_ms((B, S, H, D), torch.bfloat16, True, 2, 1, world, dev)
+        if fa2 is not None:
+            rec["fa2"] = {"value": B * S / (fa2 / 1e3), "unit": "tokens/s", "ms_per_step": fa2,
+                          "what": "flash_attn_func dense causal fwd+bwd, whole sequence on one GPU "
+                                  "(1 warm-up, 2 timed steps)"}
+    del q, k, v, go
+    torch.cuda.empty_cache()
+    return rec
 
 
 # ---------------------------------------------------------------------------------------
@@ -284,6 +449,14 @@ def run_ours(args):
                "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
                "ms_per_step": ems / args.steps}
 
+    # FA2 beside every N (each rank its own batch element), then the configs 3 and 4 records
+    fa2_ms = None if args.no_fa2 else _fa2_ms((B, S, H, D), dtype, False, args.steps, args.warmup,
+                                              world, dev)
+    extra = {}
+    if not args.no_extra:
+        extra["c3_head_sharded"] = record_c3(args, world, rank, dev)
+        extra["c4_sequence_parallel"] = record_c4(args, world, rank, dev)
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -329,124 +502,124 @@ def run_ours(args):
         "clocks": clk,
         "e2e": e2e,
     }
-    if world == 1 and not args.no_fa2:
-        line["fa2"] = fa2_reference(q.detach(), k.detach(), v.detach(), go, args)
+    if fa2_ms is not None:
+        line["fa2"] = {"value": world * B * S / (fa2_ms / 1e3), "unit": "tokens/s",
+                       "ms_per_step": fa2_ms,
+                       "what": "flash_attn_func dense attention fwd+bwd, same bshd bf16 shape per "
+                               "GPU, non-causal (library comparator, not this package's path)"}
+    line.update(extra)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_reference(args, budget_s=20.0)
+        line["cpu_baseline"] = cpu_baseline(args)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def fa2_reference(q, k, v, go, args):
-    """Dense FlashAttention-2 (flash_attn library, the metric's comparator) fwd+bwd on the
-    same bshd tensors and GPU: tokens/s, CUDA events, same warm-up / step counts."""
-    import torch
-    try:
-        from flash_attn import flash_attn_func
-    except Exception as exc:  # noqa: BLE001 - a comparator only
-        return {"unavailable": f"flash_attn not importable: {exc}"}
-    qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
-
-    def step():
-        for t in (qq, kk, vv):
-            t.grad = None
-        flash_attn_func(qq, kk, vv, causal=False).backward(go)
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    B, S = q.shape[0], q.shape[1]
-    return {"value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-            "what": "flash_attn_func dense attention fwd+bwd, same bshd bf16 q/k/v/grad_out, "
-                    "non-causal (library comparator, not this package's path)"}
-
-
 # ---------------------------------------------------------------------------------------
 # CPU arm: the numpy oracle (a port of the reference; the reference itself is Python and
-# does not travel), forked over heads on every host core
+# does not travel), forked over heads on every host core. A step is the whole fwd+bwd of a
+# subset of the heads (every query, the full tree): heads are independent trees, so the
+# subset is an exact fraction of the workload, and throughput is quoted for the full config.
 # ---------------------------------------------------------------------------------------
 _SHARED = {}
 
 
-def _cpu_heads(hs):
-    """Oracle work for heads [hs[0], hs[1]): (tree-build seconds, query seconds)."""
+def _cpu_heads(heads):
+    """Full fwd+bwd of the oracle for the given heads: Haar build, sampler, softmax, value
+    sum, analytic backward, transposed Haar build. Returns seconds."""
     from oracle import tree_oracle as O
 
     d = _SHARED
-    sl = slice(hs[0], hs[1])
     t0 = time.perf_counter()
-    k_int = O.haar_internal_node_keys(d["k"][:, :, sl], "bf16")
-    O.haar_internal_node_keys_backward(np.zeros_like(k_int))
-    t1 = time.perf_counter()
-    q, v, go, g = d["q"][:, :, sl], d["v"][:, :, sl], d["go"][:, :, sl], d["g"][:, :, :, sl]
-    fw = O.forward(q, k_int, v, g, d["P"])
-    O.backward(q, k_int, v, go, fw["leaf"], fw["weights"])
-    t2 = time.perf_counter()
-    return t1 - t0, t2 - t1
+    for h in heads:
+        sl = slice(h, h + 1)
+        q, k, v, go = (d[n][:, :, sl] for n in ("q", "k", "v", "go"))
+        g = d["g"][:, :, :, sl]
+        k_int = O.haar_internal_node_keys(k, "bf16")
+        fw = O.forward(q, k_int, v, g, d["P"])
+        _, dk_int, _ = O.backward(q, k_int, v, go, fw["leaf"], fw["weights"])
+        O.haar_internal_node_keys_backward(dk_int)
+    return time.perf_counter() - t0
 
 
-def cpu_reference(args, budget_s=20.0):
-    """Time the oracle on all S tree nodes but only Ls queries; extrapolate to a full step.
+class CpuReference:
+    """The oracle port on the host cores, one process per core, heads split over them."""
 
-    Each worker process owns a slice of the heads and times the tree build (all S keys) and
-    the fwd+bwd of the Ls sampled queries separately; a full step is
-    max(build) + max(query) * S / Ls.
-    """
-    import multiprocessing as mp
+    def __init__(self, S, H, D, P):
+        import multiprocessing as mp
 
-    sys.path.insert(0, ROOT)
-    from oracle import tree_oracle as O
+        sys.path.insert(0, ROOT)
+        from oracle import tree_oracle as O
 
-    B, S, H, D, P = 1, args.seq_len, args.heads, args.head_dim, args.num_samples
-    rng = np.random.default_rng(0)
-    Ls = 64
-    rb = lambda *s: O.round_to_bf16(rng.standard_normal(s, dtype=np.float32))  # noqa: E731
-    _SHARED.update(q=rb(Ls, B, H, D), k=rb(S, B, H, D), v=rb(S, B, H, D), go=rb(Ls, B, H, D),
-                   g=-np.log(rng.exponential(size=(O.log_n_of(S), Ls, B, H, P, 2)).astype(np.float32)),
-                   P=P)
-    cores = min(os.cpu_count() or 1, H)
-    chunks = [(i * H // cores, (i + 1) * H // cores) for i in range(cores)]
-    ctx = mp.get_context("fork")
-    samples = []
-    with ctx.Pool(cores) as pool:
-        deadline = time.perf_counter() + budget_s
-        while True:
-            res = pool.map(_cpu_heads, chunks)
-            samples.append((max(r[0] for r in res), max(r[1] for r in res)))
-            if time.perf_counter() > deadline or len(samples) >= 3:
-                break
-    t_build = min(s[0] for s in samples)
-    t_query = min(s[1] for s in samples)
-    t_step = t_build + t_query * (S / Ls)
-    return {"value": B * S / t_step, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"numpy oracle (oracle/tree_oracle.py), Haar build + transpose of all {S} keys "
-                      f"and fwd+bwd of {Ls} of {S} queries x {H} heads, {cores} processes over heads; "
-                      f"step = build + query part x {S // Ls}",
-            "build_s": t_build, "query_sample_s": t_query, "extrapolated_step_s": t_step}
+        rng = np.random.default_rng(0)
+        rb = lambda *s: O.round_to_bf16(rng.standard_normal(s, dtype=np.float32))  # noqa: E731
+        _SHARED.update(q=rb(S, 1, H, D), k=rb(S, 1, H, D), v=rb(S, 1, H, D), go=rb(S, 1, H, D),
+                       g=-np.log(rng.exponential(size=(O.log_n_of(S), S, 1, H, P, 2)).astype(np.float32)),
+                       P=P)
+        self.S, self.H = S, H
+        self.cores = min(os.cpu_count() or 1, H)
+        self.pool = mp.get_context("fork").Pool(self.cores)
+
+    def step(self, n_heads):
+        """One step over the first n_heads heads; returns wall seconds."""
+        parts = [list(range(i, n_heads, self.cores)) for i in range(self.cores)]
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_heads, [p for p in parts if p])
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def cpu_baseline(args):
+    """One bounded step (one head per host core) for our arm's line."""
+    S, H, D, P = args.seq_len, args.heads, args.head_dim, args.num_samples
+    ref = CpuReference(S, H, D, P)
+    try:
+        n = ref.cores
+        t = ref.step(n)
+    finally:
+        ref.close()
+    return {"value": S * (n / H) / t, "unit": "tokens/s", "cores": ref.cores, "kind": "port",
+            "sample": f"numpy oracle (oracle/tree_oracle.py): full fwd+bwd (Haar build, sampler, "
+                      f"value sum, backward, Haar transpose) of {n} of {H} heads, all {S} queries, "
+                      f"one process per core; value = tokens/s of the full {H}-head config",
+            "step_s": t, "heads_per_step": n}
 
 
 def run_reference(args):
+    """The reference arm: the oracle port timed over whole steps on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    r = cpu_reference(args, budget_s=30.0)
-    vals = [r["value"]]
-    value = r["value"]
+    S, H, D, P = args.seq_len, args.heads, args.head_dim, args.num_samples
+    ref = CpuReference(S, H, D, P)
+    try:
+        # calibration step (counts as the first warm-up): one head per core
+        n = ref.cores
+        t1 = ref.step(n)
+        # size a step so that warm-up + timed steps take about 150 s in all
+        per_step = 150.0 / max(1, args.steps + args.warmup)
+        n = min(H, n * max(1, int(per_step // max(t1, 1e-3))))
+        for _ in range(max(0, args.warmup - 1)):
+            ref.step(n)
+        times = [ref.step(n) for _ in range(args.steps)]
+    finally:
+        ref.close()
+    t = statistics.mean(times)
+    value = S * (n / H) / t
+    sample = (f"numpy oracle (oracle/tree_oracle.py): full fwd+bwd (Haar build, sampler, value sum, "
+              f"backward, Haar transpose) of {n} of {H} heads per step, all {S} queries, one process "
+              f"per host core; value = tokens/s of the full {H}-head config")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": args.seq_len / value * 1e3, "higher_is_better": True,
+            "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1), bf16-rounded", "config": {**WORKLOAD, "batch_per_gpu": 1},
-            "cpu_baseline": {**r, "value": value},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.cores, "kind": "port",
+                             "sample": sample, "heads_per_step": n, "step_s": times},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -631,6 +804,80 @@ def run_blocked(args):
         dist.destroy_process_group()
 
 
+def run_sweep(args):
+    """BASELINE config 5, attn-bench style: S in {1k..16k} with B*S = 16384 tokens, H=16,
+    d in {32, 64, 96, 128}, bf16 / fp16, causal off / on, 8 paths; this package's op and dense
+    FA2 on the same inputs. Per configuration 10 warm-up and 50 timed iterations of the forward
+    alone and of forward + backward, each iteration timed with CUDA events; bwd = median(step) -
+    median(fwd) (attn_bench/harness.py). One JSON line with every row."""
+    import torch
+    import treeattn_b200 as ta
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    try:
+        from flash_attn import flash_attn_func
+    except Exception:  # noqa: BLE001 - a comparator only
+        flash_attn_func = None
+    warm, iters = 10, 50
+
+    def med_ms(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for a, b in ev:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+    rows = []
+    for dname, dt in (("bf16", torch.bfloat16), ("fp16", torch.float16)):
+        for causal in (False, True):
+            for D in (32, 64, 96, 128):
+                for S in (1024, 2048, 4096, 8192, 16384):
+                    B, H, P = 16384 // S, 16, 8
+                    g = torch.Generator(device=dev).manual_seed(S + D)
+                    q, k, v, go = (torch.randn(B, S, H, D, device=dev, generator=g).to(dt) for _ in range(4))
+                    for t in (q, k, v):
+                        t.requires_grad_(True)
+
+                    def fwd_ours():
+                        with torch.no_grad():
+                            ta.tree_attention(q, k, v, causal, None, num_samples=P)
+
+                    def step_ours():
+                        for t in (q, k, v):
+                            t.grad = None
+                        ta.tree_attention(q, k, v, causal, None, num_samples=P).backward(go)
+
+                    torch.manual_seed(0)
+                    f_ms, s_ms = med_ms(fwd_ours), med_ms(step_ours)
+                    row = {"dtype": dname, "causal": causal, "seq_len": S, "batch": B, "heads": H,
+                           "head_dim": D, "ours_fwd_ms": f_ms, "ours_bwd_ms": s_ms - f_ms,
+                           "ours_step_ms": s_ms, "ours_tokens_per_s": B * S / (s_ms / 1e3)}
+                    if flash_attn_func is not None:
+                        def fwd_fa():
+                            with torch.no_grad():
+                                flash_attn_func(q, k, v, causal=causal)
+
+                        def step_fa():
+                            for t in (q, k, v):
+                                t.grad = None
+                            flash_attn_func(q, k, v, causal=causal).backward(go)
+
+                        ff, fs = med_ms(fwd_fa), med_ms(step_fa)
+                        row.update(fa2_fwd_ms=ff, fa2_bwd_ms=fs - ff, fa2_step_ms=fs,
+                                   fa2_tokens_per_s=B * S / (fs / 1e3), speedup=fs / s_ms)
+                    rows.append(row)
+                    print(json.dumps(row), file=sys.stderr, flush=True)
+                    del q, k, v, go
+    print(json.dumps({"metric": "attn-bench sweep (BASELINE config 5): fwd / bwd ms, ours vs FA2",
+                      "warmup": warm, "iters": iters, "num_samples": 8, "rows": rows}), flush=True)
+
+
 def main():
     args = parse_args()
     sys.path.insert(0, ROOT)
@@ -640,6 +887,8 @@ def main():
         run_sp(args)
     elif args.mode == "blocked":
         run_blocked(args)
+    elif args.mode == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 

@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fwd_fast_kernel(const FwdParam
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int g = threadIdx.x >> 2;
   const int t4 = threadIdx.x & 3;
   const bool active = lt * kFwdGroups + g < p.L;
@@ -586,12 +587,32 @@ __global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t n
 // Gumbel noise of one shard of a larger (rows, batch, heads, row_elems) draw: local element
 // (r, b, h, i) of the (row_count, batch_count, head_count, row_elems) output takes the value
 // torch's draw puts at global element
-// (((row0 + r) * batch_total + batch0 + b) * head_total + head0 + h) * row_elems + i. One philox 4-vector per element (a shard's elements are spread over
-// the subsequences, so the vectors are not shared).
+// (((row0 + r) * batch_total + batch0 + b) * head_total + head0 + h) * row_elems + i.
+// One philox 4-vector serves the global elements e0 + c * stride (c = 0..3) of torch's
+// grid-stride loop; the thread of the first of them that lies in the shard computes it once
+// and writes every component that lies in the shard (when the stride is a multiple of a
+// row, as for batch and head shards of the benchmark shapes, that is all four).
 struct ShardDivs {
   FastDiv row_elems, head_count, batch_count, stride;
-  uint32_t row0, batch_total, batch0, head_total, head0;
+  FastDiv g_row_elems, g_heads, g_batch;  // decomposition of a global index
+  uint32_t row0, row_count, batch_total, batch0, head_total, head0, numel;
 };
+
+// local index of global element g, or -1 when g is outside the shard
+__device__ __forceinline__ int64_t shard_local(uint32_t g, const ShardDivs& sd) {
+  if (g >= sd.numel) return -1;
+  const uint32_t t = sd.g_row_elems.div(g);
+  const uint32_t i = g - t * sd.g_row_elems.d;
+  const uint32_t t2 = sd.g_heads.div(t);
+  const uint32_t h = t - t2 * sd.g_heads.d;
+  const uint32_t row = sd.g_batch.div(t2);
+  const uint32_t b = t2 - row * sd.g_batch.d;
+  if (h < sd.head0 || h >= sd.head0 + sd.head_count.d || b < sd.batch0 ||
+      b >= sd.batch0 + sd.batch_count.d || row < sd.row0 || row >= sd.row0 + sd.row_count)
+    return -1;
+  return ((((int64_t)(row - sd.row0) * sd.batch_count.d + (b - sd.batch0)) * sd.head_count.d +
+           (h - sd.head0)) * sd.row_elems.d + i);
+}
 
 __global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
     float* out, uint32_t local_numel, ShardDivs sd, uint64_t seed, uint64_t offset,
@@ -609,8 +630,21 @@ __global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
   const uint32_t g =
       (((sd.row0 + r) * sd.batch_total + sd.batch0 + b) * sd.head_total + sd.head0 + h) *
           sd.row_elems.d + inner;
-  const float u = torch_uniform(seed, offset + (uint64_t)depth * offset_step, g, sd.stride);
-  out[(uint64_t)depth * local_numel + e] = gumbel_from_uniform(u);
+  const uint32_t bundle = sd.stride.div(g);
+  const uint32_t c = bundle & 3u;
+  const uint32_t base = g - c * sd.stride.d;
+  for (uint32_t c2 = 0; c2 < c; ++c2)  // an earlier component is in the shard: its thread writes
+    if (shard_local(base + c2 * sd.stride.d, sd) >= 0) return;
+  const uint32_t tid = base - (bundle - c) * sd.stride.d;
+  curandStatePhilox4_32_10_t st;
+  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * (uint64_t)(bundle >> 2), &st);
+  const float4 u4 = _curand_uniform4(st.output);
+  float* o = out + (uint64_t)depth * local_numel;
+  o[e] = gumbel_from_uniform(c == 0 ? u4.x : (c == 1 ? u4.y : (c == 2 ? u4.z : u4.w)));
+  for (uint32_t c2 = c + 1; c2 < 4; ++c2) {
+    const int64_t loc = shard_local(base + c2 * sd.stride.d, sd);
+    if (loc >= 0) o[loc] = gumbel_from_uniform(c2 == 1 ? u4.y : (c2 == 2 ? u4.z : u4.w));
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -686,7 +720,7 @@ static void launch_fwd_kernel(const FwdParams& p, dim3 grid, size_t smem, cudaSt
 
 template <typename T, int CPL>
 static void launch_fast_kernel(const FwdParams& p, dim3 grid, size_t smem, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_set{0};
+  static std::atomic<uint64_t> attr_set{0};  // per device: the attribute is set once
   if (smem > 48 * 1024) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -956,6 +990,11 @@ extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, const ta_shar
   sd.head_count.init((uint32_t)s.head_count);
   sd.batch_count.init((uint32_t)s.batch_count);
   sd.stride.init((uint32_t)rng->draw_stride);
+  sd.g_row_elems.init((uint32_t)row_elems);
+  sd.g_heads.init((uint32_t)s.head_total);
+  sd.g_batch.init((uint32_t)s.batch_total);
+  sd.row_count = (uint32_t)s.row_count;
+  sd.numel = (uint32_t)((uint64_t)s.row_total * s.batch_total * s.head_total * row_elems);
   sd.row0 = (uint32_t)s.row0;
   sd.batch_total = (uint32_t)s.batch_total; sd.batch0 = (uint32_t)s.batch0;
   sd.head_total = (uint32_t)s.head_total; sd.head0 = (uint32_t)s.head0;
