@@ -170,15 +170,21 @@ def _barrier(world, dev):
     torch.cuda.synchronize(dev)
 
 
-def _timed(step, steps, warmup, world, dev):
+def _timed(step, steps, warmup, world, dev, profile=False):
     """`warmup` untimed steps, then `steps` steps bracketed by barrier + synchronize and timed
-    with CUDA events on the current stream; the max over ranks, in ms per step."""
+    with CUDA events on the current stream; the max over ranks, in ms per step. With
+    ``profile`` the library's per-launch events cover the timed steps only: returns
+    (ms, {kernel: (launches, ms)})."""
     import torch
     import torch.distributed as dist
+    from treeattn_b200 import ops
 
     for _ in range(warmup):
         step()
     _barrier(world, dev)
+    if profile:
+        ops.profile_collect()  # drop anything recorded before
+        ops.profile_enable(True)
     stream = torch.cuda.current_stream(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -187,11 +193,15 @@ def _timed(step, steps, warmup, world, dev):
     t1.record(stream)
     _barrier(world, dev)
     ms = t0.elapsed_time(t1)
+    prof = None
+    if profile:
+        prof = ops.profile_collect()
+        ops.profile_enable(False)
     if world > 1:
         tm = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
         ms = float(tm.item())
-    return ms / steps
+    return (ms / steps, prof) if profile else ms / steps
 
 
 def _fa2_ms(shape, dtype, causal, steps, warmup, world, dev, sd=1.0):
@@ -248,10 +258,7 @@ def record_c3(args, world, rank, dev):
         blocked_tree_attention(q, k, v, True, None, num_samples=P, fanout=f, leaf_block=Lb,
                                shard=shard).backward(go)
 
-    ops.profile_enable(True)
-    ms = _timed(step, args.steps, args.warmup, world, dev)
-    prof = ops.profile_collect()
-    ops.profile_enable(False)
+    ms, prof = _timed(step, args.steps, args.warmup, world, dev, profile=True)
     fa2 = None if args.no_fa2 else _fa2_ms((B, S, hl, D), torch.float16, True, args.steps,
                                             args.warmup, world, dev, 0.5)
     rec = {"config": {"workload": "generalised tree (fanout 4, leaf block 128), causal", "batch": B,
@@ -295,10 +302,7 @@ def record_c4(args, world, rank, dev):
             out = ta.tree_attention(q, k, v, True, None, num_samples=P)
         out.backward(go)
 
-    ops.profile_enable(True)
-    ms = _timed(step, args.steps, args.warmup, world, dev)
-    prof = ops.profile_collect()
-    ops.profile_enable(False)
+    ms, prof = _timed(step, args.steps, args.warmup, world, dev, profile=True)
     rec = {"config": {"workload": "stochastic tree attention, causal (exact prefix + corrected "
                                   "sampler)", "batch": B, "seq_len": S, "heads": H, "head_dim": D,
                       "num_samples": P, "dtype": "bf16",

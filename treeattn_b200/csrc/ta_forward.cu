@@ -588,32 +588,13 @@ __global__ void __launch_bounds__(256) gumbel_fill_kernel(float* out, uint32_t n
 // (r, b, h, i) of the (row_count, batch_count, head_count, row_elems) output takes the value
 // torch's draw puts at global element
 // (((row0 + r) * batch_total + batch0 + b) * head_total + head0 + h) * row_elems + i.
-// One philox 4-vector serves the global elements e0 + c * stride (c = 0..3) of torch's
-// grid-stride loop; the thread of the first of them that lies in the shard computes it once
-// and writes every component that lies in the shard (when the stride is a multiple of a
-// row, as for batch and head shards of the benchmark shapes, that is all four).
 struct ShardDivs {
   FastDiv row_elems, head_count, batch_count, stride;
-  FastDiv g_row_elems, g_heads, g_batch;  // decomposition of a global index
   uint32_t row0, row_count, batch_total, batch0, head_total, head0, numel;
 };
 
-// local index of global element g, or -1 when g is outside the shard
-__device__ __forceinline__ int64_t shard_local(uint32_t g, const ShardDivs& sd) {
-  if (g >= sd.numel) return -1;
-  const uint32_t t = sd.g_row_elems.div(g);
-  const uint32_t i = g - t * sd.g_row_elems.d;
-  const uint32_t t2 = sd.g_heads.div(t);
-  const uint32_t h = t - t2 * sd.g_heads.d;
-  const uint32_t row = sd.g_batch.div(t2);
-  const uint32_t b = t2 - row * sd.g_batch.d;
-  if (h < sd.head0 || h >= sd.head0 + sd.head_count.d || b < sd.batch0 ||
-      b >= sd.batch0 + sd.batch_count.d || row < sd.row0 || row >= sd.row0 + sd.row_count)
-    return -1;
-  return ((((int64_t)(row - sd.row0) * sd.batch_count.d + (b - sd.batch0)) * sd.head_count.d +
-           (h - sd.head0)) * sd.row_elems.d + i);
-}
-
+// General case: one philox 4-vector per element (a shard's elements may be spread over the
+// subsequences so that no two share a vector).
 __global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
     float* out, uint32_t local_numel, ShardDivs sd, uint64_t seed, uint64_t offset,
     uint64_t offset_step) {
@@ -630,20 +611,48 @@ __global__ void __launch_bounds__(256) gumbel_fill_shard_kernel(
   const uint32_t g =
       (((sd.row0 + r) * sd.batch_total + sd.batch0 + b) * sd.head_total + sd.head0 + h) *
           sd.row_elems.d + inner;
-  const uint32_t bundle = sd.stride.div(g);
-  const uint32_t c = bundle & 3u;
-  const uint32_t base = g - c * sd.stride.d;
-  for (uint32_t c2 = 0; c2 < c; ++c2)  // an earlier component is in the shard: its thread writes
-    if (shard_local(base + c2 * sd.stride.d, sd) >= 0) return;
-  const uint32_t tid = base - (bundle - c) * sd.stride.d;
+  const float u = torch_uniform(seed, offset + (uint64_t)depth * offset_step, g, sd.stride);
+  out[(uint64_t)depth * local_numel + e] = gumbel_from_uniform(u);
+}
+
+// Common case: the grid stride is a multiple of a global row (batch_total * head_total *
+// row_elems elements), as for the benchmark shapes. A philox 4-vector then serves elements
+// tid + stride (4 call + c) of the same column of rows (4 call + c) stride / row apart, so
+// the vector belongs to the shard for all four or none: one thread per (call, shard column,
+// row within a stride) computes it once and writes the components in the shard's rows.
+struct ShardRowDivs {
+  FastDiv per_call, cols, row_elems, head_count, row;
+  uint32_t row_block, row0, row_count, batch0, head_total, head0, numel, stride, calls;
+};
+
+__global__ void __launch_bounds__(256) gumbel_fill_shard_rows_kernel(
+    float* out, uint32_t local_numel, ShardRowDivs sd, uint64_t seed, uint64_t offset,
+    uint64_t offset_step) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= sd.per_call.d * sd.calls) return;
+  const int depth = blockIdx.y;
+  const uint32_t call = sd.per_call.div(t);
+  const uint32_t rem = t - call * sd.per_call.d;
+  const uint32_t rr = sd.cols.div(rem);            // row within one stride
+  const uint32_t lc = rem - rr * sd.cols.d;          // shard column (b, h, i)
+  const uint32_t t2 = sd.row_elems.div(lc);
+  const uint32_t i = lc - t2 * sd.row_elems.d;
+  const uint32_t bl = sd.head_count.div(t2);
+  const uint32_t hl = t2 - bl * sd.head_count.d;
+  const uint32_t col = ((sd.batch0 + bl) * sd.head_total + sd.head0 + hl) * sd.row_elems.d + i;
+  const uint32_t tid = rr * sd.row_block + col;
   curandStatePhilox4_32_10_t st;
-  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * (uint64_t)(bundle >> 2), &st);
+  curand_init(seed, tid, offset + (uint64_t)depth * offset_step + 4ull * call, &st);
   const float4 u4 = _curand_uniform4(st.output);
   float* o = out + (uint64_t)depth * local_numel;
-  o[e] = gumbel_from_uniform(c == 0 ? u4.x : (c == 1 ? u4.y : (c == 2 ? u4.z : u4.w)));
-  for (uint32_t c2 = c + 1; c2 < 4; ++c2) {
-    const int64_t loc = shard_local(base + c2 * sd.stride.d, sd);
-    if (loc >= 0) o[loc] = gumbel_from_uniform(c2 == 1 ? u4.y : (c2 == 2 ? u4.z : u4.w));
+#pragma unroll
+  for (uint32_t c = 0; c < 4; ++c) {
+    const uint32_t g = tid + sd.stride * (4u * call + c);
+    if (g >= sd.numel) break;
+    const uint32_t row = sd.row.div(g);
+    if (row < sd.row0 || row >= sd.row0 + sd.row_count) continue;
+    o[(row - sd.row0) * sd.cols.d + lc] =
+        gumbel_from_uniform(c == 0 ? u4.x : (c == 1 ? u4.y : (c == 2 ? u4.z : u4.w)));
   }
 }
 
@@ -985,24 +994,52 @@ extern "C" int ta_gumbel_fill_shard(float* out, const ta_rng* rng, const ta_shar
     return fail(TA_ERR_INVALID, "ta_gumbel_fill_shard: invalid rng");
   const uint64_t local = (uint64_t)s.row_count * s.batch_count * s.head_count * row_elems;
   if (local == 0 || depths == 0) return TA_OK;
-  ShardDivs sd;
-  sd.row_elems.init((uint32_t)row_elems);
-  sd.head_count.init((uint32_t)s.head_count);
-  sd.batch_count.init((uint32_t)s.batch_count);
-  sd.stride.init((uint32_t)rng->draw_stride);
-  sd.g_row_elems.init((uint32_t)row_elems);
-  sd.g_heads.init((uint32_t)s.head_total);
-  sd.g_batch.init((uint32_t)s.batch_total);
-  sd.row_count = (uint32_t)s.row_count;
-  sd.numel = (uint32_t)((uint64_t)s.row_total * s.batch_total * s.head_total * row_elems);
-  sd.row0 = (uint32_t)s.row0;
-  sd.batch_total = (uint32_t)s.batch_total; sd.batch0 = (uint32_t)s.batch0;
-  sd.head_total = (uint32_t)s.head_total; sd.head0 = (uint32_t)s.head0;
+  const uint64_t row_block = (uint64_t)s.batch_total * s.head_total * row_elems;
+  const uint64_t numel = (uint64_t)s.row_total * row_block;
+  const uint32_t stride = (uint32_t)rng->draw_stride;
   TA_PROFILE("gumbel_fill", (cudaStream_t)stream);
-  dim3 grid((unsigned)((local + 255) / 256), (unsigned)depths);
-  gumbel_fill_shard_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      (float*)out, (uint32_t)local, sd, rng->seed,
-      rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
+  // the row kernel computes the vectors of every row of the shard's columns: worth it unless
+  // the shard holds under a quarter of the rows (then one vector per element costs less)
+  if (stride % row_block == 0 && 4 * s.row_count >= s.row_total) {
+    ShardRowDivs sd;
+    const uint32_t cols = (uint32_t)((uint64_t)s.batch_count * s.head_count * row_elems);
+    const uint32_t rows_per_stride = (uint32_t)(stride / row_block);
+    const uint64_t bundles = (numel + stride - 1) / stride;
+    sd.calls = (uint32_t)((bundles + 3) / 4);
+    sd.per_call.init(rows_per_stride * cols);
+    sd.cols.init(cols);
+    sd.row_elems.init((uint32_t)row_elems);
+    sd.head_count.init((uint32_t)s.head_count);
+    sd.row.init((uint32_t)row_block);
+    sd.row_block = (uint32_t)row_block;
+    sd.row0 = (uint32_t)s.row0;
+    sd.row_count = (uint32_t)s.row_count;
+    sd.batch0 = (uint32_t)s.batch0;
+    sd.head_total = (uint32_t)s.head_total;
+    sd.head0 = (uint32_t)s.head0;
+    sd.numel = (uint32_t)numel;
+    sd.stride = stride;
+    const uint64_t threads = (uint64_t)rows_per_stride * cols * sd.calls;
+    dim3 grid((unsigned)((threads + 255) / 256), (unsigned)depths);
+    gumbel_fill_shard_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        (float*)out, (uint32_t)local, sd, rng->seed,
+        rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
+  } else {
+    ShardDivs sd;
+    sd.row_elems.init((uint32_t)row_elems);
+    sd.head_count.init((uint32_t)s.head_count);
+    sd.batch_count.init((uint32_t)s.batch_count);
+    sd.stride.init(stride);
+    sd.row0 = (uint32_t)s.row0;
+    sd.row_count = (uint32_t)s.row_count;
+    sd.batch_total = (uint32_t)s.batch_total; sd.batch0 = (uint32_t)s.batch0;
+    sd.head_total = (uint32_t)s.head_total; sd.head0 = (uint32_t)s.head0;
+    sd.numel = (uint32_t)numel;
+    dim3 grid((unsigned)((local + 255) / 256), (unsigned)depths);
+    gumbel_fill_shard_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        (float*)out, (uint32_t)local, sd, rng->seed,
+        rng->offset + (uint64_t)depth0 * rng->offset_step, rng->offset_step);
+  }
   return check_launch("gumbel fill (shard)");
 }
 
