@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
   int* s_off = s_runs + kMaxLev;                                    // first row of level
   int* s_pre = s_off + kMaxLev;  // [2][kMaxLev]: the carried node began before the range
   int* s_wpre = s_pre + 2 * kMaxLev;  // [4][kMaxLev]: runs of level d in earlier path warps
+  __shared__ uint32_t s_edge[4];  // keys of the head's first / last path, and their flags
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // path of this thread; the upper half (tid >= 128) writes the low coefficient halves
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
     load_rec(range_i0, n, cur);
     if (tid < n) s_l[tid] = cur.pl / (uint32_t)p.S;
     if (tid < kMaxLev) s_pre[tid] = 1;  // at the range start, every open node began before it
+    if (tid < 4) s_edge[tid] = 0;
     if (tid < 2 * lev) flg[tid] = 0;
     for (int idx = tid; idx < kMTile * kGStride / 8; idx += kMmaThreads)
       reinterpret_cast<uint4*>(s_G)[idx] = make_uint4(0, 0, 0, 0);
@@ -375,16 +377,45 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
             for (int64_t pf = a + 1; pf < c; ++pf) zero_node(d, pf);
           }
         }
-      } else {  // the head's first path: everything to its left
-        for (int d = 0; d <= ln; ++d)
-          for (int64_t pf = 0; pf < (int64_t)(my_key >> (ln - d)); ++pf) zero_node(d, pf);
+      } else {  // the head's first path: everything to its left (zeroed by the whole CTA below)
+        s_edge[0] = my_key;
+        s_edge[2] = 1;
       }
       if (tid == n - 1 && !has_next) {  // the head's last path: everything to its right
+        s_edge[1] = my_key;
+        s_edge[3] = 1;
+      }
+    }
+    __syncthreads();
+    if (s_edge[2] | s_edge[3]) {
+      // the head's two ends (every node left of its first path, right of its last): few
+      // nodes for a head whose paths spread over its leaves, up to half the tree when they
+      // cover only part of it (causal or sequence-parallel queries), so all threads share it
+      for (int side = 0; side < 2; ++side) {
+        if (!s_edge[2 + side]) continue;
+        const uint32_t key = s_edge[side];
         for (int d = 0; d <= ln; ++d) {
-          const int64_t last = ((int64_t)1 << d) - 1;
-          for (int64_t pf = (int64_t)(my_key >> (ln - d)) + 1; pf <= last; ++pf) zero_node(d, pf);
+          const int64_t at = (int64_t)(key >> (ln - d));
+          const int64_t lo = side == 0 ? 0 : at + 1;
+          const int64_t hi = side == 0 ? at : ((int64_t)1 << d);  // exclusive
+          const int64_t pairs = (hi - lo) * (D / 2);
+          for (int64_t i = tid; i < pairs; i += kMmaThreads) {
+            const int64_t pf = lo + i / (D / 2);
+            const int c = (int)(i % (D / 2)) * 2;
+            if (d < ln) {
+              char* rowp = dkb + (((int64_t)1 << d) - 1 + pf) * p.dks * dk_es;
+              if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
+              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+            } else {
+              char* rowp = dvb + (pf + base_node - K) * p.dvs * dv_es;
+              if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
+              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+            }
+          }
         }
       }
+      __syncthreads();
+      if (tid == 0) s_edge[2] = s_edge[3] = 0;
     }
     if (last_sub) break;
     // s_g is free: gather the next sub-chunk's dO rows behind its dK product. The s_co reads
