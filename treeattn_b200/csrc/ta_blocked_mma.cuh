@@ -32,6 +32,9 @@ template <> struct Mma<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  __device__ __forceinline__ static uint16_t half_bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
 };
 template <> struct Mma<__half> {
   __device__ __forceinline__ static void run(float* c, const uint32_t* a, const uint32_t* b) {
@@ -44,6 +47,9 @@ template <> struct Mma<__half> {
   __device__ __forceinline__ static uint32_t pack(float x, float y) {
     __half2 h = __floats2half2_rn(x, y);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint16_t half_bits(float x) {
+    return __half_as_ushort(__float2half_rn(x));
   }
 };
 
@@ -270,14 +276,14 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
 // dV += (w P)^T dO, dK += dS^T Q over the tile's pairs.
 // ---------------------------------------------------------------------------------------
 constexpr int kDFMax = 32;  // levels * fanout handled by the tensor-core backward
+constexpr int kZLd = kDFMax + 8;  // row stride (16-bit units) of the dz tiles
 
 template <int LB, int D>
 __host__ __device__ constexpr size_t blk_mma_bwd_smem() {
   return (size_t)(2 * LB + 2 * 128) * (D + 8) * 2   // k, v, q, dO
          + (size_t)2 * 128 * (LB + 8) * 2            // w P, dS
          + (size_t)128 * 16                           // boundary, delta, w
-         + (size_t)128 * kDFMax * 4                   // dz rows of the tile
-         + (size_t)kDFMax * D * 4;                    // summary partial accumulators
+         + (size_t)2 * 128 * kZLd * 2;                // dz rows of the tile, 16-bit high / low
 }
 
 template <typename T> __device__ __forceinline__ float raw_to_float(uint16_t r);
@@ -306,8 +312,10 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
   int64_t* s_bnd = reinterpret_cast<int64_t*>(s_ds + 128 * G::LDP);
   float* s_delta = reinterpret_cast<float*>(s_bnd + 128);
   float* s_w = s_delta + 128;
-  float* s_dz = s_w + 128;            // [128][DF]
-  float* s_dc = s_dz + 128 * kDFMax;  // [DF][D], element e owned by thread e % 256
+  // dz rows of the tile as 16-bit high and low parts, [pair][DF row] (A^T of the summary
+  // product dc += dz^T Q)
+  uint16_t* s_zh = reinterpret_cast<uint16_t*>(s_w + 128);
+  uint16_t* s_zl = s_zh + 128 * kZLd;
   __shared__ int64_t range[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int bh = blockIdx.x / p.nb;
@@ -333,7 +341,17 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
   }
   cp_async_commit();
   const int DF = p.DF;
-  for (int e = tid; e < DF * D; e += blockDim.x) s_dc[e] = 0.0f;
+  const int zmt = (DF + 15) >> 4;  // m16 tiles of the summary product
+  // summary product items (m16 tile, pair of n8 column tiles), at most two per warp; their
+  // float32 accumulators live in registers across the block's pair tiles
+  constexpr int NPAIR = D / 16;
+  float acc_dc[2][2][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc_dc[i][t][e] = 0.0f;
   __syncthreads();
   const int64_t beg = range[0], end = range[1];
   const int g = lane >> 2, tq = lane & 3;
@@ -375,9 +393,12 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
       s_delta[tid] = dl;
       s_w[tid] = w;
     }
-    for (int i = tid; i < n * DF; i += blockDim.x) {
-      const int r = i / DF, c = i - r * DF;
-      s_dz[r * DF + c] = p.dz_rows[((int64_t)bh * p.P + vals[t0 + r]) * DF + c];
+    for (int i = tid; i < 128 * zmt * 16; i += blockDim.x) {
+      const int r = i / (zmt * 16), c = i - r * (zmt * 16);
+      const float z = (r < n && c < DF) ? p.dz_rows[((int64_t)bh * p.P + vals[t0 + r]) * DF + c] : 0.0f;
+      const uint16_t hi = Mma<T>::half_bits(z);
+      s_zh[r * kZLd + c] = hi;
+      s_zl[r * kZLd + c] = Mma<T>::half_bits(z - raw_to_float<T>(hi));
     }
     cp_async_commit();
     cp_async_wait_0();
@@ -490,16 +511,27 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
       }
     }
     __syncthreads();
-    // summary partials: dc[row][c] += sum over the tile's pairs of dz[pair][row] q[pair][c]
-    // (CUDA cores; each element has one owner thread, pairs in sorted order)
-    for (int e = tid; e < DF * D; e += blockDim.x) {
-      const int row = e / D, c = e - row * D;
-      float a = s_dc[e];
-      for (int t = 0; t < n; ++t) a = fmaf(s_dz[t * DF + row], raw_to_float<T>(s_q[t * G::LD + c]), a);
-      s_dc[e] = a;
+    // summary partials dc[row][c] += sum over the tile's pairs of dz[pair][row] q[pair][c], as
+    // tensor-core products of dz^T (high and low 16-bit parts) with the tile's q rows
+    const int kend = (n + 15) & ~15;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int item = warp + 8 * i;
+      if (item < zmt * NPAIR) {
+        const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
+        for (int kc = 0; kc < kend; kc += 16) {
+          uint32_t ah[4], al[4], bb[4];
+          frag_a_t(ah, s_zh, kZLd, zm, kc, lane);
+          frag_a_t(al, s_zl, kZLd, zm, kc, lane);
+          frag_b_kn(bb, s_q, G::LD, zn, kc, lane);
+          Mma<T>::run(acc_dc[i][0], ah, bb);
+          Mma<T>::run(acc_dc[i][0], al, bb);
+          Mma<T>::run(acc_dc[i][1], ah, bb + 2);
+          Mma<T>::run(acc_dc[i][1], al, bb + 2);
+        }
+      }
     }
     // phase 3: dV += (wP)^T dO, dK += dS^T Q over the tile's (up to) 128 pairs
-    const int kend = (n + 15) & ~15;
     for (int kc = 0; kc < kend; kc += 16) {
       uint32_t a[4], ad[4];
       frag_a_t(a, s_wp, G::LDP, km, kc, lane);
@@ -517,8 +549,24 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
     }
   }
   cp_async_wait_0();  // a block without pairs never waited for its K / V copies
-  for (int e = tid; e < DF * D; e += blockDim.x)
-    p.dc_part[((int64_t)bh * p.nb + j) * DF * D + e] = s_dc[e];
+  {
+    float* dcp = p.dc_part + ((int64_t)bh * p.nb + j) * DF * D;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int item = warp + 8 * i;
+      if (item < zmt * NPAIR) {
+        const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int c = zn + t * 8 + tq * 2;
+          if (zm + g < DF)
+            *reinterpret_cast<float2*>(dcp + (zm + g) * D + c) = make_float2(acc_dc[i][t][0], acc_dc[i][t][1]);
+          if (zm + g + 8 < DF)
+            *reinterpret_cast<float2*>(dcp + (zm + g + 8) * D + c) = make_float2(acc_dc[i][t][2], acc_dc[i][t][3]);
+        }
+      }
+    }
+  }
   // dV (input dtype) and dK of the attention part (float32, the per-key pass adds the
   // summary gradients)
   const int kr0 = km + g, kr1 = km + g + 8;
