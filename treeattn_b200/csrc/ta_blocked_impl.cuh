@@ -692,22 +692,33 @@ __global__ void __launch_bounds__(256) blk_bwd_node_kernel(const BlkParams p, in
 // gradient of the key's ancestor / (2 * keys under it)
 template <typename T>
 __global__ void __launch_bounds__(256) blk_bwd_key_kernel(const BlkParams p) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t per_head = (int64_t)p.N * p.D;
-  if (i >= per_head * p.B * p.H) return;
-  const int bh = (int)(i / per_head);
-  const int64_t r = i - (int64_t)bh * per_head;
-  const int64_t key = r / p.D;
-  const int c = (int)(r - key * p.D);
+  // one row (head, key) per D/4 threads, four channels per thread
+  const int tpr = p.D >> 2, rpb = 256 / tpr;
+  const int rl = threadIdx.x / tpr, c = (threadIdx.x - rl * tpr) * 4;
+  if (rl >= rpb) return;
+  const int64_t row = (int64_t)blockIdx.x * rpb + rl;
+  if (row >= (int64_t)p.B * p.H * p.N) return;
+  const int bh = (int)(row / p.N);
+  const int64_t key = row - (int64_t)bh * p.N;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-  float acc = p.dk_attn[((int64_t)bh * p.N + key) * p.D + c];
-  int64_t span = p.N;
+  float4 acc = *reinterpret_cast<const float4*>(p.dk_attn + row * p.D + c);
+  // node of `key` at level d: key / (N / f^d), N and f powers of two
+  const int ln = __ffsll(p.N) - 1, lf = __ffs(p.f) - 1;
   for (int d = 1; d <= p.Dp; ++d) {
-    span /= p.f;
-    const int64_t node = key / span;
-    acc = fmaf(p.dc[((int64_t)bh * p.R + p.lvl_off[d] + node) * p.D + c], 0.5f / (float)span, acc);
+    const int ls = ln - d * lf;
+    const int64_t node = key >> ls;
+    const float sc = 0.5f / (float)(1ll << ls);
+    const float4 v = *reinterpret_cast<const float4*>(p.dc + ((int64_t)bh * p.R + p.lvl_off[d] + node) * p.D + c);
+    acc.x = fmaf(v.x, sc, acc.x);
+    acc.y = fmaf(v.y, sc, acc.y);
+    acc.z = fmaf(v.z, sc, acc.z);
+    acc.w = fmaf(v.w, sc, acc.w);
   }
-  reinterpret_cast<T*>(p.dk)[key * p.dks + (int64_t)b * p.dkb + (int64_t)h * p.dkh + c] = static_cast<T>(acc);
+  T* dst = reinterpret_cast<T*>(p.dk) + key * p.dks + (int64_t)b * p.dkb + (int64_t)h * p.dkh + c;
+  dst[0] = static_cast<T>(acc.x);
+  dst[1] = static_cast<T>(acc.y);
+  dst[2] = static_cast<T>(acc.z);
+  dst[3] = static_cast<T>(acc.w);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1110,36 +1121,52 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
   }
 }
 
-// out[l,b,h] = sum_s path_out[b*H+h][l*S+s] in path order (tensor-core forward)
+// out[l,b,h] = sum_s path_out[b*H+h][l*S+s] in path order (tensor-core forward); with
+// `base` (dq), base[l,b,h] + sum_s. One row (l, b, h) per D/4 threads, four channels each.
+template <typename T>
+__device__ __forceinline__ void blk_combine_rows(const BlkParams& p, const float* paths,
+                                                 const float* base, char* dst, int64_t ss,
+                                                 int64_t sb, int64_t sh) {
+  const int tpr = p.D >> 2, rpb = 256 / tpr;
+  const int rl = threadIdx.x / tpr, c = (threadIdx.x - rl * tpr) * 4;
+  if (rl >= rpb) return;
+  const int64_t row = (int64_t)blockIdx.x * rpb + rl;  // (l, b, h)
+  if (row >= (int64_t)p.L * p.B * p.H) return;
+  const int h = (int)(row % p.H);
+  const int64_t lb = row / p.H;
+  const int b = (int)(lb % p.B);
+  const int64_t l = lb / p.B;
+  float4 acc = base ? *reinterpret_cast<const float4*>(base + row * p.D + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const float* src = paths + (((int64_t)b * p.H + h) * p.P + l * p.S) * p.D + c;
+  for (int s = 0; s < p.S; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(src + (int64_t)s * p.D);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  T* o = reinterpret_cast<T*>(dst) + l * ss + (int64_t)b * sb + (int64_t)h * sh + c;
+  o[0] = static_cast<T>(acc.x);
+  o[1] = static_cast<T>(acc.y);
+  o[2] = static_cast<T>(acc.z);
+  o[3] = static_cast<T>(acc.w);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) blk_combine_out_kernel(const BlkParams p) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)p.L * p.B * p.H * p.D) return;
-  const int c = (int)(i % p.D);
-  const int64_t row = i / p.D;  // (l, b, h)
-  const int h = (int)(row % p.H);
-  const int b = (int)((row / p.H) % p.B);
-  const int64_t l = row / ((int64_t)p.H * p.B);
-  const float* src = p.path_out + (((int64_t)b * p.H + h) * p.P + l * p.S) * p.D + c;
-  float acc = 0.0f;
-  for (int s = 0; s < p.S; ++s) acc += src[(int64_t)s * p.D];
-  reinterpret_cast<T*>(p.out)[l * p.os + (int64_t)b * p.ob + (int64_t)h * p.oh + c] = static_cast<T>(acc);
+  blk_combine_rows<T>(p, p.path_out, nullptr, p.out, p.os, p.ob, p.oh);
 }
 
 // dq = tree part + sum_s leaf-block part of path s, in path order
 template <typename T>
 __global__ void __launch_bounds__(256) blk_combine_dq_kernel(const BlkParams p) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)p.L * p.B * p.H * p.D) return;
-  const int c = (int)(i % p.D);
-  const int64_t row = i / p.D;
-  const int h = (int)(row % p.H);
-  const int b = (int)((row / p.H) % p.B);
-  const int64_t l = row / ((int64_t)p.H * p.B);
-  float acc = p.dq_tree[row * p.D + c];
-  const float* src = p.dq_path + (((int64_t)b * p.H + h) * p.P + l * p.S) * p.D + c;
-  for (int s = 0; s < p.S; ++s) acc += src[(int64_t)s * p.D];
-  reinterpret_cast<T*>(p.dq)[l * p.dqs + (int64_t)b * p.dqb + (int64_t)h * p.dqh + c] = static_cast<T>(acc);
+  blk_combine_rows<T>(p, p.dq_path, p.dq_tree, p.dq, p.dqs, p.dqb, p.dqh);
+}
+
+// grid of the row kernels above: `rows` rows of D channels
+inline unsigned blk_row_grid(int64_t rows, int D) {
+  const int rpb = 256 / (D >> 2);
+  return (unsigned)((rows + rpb - 1) / rpb);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1373,8 +1400,7 @@ int blk_fwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
     if ((rc = check_launch("blocked leaf-block attention"))) return rc;
     {
       TA_PROFILE("blocked_combine", st);
-      const int64_t n = (int64_t)p.L * p.B * p.H * p.D;
-      blk_combine_out_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+      blk_combine_out_kernel<T><<<blk_row_grid((int64_t)p.L * p.B * p.H, p.D), 256, 0, st>>>(p);
     }
     return check_launch("blocked combine");
   }
@@ -1434,13 +1460,11 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
   }
   {
     TA_PROFILE("blocked_bwd_keys", st);
-    const int64_t m = (int64_t)p.B * p.H * p.N * p.D;
-    blk_bwd_key_kernel<T><<<(unsigned)((m + 255) / 256), 256, 0, st>>>(p);
+    blk_bwd_key_kernel<T><<<blk_row_grid((int64_t)p.B * p.H * p.N, p.D), 256, 0, st>>>(p);
   }
   if (mma) {
     TA_PROFILE("blocked_combine", st);
-    const int64_t n = (int64_t)p.L * p.B * p.H * p.D;
-    blk_combine_dq_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+    blk_combine_dq_kernel<T><<<blk_row_grid((int64_t)p.L * p.B * p.H, p.D), 256, 0, st>>>(p);
   }
   return check_launch("blocked backward (keys)");
 }
