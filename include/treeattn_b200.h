@@ -388,8 +388,9 @@ int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const t
 int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
                                      int32_t backward);
 /*
- * Process-wide choice of the tensor-core forward: 1 = tcgen05 with TMEM accumulators
- * (default), 0 = mma.sync. Returns the previous setting.
+ * Process-wide choice of the tensor-core forward: 1 = tcgen05 with TMEM accumulators, 0 =
+ * mma.sync (default; it measured faster at the benchmark configurations). Returns the previous
+ * setting.
  */
 int32_t ta_blocked_set_tcgen05(int32_t enable);
 /*

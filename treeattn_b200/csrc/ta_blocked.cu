@@ -131,7 +131,10 @@ extern "C" int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* c
 }
 
 namespace {
-int g_use_tcgen05 = 1;  // leaf-block forward on tcgen05 (1) or mma.sync (0)
+// leaf-block forward on tcgen05 (1) or mma.sync (0). mma.sync is the default: it measured
+// faster (config 2: 1.32 vs 1.54 ms per forward, config 3: 7.0 vs 9.6 ms), the tcgen05 kernel
+// serialising gather, MMA and epilogue per 128-pair tile at two CTAs per SM.
+int g_use_tcgen05 = 0;
 std::atomic<uint64_t> g_tc_wait_ns{kTcWaitNs};
 std::mutex g_tc_status_mu;
 int32_t* g_tc_status = nullptr;  // mapped, portable pinned host word (process-wide, sticky)
