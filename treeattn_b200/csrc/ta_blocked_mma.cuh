@@ -83,6 +83,16 @@ __device__ __forceinline__ void frag_b_kn(uint32_t* r, const uint16_t* base, int
   ldsm4t(r, base + (k0 + ((lane >> 3) & 1) * 8 + (lane & 7)) * ld + n0 + (lane >> 4) * 8);
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Keys of a leaf block a pair may attend: its first `visible_keys` keys (keys past the pair's
+// causal boundary `bnd` are masked; INT64_MAX = no boundary).
+template <int LB>
+__device__ __forceinline__ int visible_keys(int64_t bnd, int64_t key0) {
+  const int64_t v = bnd - key0 + 1;
+  return v >= LB ? LB : (v < 0 ? 0 : (int)v);
+}
+
 struct BlkMmaParams {
   const char* q; const char* k; const char* v; const char* dout;
   int64_t qs, qb, qh, ks, kb, kh, vs, vb, vh, gs, gb, gh;
@@ -194,16 +204,17 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
     }
     // masked softmax of rows g and g + 8 (quad lanes share a row)
     const int g = lane >> 2, tq = lane & 3;
-    const int64_t bnd0 = s_bnd[m0 + g], bnd1 = s_bnd[m0 + g + 8];
     const int64_t key0 = (int64_t)j * LB;
+    const int lim0 = visible_keys<LB>(s_bnd[m0 + g], key0), lim1 = visible_keys<LB>(s_bnd[m0 + g + 8], key0);
+    const float sl2 = p.scale * kLog2e;  // scores in base 2: exp(scale s) = exp2(scale log2(e) s)
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int t = 0; t < G::NT_S; ++t) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int64_t key = key0 + t * 8 + tq * 2 + e;
-        sc[t][e] = key > bnd0 ? -INFINITY : sc[t][e] * p.scale;
-        sc[t][2 + e] = key > bnd1 ? -INFINITY : sc[t][2 + e] * p.scale;
+        const int c = t * 8 + tq * 2 + e;
+        sc[t][e] = c >= lim0 ? -INFINITY : sc[t][e] * sl2;
+        sc[t][2 + e] = c >= lim1 ? -INFINITY : sc[t][2 + e] * sl2;
         mx0 = fmaxf(mx0, sc[t][e]);
         mx1 = fmaxf(mx1, sc[t][2 + e]);
       }
@@ -217,8 +228,8 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
     for (int t = 0; t < G::NT_S; ++t) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        sc[t][e] = expf(sc[t][e] - mx0);
-        sc[t][2 + e] = expf(sc[t][2 + e] - mx1);
+        sc[t][e] = exp2f(sc[t][e] - mx0);
+        sc[t][2 + e] = exp2f(sc[t][2 + e] - mx1);
         sum0 += sc[t][e];
         sum1 += sc[t][2 + e];
       }
@@ -428,15 +439,16 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
         }
       }
       const int r0 = m0 + g, r1 = m0 + g + 8;
-      const int64_t bnd0 = s_bnd[r0], bnd1 = s_bnd[r1];
+      const int lim0 = visible_keys<LB>(s_bnd[r0], key0), lim1 = visible_keys<LB>(s_bnd[r1], key0);
+      const float sl2 = p.scale * kLog2e;
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int t = 0; t < G::NT_S; ++t)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int64_t key = key0 + t * 8 + tq * 2 + e;
-          sc[t][e] = key > bnd0 ? -INFINITY : sc[t][e] * p.scale;
-          sc[t][2 + e] = key > bnd1 ? -INFINITY : sc[t][2 + e] * p.scale;
+          const int c = t * 8 + tq * 2 + e;
+          sc[t][e] = c >= lim0 ? -INFINITY : sc[t][e] * sl2;
+          sc[t][2 + e] = c >= lim1 ? -INFINITY : sc[t][2 + e] * sl2;
           mx0 = fmaxf(mx0, sc[t][e]);
           mx1 = fmaxf(mx1, sc[t][2 + e]);
         }
@@ -449,8 +461,8 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
       for (int t = 0; t < G::NT_S; ++t)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          sc[t][e] = r0 < n ? expf(sc[t][e] - mx0) : 0.0f;
-          sc[t][2 + e] = r1 < n ? expf(sc[t][2 + e] - mx1) : 0.0f;
+          sc[t][e] = r0 < n ? exp2f(sc[t][e] - mx0) : 0.0f;
+          sc[t][2 + e] = r1 < n ? exp2f(sc[t][2 + e] - mx1) : 0.0f;
           sum0 += sc[t][e];
           sum1 += sc[t][2 + e];
         }
