@@ -17,6 +17,8 @@
 
 #include <float.h>
 
+#include <type_traits>
+
 #include "ta_common.cuh"
 
 namespace ta {
@@ -238,6 +240,161 @@ __global__ void __launch_bounds__(256) gemm_kernel(const GemmParams g) {
   }
 }
 
+// The same products on the tensor cores (16-bit models): operands staged in shared memory as
+// 16-bit values -- a float32 operand (the leaf weights W, the coefficients C) as a high and a
+// low 16-bit part, Y = A_hi B + A_lo B (about 16 more mantissa bits than one part) -- and
+// multiplied with mma.sync m16n8k16 into float32. Tiles of BM x BN, BM = 16 (BN = 256, the
+// skinny query-block products) or 64 (BN = 64); each of the 4 warps owns 16 rows x 64 columns.
+// The summation order is fixed by the tile loop, so results are bitwise repeatable.
+template <typename T16> __device__ __forceinline__ uint16_t bits16(float x);
+template <> __device__ __forceinline__ uint16_t bits16<__nv_bfloat16>(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+template <> __device__ __forceinline__ uint16_t bits16<__half>(float x) {
+  return __half_as_ushort(__float2half_rn(x));
+}
+template <typename T16> __device__ __forceinline__ float from16(uint16_t r);
+template <> __device__ __forceinline__ float from16<__nv_bfloat16>(uint16_t r) { return __uint_as_float((uint32_t)r << 16); }
+template <> __device__ __forceinline__ float from16<__half>(uint16_t r) { return __half2float(__ushort_as_half(r)); }
+
+// Stage a [R rows][32 k] tile of an operand X[row * s_row + k * s_k] (float or 16-bit) into
+// 16-bit high (and, for float, low) parts. Eight consecutive elements along whichever axis is
+// contiguous are read per step, with one 16-byte (two for float) vector load when aligned.
+template <typename TX>
+__device__ __forceinline__ bool load8(const TX* ptr, bool ok, float* v) {
+  if (!ok) return false;
+  if constexpr (std::is_same<TX, float>::value) {
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return false;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(ptr));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(ptr) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return false;
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(ptr));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = from16<TX>((uint16_t)(w[j] & 0xffffu));
+      v[2 * j + 1] = from16<TX>((uint16_t)(w[j] >> 16));
+    }
+  }
+  return true;
+}
+
+template <typename TX, typename T16, bool SPLIT, int R>
+__device__ __forceinline__ void stage_tile(const TX* X, int64_t s_row, int64_t s_k, int r0, int nrows,
+                                           int k0, int kend, uint16_t (*hi)[40], uint16_t (*lo)[40],
+                                           int tid) {
+  constexpr int BK = 32;
+  auto put = [&](int rr, int kk, float x) {
+    const uint16_t h = bits16<T16>(x);
+    hi[rr][kk] = h;
+    if constexpr (SPLIT) lo[rr][kk] = bits16<T16>(x - from16<T16>(h));
+  };
+  if (s_k == 1) {  // contiguous along k
+    for (int i = tid; i < R * (BK / 8); i += 128) {
+      const int rr = i / (BK / 8), kc = (i % (BK / 8)) * 8;
+      const int r = r0 + rr, k = k0 + kc;
+      const TX* ptr = X + (int64_t)r * s_row + k;
+      float v[8];
+      if (!load8(ptr, r < nrows && k + 8 <= kend, v))
+        for (int j = 0; j < 8; ++j) v[j] = (r < nrows && k + j < kend) ? static_cast<float>(ptr[j]) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) put(rr, kc + j, v[j]);
+    }
+  } else if (s_row == 1) {  // contiguous along the rows
+    for (int i = tid; i < BK * (R / 8); i += 128) {
+      const int kk = i / (R / 8), rc = (i % (R / 8)) * 8;
+      const int r = r0 + rc, k = k0 + kk;
+      const TX* ptr = X + r + (int64_t)k * s_k;
+      float v[8];
+      if (!load8(ptr, k < kend && r + 8 <= nrows, v))
+        for (int j = 0; j < 8; ++j) v[j] = (k < kend && r + j < nrows) ? static_cast<float>(ptr[j]) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) put(rc + j, kk, v[j]);
+    }
+  } else {
+    for (int i = tid; i < R * BK; i += 128) {
+      const int rr = i / BK, kk = i % BK;
+      const int r = r0 + rr, k = k0 + kk;
+      put(rr, kk, (r < nrows && k < kend) ? static_cast<float>(X[(int64_t)r * s_row + (int64_t)k * s_k]) : 0.0f);
+    }
+  }
+}
+
+template <typename TA_, typename TB_, typename TY, typename T16, int BM>
+__global__ void __launch_bounds__(128) gemm_mma_kernel(const GemmParams g) {
+  constexpr int BN = BM == 16 ? 256 : 64;
+  constexpr int BK = 32, LDS = BK + 8;
+  constexpr bool AF = std::is_same<TA_, float>::value, BF = std::is_same<TB_, float>::value;
+  __shared__ __align__(16) uint16_t sAh[BM][LDS];
+  __shared__ __align__(16) uint16_t sAl[AF ? BM : 1][LDS];
+  __shared__ __align__(16) uint16_t sBh[BN][LDS];
+  __shared__ __align__(16) uint16_t sBl[BF ? BN : 1][LDS];
+  const int z = blockIdx.z;
+  const int split = z % g.splits, bh = z / g.splits;
+  const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = BM == 64 ? warp * 16 : 0, wn = BM == 64 ? 0 : warp * 64;
+  const TA_* A = reinterpret_cast<const TA_*>(g.A) + (int64_t)b * g.sAb + (int64_t)h * g.sAh;
+  const TB_* Bm = reinterpret_cast<const TB_*>(g.Bm) + (int64_t)b * g.sBb + (int64_t)h * g.sBh;
+  const int kbeg = split * g.kchunk;
+  const int kend = min(g.Kd, kbeg + g.kchunk);
+  float acc[8][4] = {};
+  for (int k0 = kbeg; k0 < kend; k0 += BK) {
+    // eight consecutive elements along the operand's contiguous axis per load (16-byte vector
+    // loads where aligned), written to the [row][k] tiles
+    stage_tile<TA_, T16, AF, BM>(A, g.sAm, g.sAk, m0, g.M, k0, kend, sAh, sAl, tid);
+    stage_tile<TB_, T16, BF, BN>(Bm, g.sBn, g.sBk, n0, g.Nn, k0, kend, sBh, sBl, tid);
+    __syncthreads();
+#pragma unroll
+    for (int ks = 0; ks < BK; ks += 16) {
+      uint32_t ah[4], al[4];
+      ldsm_x4(ah, &sAh[wm + (lane & 15)][ks + (lane >> 4) * 8]);
+      if constexpr (AF) ldsm_x4(al, &sAl[wm + (lane & 15)][ks + (lane >> 4) * 8]);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int nr = wn + np * 16 + (lane >> 4) * 8 + (lane & 7);
+        const int kc = ks + ((lane >> 3) & 1) * 8;
+        uint32_t bh4[4];
+        ldsm_x4(bh4, &sBh[nr][kc]);
+        Mma16<T16>::mma(acc[2 * np], ah, bh4);
+        Mma16<T16>::mma(acc[2 * np + 1], ah, bh4 + 2);
+        if constexpr (AF) {
+          Mma16<T16>::mma(acc[2 * np], al, bh4);
+          Mma16<T16>::mma(acc[2 * np + 1], al, bh4 + 2);
+        }
+        if constexpr (BF) {
+          uint32_t bl4[4];
+          ldsm_x4(bl4, &sBl[nr][kc]);
+          Mma16<T16>::mma(acc[2 * np], ah, bl4);
+          Mma16<T16>::mma(acc[2 * np + 1], ah, bl4 + 2);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int gq = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int m = m0 + wm + gq + (e >> 1) * 8;
+      const int n = n0 + wn + t * 8 + tq * 2 + (e & 1);
+      if (m >= g.M || n >= g.Nn) continue;
+      if (g.splits > 1) {
+        const int64_t BHn = gridDim.z / g.splits;
+        g.partial[(((int64_t)split * BHn + bh) * g.M + m) * g.Nn + n] = acc[t][e];
+        continue;
+      }
+      const int64_t off = (int64_t)b * g.sYb + (int64_t)h * g.sYh + (int64_t)m * g.sYm + (int64_t)n * g.sYn;
+      TY* y = reinterpret_cast<TY*>(g.Y) + off;
+      *y = static_cast<TY>(g.accumulate ? static_cast<float>(*y) + acc[t][e] : acc[t][e]);
+    }
+  }
+}
+
 template <typename TY>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const GemmParams g, int BH) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -274,11 +431,26 @@ static void launch_gemm(GemmParams g, int BH, cudaStream_t st, const char* what)
   g.kchunk = splits > 1 ? ((g.Kd + splits - 1) / splits + 15) / 16 * 16 : g.Kd;
   if (splits > 1) splits = (g.Kd + g.kchunk - 1) / g.kchunk;
   g.splits = splits;
-  const dim3 grid((unsigned)((g.Nn + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM),
-                  (unsigned)(BH * splits));
-  if (BM == 16) gemm_kernel<TA_, TB_, TY, 16><<<grid, 256, 0, st>>>(g);
-  else if (BM == 32) gemm_kernel<TA_, TB_, TY, 32><<<grid, 256, 0, st>>>(g);
-  else gemm_kernel<TA_, TB_, TY, 64><<<grid, 256, 0, st>>>(g);
+  // 16-bit models: the tensor-core kernel (its 16-bit type is the model's, whichever operand
+  // carries it); float32 models keep the CUDA-core kernel
+  using T16 = typename std::conditional<std::is_same<TA_, float>::value, TB_, TA_>::type;
+  // (short reductions -- dV and dK over one query block -- are bound by their output tiles and
+  // stay on the CUDA-core kernel, whose epilogue writes whole row segments)
+  if (!std::is_same<T16, float>::value && g.Kd >= 128) {
+    const int MB = BM == 16 ? 16 : 64, NB = MB == 16 ? 256 : 64;
+    const dim3 mgrid((unsigned)((g.Nn + NB - 1) / NB), (unsigned)((g.M + MB - 1) / MB),
+                     (unsigned)(BH * splits));
+    if constexpr (!std::is_same<T16, float>::value) {
+      if (MB == 16) gemm_mma_kernel<TA_, TB_, TY, T16, 16><<<mgrid, 128, 0, st>>>(g);
+      else gemm_mma_kernel<TA_, TB_, TY, T16, 64><<<mgrid, 128, 0, st>>>(g);
+    }
+  } else {
+    const dim3 grid((unsigned)((g.Nn + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM),
+                    (unsigned)(BH * splits));
+    if (BM == 16) gemm_kernel<TA_, TB_, TY, 16><<<grid, 256, 0, st>>>(g);
+    else if (BM == 32) gemm_kernel<TA_, TB_, TY, 32><<<grid, 256, 0, st>>>(g);
+    else gemm_kernel<TA_, TB_, TY, 64><<<grid, 256, 0, st>>>(g);
+  }
   if (splits > 1) {
     const int64_t n = (int64_t)BH * g.M * g.Nn;
     split_reduce_kernel<TY><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, BH);
