@@ -106,10 +106,10 @@ __host__ __device__ inline size_t mma_node_smem(int D, int ln) {
 }
 constexpr size_t kMaxBlockSmem = 227 * 1024;
 
-// The tensor-core node pass serves bf16 inputs whose head_dim is a multiple of 32 (<= 256)
+// The tensor-core node pass serves 16-bit inputs whose head_dim is a multiple of 32 (<= 256)
 // and whose CTA fits the shared-memory limit.
 inline bool use_mma_node_pass(int32_t dtype, int64_t D, int ln) {
-  return dtype == TA_BF16 && D % 32 == 0 && D <= 256 && D / 32 != 5 && D / 32 != 6 && D / 32 != 7 &&
+  return (dtype == TA_BF16 || dtype == TA_F16) && D % 32 == 0 && D <= 256 && D / 32 != 5 && D / 32 != 6 && D / 32 != 7 &&
          mma_node_smem((int)D, ln) <= kMaxBlockSmem;
 }
 
@@ -966,16 +966,16 @@ template <typename T>
 int run_rest(BwdParams& p, cudaStream_t st) {
   int rc = run_sort(p, st);
   if (rc) return rc;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+  if constexpr (sizeof(T) == 2) {
     if (p.chunk == kChunkMma) {
       {
         TA_PROFILE("bwd_node", st);
         switch (p.D / 32) {
-          case 1: launch_node_mma<1>(p, st); break;
-          case 2: launch_node_mma<2>(p, st); break;
-          case 3: launch_node_mma<3>(p, st); break;
-          case 4: launch_node_mma<4>(p, st); break;
-          default: launch_node_mma<8>(p, st); break;
+          case 1: launch_node_mma<T, 1>(p, st); break;
+          case 2: launch_node_mma<T, 2>(p, st); break;
+          case 3: launch_node_mma<T, 3>(p, st); break;
+          case 4: launch_node_mma<T, 4>(p, st); break;
+          default: launch_node_mma<T, 8>(p, st); break;
         }
       }
       if ((rc = check_launch("backward node pass"))) return rc;

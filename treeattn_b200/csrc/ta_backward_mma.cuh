@@ -41,10 +41,9 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int n) {
 
 
 // NT = n8 tiles per warp (D / 32)
-template <int NT>
+template <typename T, int NT>
 __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdParams p, int range_chunks,
                                                                       int ranges_per_seg) {
-  using T = __nv_bfloat16;
   extern __shared__ __align__(16) unsigned char s_mma[];
   const int D = p.D;
   const int RS = mma_row_stride(D);
@@ -251,8 +250,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
                 s_rlev[row] = d;
               }
               const float c = s_co[d * kMmaChunk + pt];
-              const T hi = __float2bfloat16_rn(c);
-              s_G[row * kGStride + upper * kMmaChunk + pt] = upper ? __float2bfloat16_rn(c - __bfloat162float(hi)) : hi;
+              const T hi = to_t<T>(c);
+              s_G[row * kGStride + upper * kMmaChunk + pt] = upper ? to_t<T>(c - static_cast<float>(hi)) : hi;
               wrote |= 1u << row;
             }
           }
@@ -275,7 +274,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
           for (int nt = 0; nt < NT; ++nt) {
             uint32_t bfr[2];
             ldsm_x2_trans(bfr, s_b + (kb + (lane & 15)) * RS + n0 + nt * 8);
-            mma_bf16(acc[nt], afr, bfr);
+            Mma16<T>::mma(acc[nt], afr, bfr);
           }
         }
         // epilogue. A node open from the previous sub-chunk adds its carried row; a node
@@ -318,14 +317,14 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
               const int64_t node = ((int64_t)1 << d) - 1 + pre;
               char* rowp = dkb + node * p.dks * dk_es;
               if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = v;
-              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(v.x, v.y);
+              else *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(rowp) + c) = Elem<T>::pack2(v.x, v.y);
             } else {
               const int64_t leaf = (int64_t)pre + base_node - K;
               if (p.dv_f32)
                 *reinterpret_cast<float2*>(reinterpret_cast<float*>(dvb + leaf * p.dvs * 4) + c) = v;
               else
-                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
-                    __floats2bfloat162_rn(v.x, v.y);
+                *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(dvb + leaf * p.dvs * 2) + c) =
+                    Elem<T>::pack2(v.x, v.y);
             }
           }
           if ((warp & 3) == 0 && t == 0) {
@@ -340,7 +339,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
         while (wrote) {
           const int row = __ffs(wrote) - 1;
           wrote &= wrote - 1;
-          s_G[row * kGStride + upper * kMmaChunk + pt] = __float2bfloat16_rn(0.0f);
+          s_G[row * kGStride + upper * kMmaChunk + pt] = to_t<T>(0.0f);
         }
       }
       if (pass == 0) {  // s_q is free: gather the next sub-chunk's q rows behind the dV product
@@ -358,13 +357,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
           char* rowp = dkb + (((int64_t)1 << d) - 1 + pf) * zrow_dk;
           for (int c = 0; c < D; c += 2) {
             if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-            else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+            else *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(rowp) + c) = 0u;
           }
         } else {
           char* rowp = dvb + (pf + base_node - K) * zrow_dv;
           for (int c = 0; c < D; c += 2) {
             if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-            else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+            else *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(rowp) + c) = 0u;
           }
         }
       };
@@ -405,11 +404,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) bwd_node_mma_kernel(const BwdP
             if (d < ln) {
               char* rowp = dkb + (((int64_t)1 << d) - 1 + pf) * p.dks * dk_es;
               if (p.dk_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+              else *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(rowp) + c) = 0u;
             } else {
               char* rowp = dvb + (pf + base_node - K) * p.dvs * dv_es;
               if (p.dv_f32) *reinterpret_cast<float2*>(reinterpret_cast<float*>(rowp) + c) = make_float2(0.0f, 0.0f);
-              else *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<T*>(rowp) + c) = __floats2bfloat162_rn(0.0f, 0.0f);
+              else *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(rowp) + c) = 0u;
             }
           }
         }
@@ -436,14 +435,14 @@ inline void node_mma_ranges(const BwdParams& p, int& range_chunks, int& ranges_p
   ranges_per_seg = (int)((p.chunks_per_seg + rc - 1) / rc);
 }
 
-template <int NT>
+template <typename T, int NT>
 void launch_node_mma(const BwdParams& p, cudaStream_t st) {
   const size_t smem = mma_node_smem(p.D, p.log_n);
-  cudaFuncSetAttribute(bwd_node_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(bwd_node_mma_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int range_chunks, ranges_per_seg;
   node_mma_ranges(p, range_chunks, ranges_per_seg);
   const int64_t ranges = (int64_t)p.B * p.H * ranges_per_seg;
-  bwd_node_mma_kernel<NT><<<(unsigned)ranges, kMmaThreads, smem, st>>>(p, range_chunks, ranges_per_seg);
+  bwd_node_mma_kernel<T, NT><<<(unsigned)ranges, kMmaThreads, smem, st>>>(p, range_chunks, ranges_per_seg);
 }
 
 }  // namespace ta

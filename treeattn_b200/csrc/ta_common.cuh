@@ -95,6 +95,11 @@ template <> struct Elem<__half> {
   }
 };
 
+// float -> element type, round to nearest even
+template <typename T> __device__ __forceinline__ T to_t(float x);
+template <> __device__ __forceinline__ __nv_bfloat16 to_t<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half to_t<__half>(float x) { return __float2half_rn(x); }
+
 // Dot-product step over one 16-byte chunk: acc += sum_e a[e] * b[e] in element order, with
 // float32 accumulation. 16-bit types use the sm_100 mixed-precision FMA (bf16/f16 operands,
 // f32 accumulate), which is exactly the f32 FMA of the widened operands.
