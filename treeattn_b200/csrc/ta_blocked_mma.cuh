@@ -374,15 +374,37 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
 #pragma unroll
     for (int e = 0; e < 4; ++e) adv[t][e] = adk[t][e] = 0.0f;
   const int64_t key0 = (int64_t)j * LB;
+  __shared__ uint32_t s_path[128], s_lq[128];  // the tile's (query, path) pairs and queries
+  const int zsh = zmt == 1 ? 4 : 5;  // log2 of the dz tile width (16 or 32 rows of DF)
   for (int64_t t0 = beg; t0 < end; t0 += 128) {
     const int n = (int)min((int64_t)128, end - t0);
+    __syncthreads();
+    if (tid < 128) {
+      // per pair, once: its path, query, causal boundary, delta and weight
+      int64_t bnd = INT64_MAX;
+      float dl = 0.0f, w = 0.0f;
+      uint32_t path = 0, l = 0;
+      if (tid < n) {
+        path = vals[t0 + tid];
+        l = path / (uint32_t)p.S;
+        const uint32_t s = path - l * (uint32_t)p.S;
+        if (p.causal) bnd = (p.row0 + (int64_t)l) + p.N - p.row_total;
+        dl = p.delta[(int64_t)bh * p.P + path];
+        w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
+      }
+      s_path[tid] = path;
+      s_lq[tid] = l;
+      s_bnd[tid] = bnd;
+      s_delta[tid] = dl;
+      s_w[tid] = w;
+    }
     __syncthreads();
     for (int i = tid; i < 128 * CPR; i += blockDim.x) {
       const int r = i / CPR, c = i - r * CPR;
       uint16_t* dq_ = s_q + r * G::LD + c * 8;
       uint16_t* dg_ = s_g + r * G::LD + c * 8;
       if (r < n) {
-        const int64_t l = vals[t0 + r] / p.S;
+        const int64_t l = s_lq[r];
         cp_async16(dq_, p.q + (l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2 + c * 16);
         cp_async16(dg_, p.dout + (l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * 2 + c * 16);
       } else {
@@ -390,23 +412,9 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
         *reinterpret_cast<uint4*>(dg_) = make_uint4(0, 0, 0, 0);
       }
     }
-    if (tid < 128) {
-      int64_t bnd = INT64_MAX;
-      float dl = 0.0f, w = 0.0f;
-      if (tid < n) {
-        const int64_t path = vals[t0 + tid];
-        const int64_t l = path / p.S, s = path - l * p.S;
-        if (p.causal) bnd = (p.row0 + l) + p.N - p.row_total;
-        dl = p.delta[(int64_t)bh * p.P + path];
-        w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s];
-      }
-      s_bnd[tid] = bnd;
-      s_delta[tid] = dl;
-      s_w[tid] = w;
-    }
-    for (int i = tid; i < 128 * zmt * 16; i += blockDim.x) {
-      const int r = i / (zmt * 16), c = i - r * (zmt * 16);
-      const float z = (r < n && c < DF) ? p.dz_rows[((int64_t)bh * p.P + vals[t0 + r]) * DF + c] : 0.0f;
+    for (int i = tid; i < (128 << zsh); i += blockDim.x) {
+      const int r = i >> zsh, c = i & ((1 << zsh) - 1);
+      const float z = (r < n && c < DF) ? p.dz_rows[((int64_t)bh * p.P + s_path[r]) * DF + c] : 0.0f;
       const uint16_t hi = Mma<T>::half_bits(z);
       s_zh[r * kZLd + c] = hi;
       s_zl[r * kZLd + c] = Mma<T>::half_bits(z - raw_to_float<T>(hi));
@@ -503,13 +511,13 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
         }
       }
       if (r0 < n) {
-        float* dst = p.dq_path + ((int64_t)bh * p.P + vals[t0 + r0]) * D;
+        float* dst = p.dq_path + ((int64_t)bh * p.P + s_path[r0]) * D;
 #pragma unroll
         for (int t = 0; t < G::NT_D; ++t)
           *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(dq[t][0] * p.scale, dq[t][1] * p.scale);
       }
       if (r1 < n) {
-        float* dst = p.dq_path + ((int64_t)bh * p.P + vals[t0 + r1]) * D;
+        float* dst = p.dq_path + ((int64_t)bh * p.P + s_path[r1]) * D;
 #pragma unroll
         for (int t = 0; t < G::NT_D; ++t)
           *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(dq[t][2] * p.scale, dq[t][3] * p.scale);
