@@ -132,6 +132,34 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def bind_local_cpus(dev) -> dict:
+    """Pin this process to the host cores of its GPU's NUMA node (sysfs ``local_cpulist`` of
+    the GPU's PCI function), so pinned host buffers allocated afterwards are first-touched on
+    the GPU's own socket. Returns what was found, for the bench line."""
+    import torch
+
+    pr = torch.cuda.get_device_properties(dev)
+    bdf = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+    base = os.path.join("/sys/bus/pci/devices", bdf)
+    info = {"pci": bdf}
+    try:
+        with open(os.path.join(base, "numa_node")) as f:
+            info["numa_node"] = int(f.read().strip())
+        with open(os.path.join(base, "local_cpulist")) as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            info["cpus"] = len(cpus)
+    except (OSError, ValueError) as e:
+        info["error"] = str(e)[:80]
+    return info
+
+
 # ---------------------------------------------------------------------------------------
 # algorithmic bytes per launch (compulsory unique traffic of each kernel)
 # ---------------------------------------------------------------------------------------
@@ -397,6 +425,7 @@ def run_ours(args):
     # upload and step i-1's download overlap step i's kernels; the events bracket all of it.
     e2e = None
     if not args.no_e2e:
+        numa = bind_local_cpus(dev) if world > 1 else None
         hq, hk, hv, hgo = (t.detach().cpu().pin_memory() for t in (q, k, v, go))
         hout, hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(4))
         bufs = [[torch.empty_like(t) for t in (q, k, v, go)] for _ in range(2)]
@@ -452,6 +481,26 @@ def run_ours(args):
         e2e = {"value": tokens_step / (ems / args.steps / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
                "ms_per_step": ems / args.steps}
+        # the host link alone: every rank uploads its four inputs at once, then downloads
+        # them (pinned memory, one stream); the slowest rank's rate, GB/s per rank
+        link = {}
+        for name, pairs in (("h2d", [(b, h) for b, h in zip(bufs[0], (hq, hk, hv, hgo))]),
+                            ("d2h", [(h, b) for b, h in zip(bufs[0], (hout, hdq, hdk, hdv))])):
+            barrier()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for dst, src in pairs:
+                dst.copy_(src, non_blocking=True)
+            c1.record(stream)
+            barrier()
+            cms = c0.elapsed_time(c1)
+            if world > 1:
+                tm = torch.tensor([cms], device=dev, dtype=torch.float64)
+                dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+                cms = float(tm.item())
+            link[name + "_gbs_per_rank"] = 4 * nbytes / (cms / 1e3) / 1e9
+        e2e["host_link"] = {**link, "ranks_at_once": world,
+                            **({"numa": numa} if numa else {})}
 
     # FA2 beside every N (each rank its own batch element), then the configs 3 and 4 records
     fa2_ms = None if args.no_fa2 else _fa2_ms((B, S, H, D), dtype, False, args.steps, args.warmup,
@@ -500,6 +549,7 @@ def run_ours(args):
                                   "each rank draws its slice of the global problem's noise)",
                    "l2": "inputs larger than L2 (q, k, v, grad_out: 4 x %d MiB)" % (B * S * H * D * 2 >> 20)},
         "value_per_gpu": value / world,
+        "value_is": "whole-job tokens/s over all GPUs (value_per_gpu: per GPU)",
         "gpu_launches": int(sum(c for c, _ in prof.values())),
         "kernels": kernels,
         "roofline": roof,

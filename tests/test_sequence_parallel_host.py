@@ -8,6 +8,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from treeattn_b200 import sequence_parallel as sp
 from treeattn_b200.sequence_parallel import TorchDistComm, plan, sp_tree_attention
 
 
@@ -28,6 +29,16 @@ def test_plan_covers_queries_in_order(N, R, S, causal):
     else:
         assert exact_q == []
         assert sampled_t == list(range(N))
+
+
+def test_prefix_balance_rule():
+    # the exact prefix (first S queries) splits by heads only inside rank 0's chunk with H % R == 0
+    assert plan(64, 2, 0, 8, True).prefix == 8
+    assert plan(64, 2, 1, 8, True).balanced(2, 4)
+    assert not plan(64, 2, 1, 8, True).balanced(2, 3)
+    assert not plan(64, 8, 0, 16, True).balanced(8, 8)   # chunk 8 < prefix 16
+    assert not plan(64, 2, 0, 8, False).balanced(2, 4)
+    assert not plan(8, 2, 0, 8, True).balanced(2, 4)     # N <= S: no hybrid prefix
 
 
 def test_plan_rejects_uneven_splits():
@@ -62,6 +73,17 @@ def _worker(rank, world, port, q):
         comm.reduce_scatter_seq(mine, full)
         tot = sum(r + 1 for r in range(world))
         ok_rs = torch.equal(mine, torch.arange(n * world * 5, dtype=torch.float32).view(n * world, 5)[rank * n:(rank + 1) * n] * tot)
+        # the balanced exact prefix: rank 0's rows reach every rank, head slices come back
+        E, B, H, D = 2, 1, 4, 3
+        rows = torch.arange(E * B * H * D, dtype=torch.float32).view(E, B, H, D) + 100 * rank
+        got = sp._from_rank0(comm, rows)
+        ok_bcast = torch.equal(got, rows - 100 * rank)
+        hs = sp._prefix_heads(comm, H)
+        dst = torch.zeros(E, B, H, D)
+        sp._heads_to_rank0(comm, dst, got[:, :, hs].contiguous() * 2)
+        ok_heads = (not torch.equal(dst, torch.zeros_like(dst))) if rank == 0 else True
+        ok_heads = ok_heads and (rank != 0 or torch.equal(dst, 2 * (rows - 100 * rank)))
+        ok_gather = ok_gather and ok_bcast and ok_heads
         # the public entry point validates shapes before any device work
         ok_err = False
         try:

@@ -21,6 +21,15 @@ Noise: non-causal, each rank fills its query rows of the global per-depth draws
 (t * log2 N + d steps), so a rank starts at its first sampled query's offset. Every rank
 advances its generator by the full problem's draw, like the unsharded call.
 
+Causal hybrid: the first S = num_samples queries take the exact path, which reads the whole
+tree of every head (O(N·D) per query and head). They all sit on rank 0, so when H divides by
+R every rank runs the exact prefix for its own H/R heads instead: rank 0's prefix rows of q
+(and, in the backward, of grad_out) are all-gathered (S·B·H·D elements), each rank adds its
+heads' exact dK/dV into the full-size partials that are reduce-scattered anyway, and the
+prefix rows of out and dq come back to rank 0 through one more all-gather. The exact GEMMs'
+split-K slicing depends on the number of heads, so those S rows of out equal the unsharded
+call's up to float32 summation order; every sampled row stays bit-identical.
+
 ``comm`` is any object with ``rank``, ``world``, ``all_gather_seq(out, chunk)`` and
 ``reduce_scatter_seq(out_chunk, full)`` along dim 0; ``TorchDistComm`` is the NCCL one.
 """
@@ -73,6 +82,13 @@ class SpPlan:
     exact: int            # local queries [0, exact) take the exact causal path
     sampled_t0: int       # index of the first sampled query in the global sampled order
     causal: bool
+    prefix: int = 0       # global exact queries [0, prefix) (causal hybrid)
+
+    def balanced(self, world: int, heads: int) -> bool:
+        """True when the exact prefix is split over the ranks by heads: it lies inside rank
+        0's chunk and the heads divide evenly (``BALANCE_PREFIX`` switches it off)."""
+        return (BALANCE_PREFIX and world > 1 and 0 < self.prefix <= self.chunk
+                and heads % world == 0)
 
     @property
     def sampled_offset(self) -> int:
@@ -97,7 +113,34 @@ def plan(seq_len: int, world: int, rank: int, num_samples: int, causal: bool) ->
     hybrid = seq_len > num_samples
     exact = min(max(num_samples - q0, 0), n) if hybrid else 0
     t0 = q0 + exact - (num_samples if hybrid else 0)
-    return SpPlan(seq_len, n, q0, exact, t0, True)
+    return SpPlan(seq_len, n, q0, exact, t0, True, num_samples if hybrid else 0)
+
+
+BALANCE_PREFIX = True
+
+
+def _prefix_heads(comm, heads: int) -> slice:
+    hr = heads // comm.world
+    return slice(comm.rank * hr, (comm.rank + 1) * hr)
+
+
+def _from_rank0(comm, rows: torch.Tensor) -> torch.Tensor:
+    """Rank 0's (E, B, H, D) rows on every rank (all-gather; the other ranks' slots unused)."""
+    E = rows.shape[0]
+    buf = torch.empty((comm.world * E,) + tuple(rows.shape[1:]), device=rows.device,
+                      dtype=rows.dtype)
+    comm.all_gather_seq(buf, rows)
+    return buf[:E]
+
+
+def _heads_to_rank0(comm, dst, part: torch.Tensor) -> None:
+    """Every rank's (E, B, H/R, D) head slice into rank 0's (E, B, H, D) ``dst``."""
+    E, B, hr, D = part.shape
+    R = comm.world
+    buf = torch.empty((R * E, B, hr, D), device=part.device, dtype=part.dtype)
+    comm.all_gather_seq(buf, part)
+    if comm.rank == 0:
+        dst.copy_(buf.view(R, E, B, hr, D).permute(1, 2, 0, 3, 4).reshape(E, B, R * hr, D))
 
 
 def _offset_rng(base, draws: int):
@@ -123,6 +166,7 @@ class SpSaved:
     plan: SpPlan
     num_samples: int
     tensors: tuple
+    prefix_q: torch.Tensor | None = None   # rank 0's prefix query rows (balanced prefix)
 
 
 def sp_forward(q, k, v, num_samples: int, causal: bool, comm, rng):
@@ -144,14 +188,22 @@ def sp_forward(q, k, v, num_samples: int, causal: bool, comm, rng):
         res = ops.forward(qv, k_int, vf, S, out=ov, rng=rng, query_rows=(p.q0, N))
         return out, SpSaved(p, S, (q, k_int, vf, res.leaf, res.weights, res.branch_prob))
     e = p.exact
-    if e:
+    qpre = None
+    if p.balanced(R, H):
+        E, hs = p.prefix, _prefix_heads(comm, H)
+        qpre = _from_rank0(comm, qv[:E])
+        opart = torch.empty((E, B, hs.stop - hs.start, D), device=dev, dtype=q.dtype)
+        ops.exact_forward(qpre[:, :, hs], k_int[:, :, hs], vf[:, :, hs], True, 0, out=opart,
+                          want_weights=False)
+        _heads_to_rank0(comm, ov[:E], opart)
+    elif e:
         ops.exact_forward(qv[:e], k_int, vf, True, p.q0, out=ov[:e], want_weights=False)
     saved = (q, k_int, vf)
     if e < n:
         rng_l = _offset_rng(rng, p.sampled_t0 * ops.log_n_of(N))
         _, st = ops.causal_forward(qv[e:], k_int, vf, S, p.sampled_offset, out=ov[e:], rng=rng_l)
         saved += (st.leaf, st.weights, st.branch_prob, st.corrected, st.masses)
-    return out, SpSaved(p, S, saved)
+    return out, SpSaved(p, S, saved, qpre)
 
 
 def sp_backward(saved: SpSaved, grad_out, comm):
@@ -178,7 +230,15 @@ def sp_backward(saved: SpSaved, grad_out, comm):
         else:
             dk_int.zero_()
             dv32.zero_()
-        if e:
+        if saved.prefix_q is not None:
+            E, hs, qpre = p.prefix, _prefix_heads(comm, H), saved.prefix_q
+            gpre = _from_rank0(comm, gv[:E])
+            dqpart = torch.empty((E, B, hs.stop - hs.start, D), device=dev, dtype=q.dtype)
+            ops.exact_backward(qpre[:, :, hs], k_int[:, :, hs], vf[:, :, hs], gpre[:, :, hs], True,
+                               0, dq=dqpart, dk=dk_int[:, :, hs], dv=dv32[:, :, hs],
+                               accumulate=True)
+            _heads_to_rank0(comm, dqv[:E], dqpart)
+        elif e:
             ops.exact_backward(qv[:e], k_int, vf, gv[:e], True, p.q0, dq=dqv[:e], dk=dk_int,
                                dv=dv32, accumulate=True)
     dk32 = torch.empty((N, B, H, D), device=dev, dtype=torch.float32)
