@@ -381,9 +381,11 @@ int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const t
 /*
  * Leaf-block attention on the tensor cores (16-bit inputs, head_dim 64 or 128, leaf block 16..128;
  * the backward also needs leaf_block >= 32 and leaf_block * head_dim <= 8192): the forward then
- * takes `path_out` (float32 [B*H][L*S][D], w_s * o_s per path, kept for the backward) and a
- * workspace of ta_blocked_forward_workspace_size bytes; with path_out NULL (or for other shapes)
- * everything runs on the CUDA cores. ta_blocked_uses_tensor_cores tells which.
+ * takes `path_out` (float32: [B*H][L*S][D] rows of w_s * o_s per path followed by [B*H][L*S]
+ * base-2 log-sum-exps of each path's scaled leaf-block scores, B*H*L*S*(D+1) floats in all,
+ * kept for the backward) and a workspace of ta_blocked_forward_workspace_size bytes; with
+ * path_out NULL (or for other shapes) everything runs on the CUDA cores.
+ * ta_blocked_uses_tensor_cores tells which.
  */
 int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cfg,
                                      int32_t backward);
@@ -394,7 +396,13 @@ int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cf
  */
 int32_t ta_blocked_set_tcgen05(int32_t enable);
 /*
- * Every mbarrier wait of the tcgen05 forward is bounded (default 1 s). A CTA whose wait
+ * Process-wide choice of the tensor-core backward for (leaf_block, head_dim) = (128, 64) and
+ * (64, 128): 1 = tcgen05 with TMEM accumulators (default), 0 = mma.sync. Other shapes always
+ * use mma.sync. Returns the previous setting. (No reference counterpart.)
+ */
+int32_t ta_blocked_set_tcgen05_backward(int32_t enable);
+/*
+ * Every mbarrier wait of the tcgen05 kernels is bounded (default 1 s). A CTA whose wait
  * expires records it in a process-wide status word in mapped host memory, waits for its
  * issued MMA, frees its TMEM and returns; that call's results are invalid. The word is read
  * without a device synchronisation: ta_blocked_status returns it (1 = an expired wait since

@@ -1,9 +1,10 @@
-"""The tcgen05 (TMEM) leaf-block forward against the mma.sync one on the same sampled paths,
-and its bounded-wait status word."""
+"""The tcgen05 (TMEM) leaf-block forward and backward against the mma.sync ones on the same
+sampled paths, and their bounded-wait status word."""
 
 import pytest
 import torch
 
+from tests.tolerance import assert_within
 from treeattn_b200 import _lib as L
 from treeattn_b200 import blocked as TB
 
@@ -65,3 +66,68 @@ def test_expired_wait_is_reported_by_the_next_call():
         assert torch.isfinite(out).all() and lib.ta_blocked_status(0) == 0
     finally:
         lib.ta_blocked_set_tcgen05(old_tc)
+
+
+def _fwd_bwd(q, k, v, go, causal, S, f, Lb, tc_bwd):
+    lib = L.load()
+    old = lib.ta_blocked_set_tcgen05_backward(1 if tc_bwd else 0)
+    try:
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        torch.manual_seed(7)
+        out, blk, _ = TB.blocked_tree_attention(qq, kk, vv, causal, None, num_samples=S, fanout=f,
+                                                leaf_block=Lb, return_paths=True)
+        out.backward(go)
+        torch.cuda.synchronize()
+        return blk, qq.grad, kk.grad, vv.grad
+    finally:
+        lib.ta_blocked_set_tcgen05_backward(old)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,N,H,D,S,f,Lb,causal", [
+    (1, 2048, 2, 64, 8, 4, 128, True),     # keys as the dV / dK MMA rows (config-3 shape)
+    (2, 2048, 1, 64, 8, 2, 128, False),
+    (1, 1024, 2, 128, 8, 2, 64, False),    # head_dim as the rows (config-2 shape)
+    (1, 512, 3, 128, 4, 2, 64, True),      # partial tiles, blocks no pair reaches
+])
+def test_tcgen05_backward_matches_mma_sync(dtype, B, N, H, D, S, f, Lb, causal):
+    """The tcgen05 leaf-block backward (TMEM accumulators, P from the forward's log-sum-exp)
+    against the mma.sync one on the same sampled paths, at the north-star bar."""
+    g = torch.Generator(device="cuda").manual_seed(N + 3 * D)
+    sd = 0.5 if dtype == torch.float16 else 1.0
+    q, k, v, go = (torch.randn(B, N, H, D, device="cuda", generator=g).mul(sd).to(dtype)
+                   for _ in range(4))
+    blk_t, *g_tc = _fwd_bwd(q, k, v, go, causal, S, f, Lb, True)
+    blk_m, *g_ms = _fwd_bwd(q, k, v, go, causal, S, f, Lb, False)
+    assert torch.equal(blk_t, blk_m)
+    name = "bf16" if dtype == torch.bfloat16 else "f16"
+    for n_, a, b in zip(("dq", "dk", "dv"), g_tc, g_ms):
+        assert torch.isfinite(a).all(), n_
+        assert_within(a.float().cpu().numpy(), b.float().cpu().numpy(), name, n_)
+
+
+def test_tcgen05_backward_expired_wait_is_reported():
+    """A 1 ns bound around the backward alone: the tcgen05 backward's first wait expires, the
+    CTA drains its MMAs and frees its TMEM, and the next blocked call raises."""
+    lib = L.load()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v, go = (torch.randn(1, 2048, 2, 64, device="cuda", generator=g).to(torch.bfloat16)
+                   for _ in range(4))
+    lib.ta_blocked_status(1)
+    old_b = lib.ta_blocked_set_tcgen05_backward(1)
+    try:
+        qq = q.clone().requires_grad_(True)
+        out = TB.blocked_tree_attention(qq, k, v, True, None, num_samples=8, fanout=4, leaf_block=128)
+        torch.cuda.synchronize()
+        old = lib.ta_blocked_set_tc_wait_ns(1)
+        try:
+            out.backward(go)
+            torch.cuda.synchronize()
+        finally:
+            lib.ta_blocked_set_tc_wait_ns(old)
+        assert lib.ta_blocked_status(0) == 1
+        with pytest.raises(L.TreeAttnError, match="expired"):
+            TB.blocked_tree_attention(q, k, v, True, None, num_samples=8, fanout=4, leaf_block=128)
+        assert lib.ta_blocked_status(0) == 0
+    finally:
+        lib.ta_blocked_set_tcgen05_backward(old_b)

@@ -98,6 +98,7 @@ SIGNATURES = {
     "ta_blocked_gumbel_fill": (ctypes.c_int, [ctypes.POINTER(Shape), ctypes.POINTER(Blocked),
                                               ctypes.POINTER(Rng), _P, _P]),
     "ta_blocked_set_tcgen05": (_I32, [_I32]),
+    "ta_blocked_set_tcgen05_backward": (_I32, [_I32]),
     "ta_blocked_status": (_I32, [_I32]),
     "ta_blocked_set_tc_wait_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "ta_backward_set_node_range": (_I32, [_I32]),

@@ -135,6 +135,7 @@ namespace {
 // faster (config 2: 1.32 vs 1.54 ms per forward, config 3: 7.0 vs 9.6 ms), the tcgen05 kernel
 // serialising gather, MMA and epilogue per 128-pair tile at two CTAs per SM.
 int g_use_tcgen05 = 0;
+int g_use_tcgen05_bwd = 1;
 std::atomic<uint64_t> g_tc_wait_ns{kTcWaitNs};
 std::mutex g_tc_status_mu;
 int32_t* g_tc_status = nullptr;  // mapped, portable pinned host word (process-wide, sticky)
@@ -164,7 +165,7 @@ int32_t take_tc_status() {
 // from the next blocked call (the flag is cleared when reported).
 int check_tc_status() {
   if (take_tc_status() != 0)
-    return fail(TA_ERR_CUDA, "an earlier tcgen05 leaf-block forward gave up on an expired "
+    return fail(TA_ERR_CUDA, "an earlier tcgen05 leaf-block kernel gave up on an expired "
                              "mbarrier wait; its results are invalid");
   return TA_OK;
 }
@@ -173,6 +174,12 @@ int check_tc_status() {
 extern "C" int32_t ta_blocked_set_tcgen05(int32_t enable) {
   const int32_t old = g_use_tcgen05;
   g_use_tcgen05 = enable ? 1 : 0;
+  return old;
+}
+
+extern "C" int32_t ta_blocked_set_tcgen05_backward(int32_t enable) {
+  const int32_t old = g_use_tcgen05_bwd;
+  g_use_tcgen05_bwd = enable ? 1 : 0;
   return old;
 }
 
@@ -287,6 +294,18 @@ extern "C" int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg,
     p.path_out = const_cast<float*>(path_out);
     p.delta = (float*)(base + w.delta); p.dq_tree = (float*)(base + w.dq_tree);
     p.dq_path = (float*)(base + w.dq_path);
+    p.ranges = (uint32_t*)(base + w.ranges);
+    p.use_tcgen05_bwd = g_use_tcgen05_bwd && blk_tc_bwd_shape(p.Lb, p.D);
+    if (p.use_tcgen05_bwd) {
+      int32_t* word = tc_status_word();
+      void* dword = nullptr;
+      if (word == nullptr || cudaHostGetDevicePointer(&dword, word, 0) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TA_ERR_CUDA, "cannot map the tcgen05 status word");
+      }
+      p.status = (volatile int32_t*)dword;
+      p.wait_ns = g_tc_wait_ns.load();
+    }
   } else {
     p.ds_rows = (float*)(base + w.ds); p.wp_rows = (float*)(base + w.wp);
   }

@@ -3,6 +3,7 @@
 // ta_blocked_<dtype>_f<fanout>.cu, which split the compile across processes.
 #pragma once
 
+#include <atomic>
 #include <type_traits>
 
 // Generalised tree attention: fanout f, leaf blocks of Lb keys (sm_100a).
@@ -34,6 +35,7 @@
 #include "ta_backward_kernels.cuh"
 #include "ta_blocked_mma.cuh"
 #include "ta_blocked_tc.cuh"
+#include "ta_blocked_tc_bwd.cuh"
 #include "ta_rng.cuh"
 
 namespace ta {
@@ -85,6 +87,8 @@ struct BlkParams {
   volatile int32_t* status;  // tensor-core wait status word (mapped host memory)
   uint64_t wait_ns;          // bound of one tensor-core mbarrier wait
   int32_t use_tcgen05;   // leaf-block forward on tcgen05 (else mma.sync)
+  int32_t use_tcgen05_bwd;  // leaf-block backward on tcgen05 where its shape allows
+  uint32_t* ranges;          // [B*H][nb + 1] first sorted pair of each leaf block
 };
 
 template <typename T, int EPL>
@@ -1268,6 +1272,9 @@ static BlkMmaParams blk_mma_params(const BlkParams& p) {
   m.qs = p.qs; m.qb = p.qb; m.qh = p.qh; m.ks = p.ks; m.kb = p.kb; m.kh = p.kh;
   m.vs = p.vs; m.vb = p.vb; m.vh = p.vh; m.gs = p.gs; m.gb = p.gb; m.gh = p.gh;
   m.skeys = p.skeys; m.svals = p.svals; m.weights = p.weights; m.path_out = p.path_out;
+  m.ranges = p.ranges;
+  // the per-pair log-sum-exp follows the [B*H][P][D] rows in the same buffer
+  m.lse = p.path_out != nullptr ? p.path_out + (int64_t)p.B * p.H * p.P * p.D : nullptr;
   m.delta = p.delta; m.dq_path = p.dq_path; m.dk_attn = p.dk_attn;
   m.dz_rows = p.dz_rows; m.dc_part = p.dc_part; m.DF = p.Dp * p.f;
   m.dv = p.dv; m.dvs = p.dvs; m.dvb = p.dvb; m.dvh = p.dvh;
@@ -1293,6 +1300,32 @@ static void launch_attn_bwd_mma(const BlkMmaParams& m, unsigned grid, cudaStream
     cudaFuncSetAttribute(blk_attn_bwd_mma_kernel<T, LB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     blk_attn_bwd_mma_kernel<T, LB, D><<<grid, 256, smem, st>>>(m);
   }
+}
+
+template <typename T, int LB, int D>
+static bool launch_attn_bwd_tc(const BlkMmaParams& m, unsigned grid, cudaStream_t st) {
+  if constexpr (BlkTcBwdGeom<LB, D>::OK) {
+    using G = BlkTcBwdGeom<LB, D>;
+    const size_t smem = G::smem(m.DF <= 16 ? 16 : 32);
+    if (smem > (size_t)227 * 1024) return false;
+    static std::atomic<uint32_t> set_on{0};  // devices whose function attribute is set
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint32_t bit = 1u << (dev & 31);
+    if (!(set_on.load() & bit)) {
+      cudaFuncSetAttribute(blk_attn_bwd_tc_kernel<T, LB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           227 * 1024);
+      set_on.fetch_or(bit);
+    }
+    blk_attn_bwd_tc_kernel<T, LB, D><<<grid, 256, smem, st>>>(m);
+    return true;
+  }
+  return false;
+}
+
+// the tcgen05 backward covers (leaf block, head_dim) = (128, 64) and (64, 128)
+inline bool blk_tc_bwd_shape(int Lb, int D) {
+  return (Lb == 128 && D == 64) || (Lb == 64 && D == 128);
 }
 
 template <typename T, int LB, int D>
@@ -1347,6 +1380,16 @@ template <typename T>
 void attn_bwd_mma(const BlkParams& p, cudaStream_t st) {
   const BlkMmaParams m = blk_mma_params(p);
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.nb);
+  if (p.use_tcgen05_bwd && p.status != nullptr && p.ranges != nullptr && blk_tc_bwd_shape(p.Lb, p.D) &&
+      p.Dp * p.f <= kDFMax) {
+    TA_PROFILE("blocked_attn_bwd_tc", st);
+    const int64_t HB = (int64_t)p.B * p.H;
+    const int64_t nr = HB * (p.P + 1);
+    blk_block_ranges_kernel<<<(unsigned)((nr + 255) / 256), 256, 0, st>>>(p.skeys, p.P, p.nb, HB, p.ranges);
+    const bool ran = p.D == 64 ? launch_attn_bwd_tc<T, 128, 64>(m, grid, st)
+                               : launch_attn_bwd_tc<T, 64, 128>(m, grid, st);
+    if (ran) return;
+  }
   TA_PROFILE("blocked_attn_bwd_mma", st);
   if (p.D == 64) {
     switch (p.Lb) {
@@ -1470,7 +1513,7 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
 }
 
 struct BlkWs {
-  size_t keys[2], vals[2], hist, ds, wp, dz, dk_attn, dc_part, dc, delta, dq_tree, dq_path, total;
+  size_t keys[2], vals[2], hist, ds, wp, dz, dk_attn, dc_part, dc, delta, dq_tree, dq_path, ranges, total;
 };
 
 // Backward workspace; `mma` = tensor-core leaf-block path (no per-path dS / wP rows, but
@@ -1491,6 +1534,7 @@ static BlkWs blk_ws(const BlkParams& p, bool mma) {
     w.delta = take(HB * p.P * 4);
     w.dq_tree = take(HB * p.L * p.D * 4);
     w.dq_path = take(HB * p.P * p.D * 4);
+    w.ranges = take(HB * (p.nb + 1) * 4);
   }
   w.dz = take(HB * p.P * (p.Dp * p.f > 0 ? p.Dp * p.f : 1) * 4);
   w.dk_attn = take(HB * p.N * p.D * 4);

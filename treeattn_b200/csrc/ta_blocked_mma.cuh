@@ -97,8 +97,10 @@ struct BlkMmaParams {
   const char* q; const char* k; const char* v; const char* dout;
   int64_t qs, qb, qh, ks, kb, kh, vs, vb, vh, gs, gb, gh;
   const uint32_t* skeys; const uint32_t* svals;  // [B*H][P] sorted by leaf block
+  const uint32_t* ranges;  // [B*H][nb + 1] first sorted pair of each leaf block (or null)
   const float* weights;    // [L][B][H][S] path weights
   float* path_out;         // [B*H][P][D]: w_s o_s (forward out, backward in)
+  float* lse;              // [B*H][P]: base-2 log-sum-exp of each pair's scaled scores
   const float* delta;      // [B*H][P] dO_q . (w_s o_s) (backward)
   float* dq_path;          // [B*H][P][D] (backward)
   float* dk_attn;          // [B*H][N][D] (backward)
@@ -264,6 +266,7 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum0;
       float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
+      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx0 + log2f(sum0);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
         *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][0] * w, oc[t][1] * w);
@@ -273,6 +276,7 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum1;
       float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
+      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx1 + log2f(sum1);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
         *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][2] * w, oc[t][3] * w);

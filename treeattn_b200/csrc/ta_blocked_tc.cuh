@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
     // row max, then P = exp(s - max) (16-bit, K-major) and the row sum; the S row is read from
     // TMEM once when it fits in registers (Lb <= 64), else twice
     const int64_t key0 = (int64_t)j * LB;
-    float sum = 0.0f;
+    float sum = 0.0f, row_max = -INFINITY;
     if constexpr (LB <= 64) {
       float sv[LB];
 #pragma unroll
@@ -246,6 +246,7 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
         sv[i] = key0 + i > bnd ? -INFINITY : sv[i] * p.scale;
         mx = fmaxf(mx, sv[i]);
       }
+      row_max = mx;
 #pragma unroll
       for (int c0 = 0; c0 < LB; c0 += 8) {
         uint32_t pk[4];
@@ -270,6 +271,7 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
           mx = fmaxf(mx, sc);
         }
       }
+      row_max = mx;
 #pragma unroll
       for (int c0 = 0; c0 < LB; c0 += 16) {
         float v[16];
@@ -307,6 +309,7 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
       const int64_t l = path / p.S, s = path - l * p.S;
       w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum;
       dst = reinterpret_cast<float4*>(p.path_out + ((int64_t)bh * p.P + path) * D);
+      if (p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = (row_max + logf(sum)) * kLog2e;
     }
     __syncwarp();
 #pragma unroll

@@ -1,0 +1,433 @@
+// Leaf-block attention backward of the generalised tree on the 5th-generation tensor cores
+// (tcgen05 + TMEM), sm_100a, 16-bit inputs.
+//
+// One CTA of 256 threads per (batch*head, leaf block) walks the block's leaf-sorted
+// (query, path) pairs in tiles of 128 (one pair per TMEM lane). Per tile:
+//   1. S = Q_g K^T and dP = dO_g V^T: 2 * D/16 tcgen05.mma (M = 128 pairs, N = Lb) issued by
+//      one thread into TMEM, committed to an mbarrier;
+//   2. warp w reads TMEM lanes [32 (w % 4), +32) (its pairs) and half (w / 4) of the columns:
+//      P = exp2(scale log2(e) s - lse2) with the pair's base-2 log-sum-exp saved by the forward
+//      (no row reduction), keys beyond the causal boundary masked, then w_s P and
+//      dS = P (w_s dP - delta) as 16-bit K-major tiles in shared memory;
+//   3. one thread issues dq = dS K (N = D; into the S columns, which are dead by then),
+//      dV += (w P)^T dO and dK += dS^T Q; dV / dK accumulate in TMEM over the block's tiles,
+//      with the block's keys as the MMA rows when Lb = 128, else transposed (head_dim = 128
+//      rows, keys as columns);
+//   4. while those run, the warps issue every global read of the next tile (its query and dO
+//      rows, its pairs' w_s, delta and log-sum-exp, its raw dz rows, and the paths of the tile
+//      after it) as cp.async into the other buffers, so no thread waits on a global load, and
+//      add this tile's summary gradients dc += dz^T Q on mma.sync (dz split into 16-bit high
+//      and low parts; M = levels * fanout is too small for tcgen05);
+//   5. each warp reads its dq rows back and stores them to the float32 per-path buffer.
+// A block's pair range comes from a table built once per call (blk_block_ranges_kernel).
+// The same physical layout (8-row x 16-byte core matrices, chunk (row, c / 8) at
+// (row / 8) * cols * 16 + (c / 8) * 128 + (row % 8) * 16) serves as a K-major operand over
+// its columns (LBO 128, SBO cols * 16) and as an MN-major operand over its rows (LBO
+// cols * 16, SBO 128), so K, Q, dO, w P and dS are each staged once. Every mbarrier wait is
+// bounded as in the forward: the CTA agrees on a failure, waits once more for its issued MMAs,
+// records the status word and frees its TMEM.
+#pragma once
+
+#include "ta_blocked_tc.cuh"
+
+namespace ta {
+
+template <int LB, int D>
+struct BlkTcBwdGeom {
+  static constexpr bool KEY_ROWS = LB == 128;           // dV / dK rows = keys (else head_dim)
+  static constexpr int NV = KEY_ROWS ? D : LB;          // TMEM columns of dV, and of dK
+  static constexpr int COLS_USED = 2 * LB + 2 * NV;     // S | dP (then dq), dV, dK
+  static constexpr int COLS = COLS_USED <= 256 ? 256 : 512;
+  static constexpr size_t KT = (size_t)LB * D * 2;       // K_blk or V_blk
+  static constexpr size_t QT = (size_t)kTcRows * D * 2;  // one Q or dO tile
+  static constexpr size_t PT = (size_t)kTcRows * LB * 2; // the w P or dS tile
+  static constexpr size_t ZT = (size_t)kTcRows * kZLd * 2;
+  static constexpr size_t SCAL = (size_t)3 * kTcRows * 4;  // w_s, delta, lse2 of one tile
+  static constexpr size_t oK = 0, oV = KT, oQ = 2 * KT, oG = oQ + 2 * QT, oWP = oG + 2 * QT,
+                          oDS = oWP + PT, oZH = oDS + PT, oZL = oZH + ZT, oSC = oZL + ZT,
+                          oPATH = oSC + 2 * SCAL, oBAR = oPATH + 3 * kTcRows * 4,
+                          oZRAW = oBAR + 64;
+  // shared memory with a raw dz staging tile of zw float32 columns
+  static constexpr size_t smem(int zw) { return oZRAW + (size_t)kTcRows * zw * 4; }
+  static constexpr bool OK = (LB == 128 || D == 128) && LB >= 32 && LB % 16 == 0 && D % 16 == 0 &&
+                             D <= 2 * LB && COLS_USED <= 512;
+};
+
+// Two 16-column TMEM reads of this thread's lane and their completion wait in one asm
+// statement, so no use of the registers can be scheduled before the wait.
+__device__ __forceinline__ void tc_ld16x2(uint32_t a0, uint32_t a1, float* x, float* y) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    x[i] = __uint_as_float(r[i]);
+    y[i] = __uint_as_float(r[16 + i]);
+  }
+}
+
+// B fragments of two n8 tiles (n0, n0 + 8), k16, from a [k][n] tile stored in the core-matrix
+// layout above (n contiguous within a chunk): the same rows and columns as frag_b_kn.
+__device__ __forceinline__ void frag_b_kn_core(uint32_t* r, const unsigned char* base, int cols, int n0,
+                                               int k0, int lane) {
+  ldsm4t(r, base + kmaj_off(k0 + ((lane >> 3) & 1) * 8 + (lane & 7), n0 + (lane >> 4) * 8, cols));
+}
+
+// First sorted (query, path) pair of every leaf block of every head: out[bh][j] for j in
+// [0, nb], out[bh][nb] = P (one thread per sorted position; each boundary writes the blocks it
+// opens, so empty blocks get their successor's start).
+static __global__ void __launch_bounds__(256) blk_block_ranges_kernel(const uint32_t* skeys, int64_t P, int nb,
+                                                               int64_t HB, uint32_t* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= HB * (P + 1)) return;
+  const int64_t bh = i / (P + 1), x = i - bh * (P + 1);
+  const uint32_t* keys = skeys + bh * P;
+  const int64_t prev = x > 0 ? (int64_t)keys[x - 1] : -1;
+  const int64_t cur = x < P ? (int64_t)keys[x] : (int64_t)nb;
+  for (int64_t kk = prev + 1; kk <= cur && kk <= nb; ++kk) out[bh * (nb + 1) + kk] = (uint32_t)x;
+}
+
+template <typename T, int LB, int D>
+__global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaParams p) {
+  using G = BlkTcBwdGeom<LB, D>;
+  static_assert(G::OK, "unsupported leaf block / head_dim for the tcgen05 backward");
+  extern __shared__ __align__(128) unsigned char sm[];
+  unsigned char* sK = sm + G::oK;
+  unsigned char* sV = sm + G::oV;
+  unsigned char* sWP = sm + G::oWP;
+  unsigned char* sDS = sm + G::oDS;
+  uint16_t* s_zh = reinterpret_cast<uint16_t*>(sm + G::oZH);
+  uint16_t* s_zl = reinterpret_cast<uint16_t*>(sm + G::oZL);
+  uint32_t* s_path = reinterpret_cast<uint32_t*>(sm + G::oPATH);  // [3][128] ring of tiles
+  float* s_zraw = reinterpret_cast<float*>(sm + G::oZRAW);        // [128][zw]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + G::oBAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int quad = warp & 3, half = warp >> 2;
+  const int bh = blockIdx.x / p.nb;
+  const int j = blockIdx.x - bh * p.nb;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  const uint32_t* vals = p.svals + (int64_t)bh * p.P;
+  const uint32_t mS = smem_u32(bars), mD = smem_u32(bars + 1);
+  const int64_t key0 = (int64_t)j * LB;
+  const int64_t beg = p.ranges[(int64_t)bh * (p.nb + 1) + j];
+  const int64_t end = p.ranges[(int64_t)bh * (p.nb + 1) + j + 1];
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mS) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mD) : "memory");
+  }
+  __syncwarp();  // tcgen05.alloc is .sync.aligned: warp 0 must be converged
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
+                 "r"(G::COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  const int DF = p.DF;
+  const int zsh = DF <= 16 ? 4 : 5;  // log2 of the dz tile width
+  const int zmt = (DF + 15) >> 4;
+  constexpr int NPAIR = D / 16;
+  // the paths of tile x (at t0) into ring slot x % 3
+  auto fetch_paths = [&](int64_t t0, int slot) {
+    if (tid < kTcRows) {
+      uint32_t* dst = s_path + slot * kTcRows + tid;
+      if (t0 + tid < end) cp_async4(dst, vals + t0 + tid);
+      else *dst = 0u;
+    }
+  };
+  // K_blk and V_blk, both in the core-matrix layout over (key, d); the first tile's paths
+  constexpr int CPR = D * 2 / 16;
+  for (int i = tid; i < LB * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i - r * CPR;
+    const int64_t key = key0 + r;
+    cp_async16(sK + kmaj_off(r, c * 8, D), p.k + (key * p.ks + (int64_t)b * p.kb + (int64_t)h * p.kh) * 2 + c * 16);
+    cp_async16(sV + kmaj_off(r, c * 8, D), p.v + (key * p.vs + (int64_t)b * p.vb + (int64_t)h * p.vh) * 2 + c * 16);
+  }
+  if (beg < end) fetch_paths(beg, 0);
+  cp_async_commit();
+
+  // every global read of tile x (at t0, buffer `buf`), issued one tile ahead with cp.async:
+  // threads 0-127 the query rows and the pair scalars, threads 128-255 the dO rows; all
+  // threads the raw dz rows; and the paths of tile x + 1. Rows past the tile are zero.
+  auto gather = [&](int64_t t0, int buf, int slot) {
+    const int n = (int)min((int64_t)kTcRows, end - t0);
+    const int r = tid & (kTcRows - 1);
+    const bool dout = tid >= kTcRows;
+    unsigned char* dst = sm + (dout ? G::oG : G::oQ) + buf * G::QT;
+    const uint32_t path = s_path[slot * kTcRows + r];
+    const int64_t l = (int64_t)(path / (uint32_t)p.S);
+    const char* src = dout ? p.dout + (l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * 2
+                           : p.q + (l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2;
+#pragma unroll
+    for (int c = 0; c < CPR; ++c) {
+      unsigned char* d_ = dst + kmaj_off(r, c * 8, D);
+      if (r < n) cp_async16(d_, src + c * 16);
+      else *reinterpret_cast<uint4*>(d_) = make_uint4(0, 0, 0, 0);
+    }
+    if (!dout) {
+      float* sc = reinterpret_cast<float*>(sm + G::oSC + buf * G::SCAL);
+      if (r < n) {
+        const int64_t s = (int64_t)path - l * p.S;
+        cp_async4(sc + r, p.weights + ((l * p.B + b) * p.H + h) * p.S + s);
+        cp_async4(sc + kTcRows + r, p.delta + (int64_t)bh * p.P + path);
+        cp_async4(sc + 2 * kTcRows + r, p.lse + (int64_t)bh * p.P + path);
+      } else {
+        sc[r] = sc[kTcRows + r] = sc[2 * kTcRows + r] = 0.0f;
+      }
+    }
+    for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) {
+      const int rr = i >> zsh, c = i & ((1 << zsh) - 1);
+      if (rr < n && c < DF)
+        cp_async4(s_zraw + i, p.dz_rows + ((int64_t)bh * p.P + s_path[slot * kTcRows + rr]) * DF + c);
+      else
+        s_zraw[i] = 0.0f;
+    }
+    if (t0 + kTcRows < end) fetch_paths(t0 + kTcRows, slot == 2 ? 0 : slot + 1);
+    cp_async_commit();
+  };
+
+  float acc_dc[2][2][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc_dc[i][t][e] = 0.0f;
+
+  cp_async_wait_0();  // K_blk, V_blk, the first tile's paths
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const uint32_t tS = tmem, tP = tmem + LB, tV = tmem + 2 * LB, tK = tmem + 2 * LB + G::NV;
+  const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+  if (beg < end) gather(beg, 0, 0);
+  constexpr uint32_t idS = tc_idesc<T>(kTcRows, LB, 0, 0);
+  constexpr uint32_t idDQ = tc_idesc<T>(kTcRows, D, 0, 1);
+  constexpr uint32_t idKV = G::KEY_ROWS ? tc_idesc<T>(LB, D, 1, 1) : tc_idesc<T>(D, LB, 1, 1);
+  const float sl2 = p.scale * kLog2e;
+  const int r = quad * 32 + lane;  // this thread's pair row (TMEM lane)
+  uint32_t phS = 0, phD = 0;
+  int failed = 0;  // 1: the S / dP wait expired, 2: the dq / dV / dK wait expired
+  int buf = 0, slot = 0;
+  for (int64_t t0 = beg; t0 < end; t0 += kTcRows, buf ^= 1, slot = slot == 2 ? 0 : slot + 1) {
+    const int n = (int)min((int64_t)kTcRows, end - t0);
+    const unsigned char* sQ = sm + G::oQ + buf * G::QT;
+    const unsigned char* sG = sm + G::oG + buf * G::QT;
+    cp_async_wait_0();  // everything of this tile, and the next tile's paths
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        tc_mma(tS, tc_desc(smem_u32(sQ) + kk * 256, 128, D * 16), tc_desc(smem_u32(sK) + kk * 256, 128, D * 16),
+               idS, kk > 0 ? 1u : 0u);
+        tc_mma(tP, tc_desc(smem_u32(sG) + kk * 256, 128, D * 16), tc_desc(smem_u32(sV) + kk * 256, 128, D * 16),
+               idS, kk > 0 ? 1u : 0u);
+      }
+      tc_commit(mS);
+    }
+    // while S and dP run: this tile's dz rows as 16-bit high / low parts
+    for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) {
+      const int rr = i >> zsh, c = i & ((1 << zsh) - 1);
+      const float z = s_zraw[i];
+      const uint16_t hi = Mma<T>::half_bits(z);
+      s_zh[rr * kZLd + c] = hi;
+      s_zl[rr * kZLd + c] = Mma<T>::half_bits(z - raw_to_float<T>(hi));
+    }
+    if (__syncthreads_or(!tc_wait(mS, phS, p.wait_ns))) { failed = 1; break; }
+    phS ^= 1u;
+    tc_fence_after();
+    {
+      // w P and dS of this thread's pair over its half of the keys
+      const float* sc = reinterpret_cast<const float*>(sm + G::oSC + buf * G::SCAL);
+      const uint32_t path = s_path[slot * kTcRows + r];
+      int vis = 0;
+      if (r < n) {
+        const int64_t bnd = p.causal ? (p.row0 + (int64_t)(path / (uint32_t)p.S)) + p.N - p.row_total
+                                     : INT64_MAX;
+        vis = visible_keys<LB>(bnd, key0);
+      }
+      const float w = sc[r], dl = sc[kTcRows + r], lse2 = sc[2 * kTcRows + r];
+#pragma unroll
+      for (int c0 = half * (LB / 2); c0 < (half + 1) * (LB / 2); c0 += 16) {
+        float sv[16], dv[16];
+        tc_ld16x2(tS + lane_addr + c0, tP + lane_addr + c0, sv, dv);
+        uint32_t pw[8], pd[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = c0 + i < vis ? exp2f(fmaf(sv[i], sl2, -lse2)) : 0.0f;
+          const float p1 = c0 + i + 1 < vis ? exp2f(fmaf(sv[i + 1], sl2, -lse2)) : 0.0f;
+          pw[i >> 1] = Mma<T>::pack(w * p0, w * p1);
+          pd[i >> 1] = Mma<T>::pack(p0 * (w * dv[i] - dl), p1 * (w * dv[i + 1] - dl));
+        }
+        *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0, LB)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0 + 8, LB)) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+        *reinterpret_cast<uint4*>(sDS + kmaj_off(r, c0, LB)) = make_uint4(pd[0], pd[1], pd[2], pd[3]);
+        *reinterpret_cast<uint4*>(sDS + kmaj_off(r, c0 + 8, LB)) = make_uint4(pd[4], pd[5], pd[6], pd[7]);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      // dq = dS K (K_blk as the MN-major B operand over its key rows), into the S columns
+#pragma unroll
+      for (int kk = 0; kk < LB / 16; ++kk)
+        tc_mma(tS, tc_desc(smem_u32(sDS) + kk * 256, 128, LB * 16),
+               tc_desc(smem_u32(sK) + kk * 32 * D, D * 16, 128), idDQ, kk > 0 ? 1u : 0u);
+      // dV += (w P)^T dO, dK += dS^T Q over the tile's pairs (the MMA's K), both operands
+      // MN-major over their pair rows
+      const int kend = (n + 15) >> 4;
+      for (int kk = 0; kk < kend; ++kk) {
+        const uint32_t acc = (t0 > beg || kk > 0) ? 1u : 0u;
+        const uint64_t dwp = tc_desc(smem_u32(sWP) + kk * 32 * LB, LB * 16, 128);
+        const uint64_t dds = tc_desc(smem_u32(sDS) + kk * 32 * LB, LB * 16, 128);
+        const uint64_t dgo = tc_desc(smem_u32(sG) + kk * 32 * D, D * 16, 128);
+        const uint64_t dq_ = tc_desc(smem_u32(sQ) + kk * 32 * D, D * 16, 128);
+        if constexpr (G::KEY_ROWS) {
+          tc_mma(tV, dwp, dgo, idKV, acc);
+          tc_mma(tK, dds, dq_, idKV, acc);
+        } else {
+          tc_mma(tV, dgo, dwp, idKV, acc);
+          tc_mma(tK, dq_, dds, idKV, acc);
+        }
+      }
+      tc_commit(mD);
+    }
+    // while the tensor cores run: the next tile's reads, then this tile's summary gradients
+    if (t0 + kTcRows < end) gather(t0 + kTcRows, buf ^ 1, slot == 2 ? 0 : slot + 1);
+    {
+      const int kend = (n + 15) & ~15;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int item = warp + 8 * i;
+        if (item < zmt * NPAIR) {
+          const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
+          for (int kc = 0; kc < kend; kc += 16) {
+            uint32_t ah[4], al[4], bb[4];
+            frag_a_t(ah, s_zh, kZLd, zm, kc, lane);
+            frag_a_t(al, s_zl, kZLd, zm, kc, lane);
+            frag_b_kn_core(bb, sQ, D, zn, kc, lane);
+            Mma<T>::run(acc_dc[i][0], ah, bb);
+            Mma<T>::run(acc_dc[i][0], al, bb);
+            Mma<T>::run(acc_dc[i][1], ah, bb + 2);
+            Mma<T>::run(acc_dc[i][1], al, bb + 2);
+          }
+        }
+      }
+    }
+    if (__syncthreads_or(!tc_wait(mD, phD, p.wait_ns))) { failed = 2; break; }
+    phD ^= 1u;
+    tc_fence_after();
+    {
+      // dq rows of this tile (this thread's pair, its half of the columns)
+      const uint32_t path = s_path[slot * kTcRows + r];
+      float* dst = r < n ? p.dq_path + ((int64_t)bh * p.P + path) * D : nullptr;
+#pragma unroll
+      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 32) {
+        float x[16], y[16];
+        tc_ld16x2(tS + lane_addr + c0, tS + lane_addr + c0 + 16, x, y);
+        if (dst != nullptr) {
+          float4* d4 = reinterpret_cast<float4*>(dst + c0);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            d4[i >> 2] = make_float4(x[i] * p.scale, x[i + 1] * p.scale, x[i + 2] * p.scale, x[i + 3] * p.scale);
+            d4[(16 + i) >> 2] = make_float4(y[i] * p.scale, y[i + 1] * p.scale, y[i + 2] * p.scale, y[i + 3] * p.scale);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  cp_async_wait_0();
+  if (failed) {
+    // let the MMAs issued before the expired wait finish before their TMEM is freed
+    if (failed == 1) tc_wait(mS, phS, kTcWaitNs);
+    else tc_wait(mD, phD, kTcWaitNs);
+    if (tid == 0) {
+      *p.status = 1;
+      __threadfence_system();
+    }
+  } else {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // summary partials of this block
+    {
+      const int g = lane >> 2, tq = lane & 3;
+      float* dcp = p.dc_part + ((int64_t)bh * p.nb + j) * DF * D;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int item = warp + 8 * i;
+        if (item < zmt * NPAIR) {
+          const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int c = zn + t * 8 + tq * 2;
+            if (zm + g < DF)
+              *reinterpret_cast<float2*>(dcp + (zm + g) * D + c) = make_float2(acc_dc[i][t][0], acc_dc[i][t][1]);
+            if (zm + g + 8 < DF)
+              *reinterpret_cast<float2*>(dcp + (zm + g + 8) * D + c) = make_float2(acc_dc[i][t][2], acc_dc[i][t][3]);
+          }
+        }
+      }
+    }
+    // dV (input dtype) and the attention part of dK (float32); zeros for a block no pair reached
+    T* dvb = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dvb + (int64_t)h * p.dvh;
+    float* dkb = p.dk_attn + (int64_t)bh * p.N * D;
+    const bool any = beg < end;
+    if constexpr (G::KEY_ROWS) {
+      // lane = key row, columns = head_dim (this warp's half)
+      const int64_t key = key0 + r;
+#pragma unroll
+      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 16) {
+        float x[16], y[16];
+        tc_ld16x2(tV + lane_addr + c0, tK + lane_addr + c0, x, y);
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) pk[i >> 1] = any ? Mma<T>::pack(x[i], x[i + 1]) : 0u;
+        uint4* vd = reinterpret_cast<uint4*>(dvb + key * p.dvs + c0);
+        vd[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        vd[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        float4* kd = reinterpret_cast<float4*>(dkb + key * D + c0);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          kd[i >> 2] = any ? make_float4(y[i] * p.scale, y[i + 1] * p.scale, y[i + 2] * p.scale, y[i + 3] * p.scale)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    } else {
+      // lane = head_dim column d, TMEM columns = keys (this warp's half)
+      const int d = r;
+#pragma unroll
+      for (int c0 = half * (LB / 2); c0 < (half + 1) * (LB / 2); c0 += 16) {
+        float x[16], y[16];
+        tc_ld16x2(tV + lane_addr + c0, tK + lane_addr + c0, x, y);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int64_t key = key0 + c0 + i;
+          dvb[key * p.dvs + d] = static_cast<T>(any ? x[i] : 0.0f);
+          dkb[key * D + d] = any ? y[i] * p.scale : 0.0f;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  __syncwarp();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::COLS) : "memory");
+}
+
+}  // namespace ta
