@@ -132,7 +132,7 @@ __host__ __device__ constexpr size_t blk_mma_fwd_smem() {
 // forward: 4 warps, 64 pairs per tile (16 rows per warp)
 // ---------------------------------------------------------------------------------------
 template <typename T, int LB, int D>
-__global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParams p) {
+__global__ void __launch_bounds__(128, LB * D > 8192 ? 2 : 4) blk_attn_fwd_mma_kernel(const BlkMmaParams p) {
   using G = BlkMmaGeom<LB, D>;
   extern __shared__ __align__(16) unsigned char smraw[];
   uint16_t* s_k = reinterpret_cast<uint16_t*>(smraw);
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum0;
       float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
-      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx0 + log2f(sum0);
+      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx0 + __log2f(sum0);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
         *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][0] * w, oc[t][1] * w);
@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(128) blk_attn_fwd_mma_kernel(const BlkMmaParam
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum1;
       float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
-      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx1 + log2f(sum1);
+      if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx1 + __log2f(sum1);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
         *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][2] * w, oc[t][3] * w);

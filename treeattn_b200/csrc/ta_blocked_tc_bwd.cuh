@@ -9,8 +9,8 @@
 //      P = exp2(scale log2(e) s - lse2) with the pair's base-2 log-sum-exp saved by the forward
 //      (no row reduction), keys beyond the causal boundary masked, then w_s P and
 //      dS = P (w_s dP - delta) as 16-bit K-major tiles in shared memory;
-//   3. one thread issues dq = dS K (N = D; into the S columns, which are dead by then),
-//      dV += (w P)^T dO and dK += dS^T Q; dV / dK accumulate in TMEM over the block's tiles,
+//   3. one thread issues dq = dS K (N = D, TMEM columns of its own), dV += (w P)^T dO and
+//      dK += dS^T Q; dV / dK accumulate in TMEM over the block's tiles,
 //      with the block's keys as the MMA rows when Lb = 128, else transposed (head_dim = 128
 //      rows, keys as columns);
 //   4. while those run, the warps issue every global read of the next tile (its query and dO
@@ -18,7 +18,8 @@
 //      after it) as cp.async into the other buffers, so no thread waits on a global load, and
 //      add this tile's summary gradients dc += dz^T Q on mma.sync (dz split into 16-bit high
 //      and low parts; M = levels * fanout is too small for tcgen05);
-//   5. each warp reads its dq rows back and stores them to the float32 per-path buffer.
+//   5. each warp reads its dq rows back and stores them to the float32 per-path buffer, while
+//      the next tile's S and dP MMAs run.
 // A block's pair range comes from a table built once per call (blk_block_ranges_kernel).
 // The same physical layout (8-row x 16-byte core matrices, chunk (row, c / 8) at
 // (row / 8) * cols * 16 + (c / 8) * 128 + (row % 8) * 16) serves as a K-major operand over
@@ -36,7 +37,7 @@ template <int LB, int D>
 struct BlkTcBwdGeom {
   static constexpr bool KEY_ROWS = LB == 128;           // dV / dK rows = keys (else head_dim)
   static constexpr int NV = KEY_ROWS ? D : LB;          // TMEM columns of dV, and of dK
-  static constexpr int COLS_USED = 2 * LB + 2 * NV;     // S | dP (then dq), dV, dK
+  static constexpr int COLS_USED = 2 * LB + 2 * NV + D;  // S, dP, dV, dK, dq
   static constexpr int COLS = COLS_USED <= 256 ? 256 : 512;
   static constexpr size_t KT = (size_t)LB * D * 2;       // K_blk or V_blk
   static constexpr size_t QT = (size_t)kTcRows * D * 2;  // one Q or dO tile
@@ -50,7 +51,7 @@ struct BlkTcBwdGeom {
   // shared memory with a raw dz staging tile of zw float32 columns
   static constexpr size_t smem(int zw) { return oZRAW + (size_t)kTcRows * zw * 4; }
   static constexpr bool OK = (LB == 128 || D == 128) && LB >= 32 && LB % 16 == 0 && D % 16 == 0 &&
-                             D <= 2 * LB && COLS_USED <= 512;
+                             COLS_USED <= 512;
 };
 
 // Two 16-column TMEM reads of this thread's lane and their completion wait in one asm
@@ -72,6 +73,13 @@ __device__ __forceinline__ void tc_ld16x2(uint32_t a0, uint32_t a1, float* x, fl
     x[i] = __uint_as_float(r[i]);
     y[i] = __uint_as_float(r[16 + i]);
   }
+}
+
+// 2^x with the hardware approximation (inputs are <= 0 up to rounding; -inf gives 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // B fragments of two n8 tiles (n0, n0 + 8), k16, from a [k][n] tile stored in the core-matrix
@@ -206,7 +214,8 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  const uint32_t tS = tmem, tP = tmem + LB, tV = tmem + 2 * LB, tK = tmem + 2 * LB + G::NV;
+  const uint32_t tS = tmem, tP = tmem + LB, tV = tmem + 2 * LB, tK = tmem + 2 * LB + G::NV,
+                 tQ = tmem + 2 * LB + 2 * G::NV;
   const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
   if (beg < end) gather(beg, 0, 0);
   constexpr uint32_t idS = tc_idesc<T>(kTcRows, LB, 0, 0);
@@ -215,8 +224,29 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   const float sl2 = p.scale * kLog2e;
   const int r = quad * 32 + lane;  // this thread's pair row (TMEM lane)
   uint32_t phS = 0, phD = 0;
-  int failed = 0;  // 1: the S / dP wait expired, 2: the dq / dV / dK wait expired
+  int failed = 0;  // 1: a wait in the tile loop expired (the last commit was mS), 2: the final
+                   // dq / dV / dK wait expired (the last commit was mD)
   int buf = 0, slot = 0;
+  // dq rows of the tile in ring slot `sl` with `n` pairs (this thread's pair, its half of the
+  // columns), once its MMAs completed
+  auto dq_out = [&](int sl, int n) {
+    const uint32_t path = s_path[sl * kTcRows + r];
+    float* dst = r < n ? p.dq_path + ((int64_t)bh * p.P + path) * D : nullptr;
+#pragma unroll
+    for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 32) {
+      float x[16], y[16];
+      tc_ld16x2(tQ + lane_addr + c0, tQ + lane_addr + c0 + 16, x, y);
+      if (dst != nullptr) {
+        float4* d4 = reinterpret_cast<float4*>(dst + c0);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          d4[i >> 2] = make_float4(x[i] * p.scale, x[i + 1] * p.scale, x[i + 2] * p.scale, x[i + 3] * p.scale);
+          d4[(16 + i) >> 2] = make_float4(y[i] * p.scale, y[i + 1] * p.scale, y[i + 2] * p.scale, y[i + 3] * p.scale);
+        }
+      }
+    }
+  };
+  int prev_slot = -1, prev_n = 0;  // the tile whose dq MMAs are in flight
   for (int64_t t0 = beg; t0 < end; t0 += kTcRows, buf ^= 1, slot = slot == 2 ? 0 : slot + 1) {
     const int n = (int)min((int64_t)kTcRows, end - t0);
     const unsigned char* sQ = sm + G::oQ + buf * G::QT;
@@ -236,13 +266,22 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
       }
       tc_commit(mS);
     }
-    // while S and dP run: this tile's dz rows as 16-bit high / low parts
+    // while S and dP run: this tile's dz rows as 16-bit high / low parts, and the previous
+    // tile's dq rows
     for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) {
       const int rr = i >> zsh, c = i & ((1 << zsh) - 1);
       const float z = s_zraw[i];
       const uint16_t hi = Mma<T>::half_bits(z);
       s_zh[rr * kZLd + c] = hi;
       s_zl[rr * kZLd + c] = Mma<T>::half_bits(z - raw_to_float<T>(hi));
+    }
+    if (prev_slot >= 0) {
+      // (an expired wait here leaves this tile's S / dP in flight too: failed = 1 drains them,
+      // and with them everything issued before)
+      if (__syncthreads_or(!tc_wait(mD, phD, p.wait_ns))) { failed = 1; break; }
+      phD ^= 1u;
+      tc_fence_after();
+      dq_out(prev_slot, prev_n);
     }
     if (__syncthreads_or(!tc_wait(mS, phS, p.wait_ns))) { failed = 1; break; }
     phS ^= 1u;
@@ -257,18 +296,28 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
                                      : INT64_MAX;
         vis = visible_keys<LB>(bnd, key0);
       }
-      const float w = sc[r], dl = sc[kTcRows + r], lse2 = sc[2 * kTcRows + r];
+      const float w = sc[r], dl = sc[kTcRows + r], nlse2 = -sc[2 * kTcRows + r];
 #pragma unroll
       for (int c0 = half * (LB / 2); c0 < (half + 1) * (LB / 2); c0 += 16) {
         float sv[16], dv[16];
         tc_ld16x2(tS + lane_addr + c0, tP + lane_addr + c0, sv, dv);
         uint32_t pw[8], pd[8];
+        if (c0 + 16 <= vis) {
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float p0 = c0 + i < vis ? exp2f(fmaf(sv[i], sl2, -lse2)) : 0.0f;
-          const float p1 = c0 + i + 1 < vis ? exp2f(fmaf(sv[i + 1], sl2, -lse2)) : 0.0f;
-          pw[i >> 1] = Mma<T>::pack(w * p0, w * p1);
-          pd[i >> 1] = Mma<T>::pack(p0 * (w * dv[i] - dl), p1 * (w * dv[i + 1] - dl));
+          for (int i = 0; i < 16; i += 2) {
+            const float p0 = ex2_approx(fmaf(sv[i], sl2, nlse2));
+            const float p1 = ex2_approx(fmaf(sv[i + 1], sl2, nlse2));
+            pw[i >> 1] = Mma<T>::pack(w * p0, w * p1);
+            pd[i >> 1] = Mma<T>::pack(p0 * fmaf(w, dv[i], -dl), p1 * fmaf(w, dv[i + 1], -dl));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float p0 = c0 + i < vis ? ex2_approx(fmaf(sv[i], sl2, nlse2)) : 0.0f;
+            const float p1 = c0 + i + 1 < vis ? ex2_approx(fmaf(sv[i + 1], sl2, nlse2)) : 0.0f;
+            pw[i >> 1] = Mma<T>::pack(w * p0, w * p1);
+            pd[i >> 1] = Mma<T>::pack(p0 * fmaf(w, dv[i], -dl), p1 * fmaf(w, dv[i + 1], -dl));
+          }
         }
         *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0, LB)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0 + 8, LB)) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
@@ -281,10 +330,10 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
     __syncthreads();
     tc_fence_after();
     if (tid == 0) {
-      // dq = dS K (K_blk as the MN-major B operand over its key rows), into the S columns
+      // dq = dS K (K_blk as the MN-major B operand over its key rows)
 #pragma unroll
       for (int kk = 0; kk < LB / 16; ++kk)
-        tc_mma(tS, tc_desc(smem_u32(sDS) + kk * 256, 128, LB * 16),
+        tc_mma(tQ, tc_desc(smem_u32(sDS) + kk * 256, 128, LB * 16),
                tc_desc(smem_u32(sK) + kk * 32 * D, D * 16, 128), idDQ, kk > 0 ? 1u : 0u);
       // dV += (w P)^T dO, dK += dS^T Q over the tile's pairs (the MMA's K), both operands
       // MN-major over their pair rows
@@ -305,7 +354,10 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
       }
       tc_commit(mD);
     }
-    // while the tensor cores run: the next tile's reads, then this tile's summary gradients
+    prev_slot = slot;
+    prev_n = n;
+    // while the tensor cores run: the next tile's reads (its buffers were last read by the
+    // previous tile's MMAs, complete), then this tile's summary gradients
     if (t0 + kTcRows < end) gather(t0 + kTcRows, buf ^ 1, slot == 2 ? 0 : slot + 1);
     {
       const int kend = (n + 15) & ~15;
@@ -327,28 +379,16 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
         }
       }
     }
-    if (__syncthreads_or(!tc_wait(mD, phD, p.wait_ns))) { failed = 2; break; }
-    phD ^= 1u;
-    tc_fence_after();
-    {
-      // dq rows of this tile (this thread's pair, its half of the columns)
-      const uint32_t path = s_path[slot * kTcRows + r];
-      float* dst = r < n ? p.dq_path + ((int64_t)bh * p.P + path) * D : nullptr;
-#pragma unroll
-      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 32) {
-        float x[16], y[16];
-        tc_ld16x2(tS + lane_addr + c0, tS + lane_addr + c0 + 16, x, y);
-        if (dst != nullptr) {
-          float4* d4 = reinterpret_cast<float4*>(dst + c0);
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            d4[i >> 2] = make_float4(x[i] * p.scale, x[i + 1] * p.scale, x[i + 2] * p.scale, x[i + 3] * p.scale);
-            d4[(16 + i) >> 2] = make_float4(y[i] * p.scale, y[i + 1] * p.scale, y[i + 2] * p.scale, y[i + 3] * p.scale);
-          }
-        }
-      }
-    }
     tc_fence_before();
+  }
+  if (!failed && prev_slot >= 0) {
+    if (__syncthreads_or(!tc_wait(mD, phD, p.wait_ns))) {
+      failed = 2;
+    } else {
+      phD ^= 1u;
+      tc_fence_after();
+      dq_out(prev_slot, prev_n);
+    }
   }
   cp_async_wait_0();
   if (failed) {
