@@ -1317,7 +1317,7 @@ static bool launch_attn_bwd_tc(const BlkMmaParams& m, unsigned grid, cudaStream_
                            227 * 1024);
       set_on.fetch_or(bit);
     }
-    blk_attn_bwd_tc_kernel<T, LB, D><<<grid, 256, smem, st>>>(m);
+    blk_attn_bwd_tc_kernel<T, LB, D><<<grid, kTcBwdThreads, smem, st>>>(m);
     return true;
   }
   return false;

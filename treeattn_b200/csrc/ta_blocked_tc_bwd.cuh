@@ -1,11 +1,12 @@
 // Leaf-block attention backward of the generalised tree on the 5th-generation tensor cores
 // (tcgen05 + TMEM), sm_100a, 16-bit inputs.
 //
-// One CTA of 256 threads per (batch*head, leaf block) walks the block's leaf-sorted
+// One CTA of 512 threads per (batch*head, leaf block) walks the block's leaf-sorted
 // (query, path) pairs in tiles of 128 (one pair per TMEM lane). Per tile:
 //   1. S = Q_g K^T and dP = dO_g V^T: 2 * D/16 tcgen05.mma (M = 128 pairs, N = Lb) issued by
 //      one thread into TMEM, committed to an mbarrier;
-//   2. warp w reads TMEM lanes [32 (w % 4), +32) (its pairs) and half (w / 4) of the columns:
+//   2. warp w reads TMEM lanes [32 (w % 4), +32) (its pairs) and part w / 4 of four column
+//      parts:
 //      P = exp2(scale log2(e) s - lse2) with the pair's base-2 log-sum-exp saved by the forward
 //      (no row reduction), keys beyond the causal boundary masked, then w_s P and
 //      dS = P (w_s dP - delta) as 16-bit K-major tiles in shared memory;
@@ -21,10 +22,12 @@
 //   5. each warp reads its dq rows back and stores them to the float32 per-path buffer, while
 //      the next tile's S and dP MMAs run.
 // A block's pair range comes from a table built once per call (blk_block_ranges_kernel).
-// The same physical layout (8-row x 16-byte core matrices, chunk (row, c / 8) at
-// (row / 8) * cols * 16 + (c / 8) * 128 + (row % 8) * 16) serves as a K-major operand over
-// its columns (LBO 128, SBO cols * 16) and as an MN-major operand over its rows (LBO
-// cols * 16, SBO 128), so K, Q, dO, w P and dS are each staged once. Every mbarrier wait is
+// Every operand tile is stored as 128-byte-swizzled atoms (8 rows x 64 16-bit columns, the
+// 16-byte chunks of row i XOR-permuted by i % 8; sw128_off), which the tensor cores read
+// without bank conflicts. The same physical tile serves as a K-major operand over its columns
+// (SBO 1024, a 16-column step is 32 bytes into the atom) and as an MN-major operand over its
+// rows (LBO = the atom-column stride, SBO 1024, a 16-row step is 2048 bytes), so K, Q, dO,
+// w P and dS are each staged once. Every mbarrier wait is
 // bounded as in the forward: the CTA agrees on a failure, waits once more for its issued MMAs,
 // records the status word and frees its TMEM.
 #pragma once
@@ -32,6 +35,11 @@
 #include "ta_blocked_tc.cuh"
 
 namespace ta {
+
+constexpr int kTcBwdWarps = 16;                 // 4 TMEM lane quadrants x 4 column parts
+constexpr int kTcBwdThreads = kTcBwdWarps * 32;
+constexpr int kTcBwdParts = kTcBwdWarps / 4;
+constexpr int kTcBwdDcItems = (16 + kTcBwdWarps - 1) / kTcBwdWarps;  // summary items per warp
 
 template <int LB, int D>
 struct BlkTcBwdGeom {
@@ -49,7 +57,7 @@ struct BlkTcBwdGeom {
                           oPATH = oSC + 2 * SCAL, oBAR = oPATH + 3 * kTcRows * 4,
                           oZRAW = oBAR + 64;
   // shared memory with a raw dz staging tile of zw float32 columns
-  static constexpr size_t smem(int zw) { return oZRAW + (size_t)kTcRows * zw * 4; }
+  static constexpr size_t smem(int zw) { return oZRAW + (size_t)kTcRows * zw * 4 + 1024; }
   static constexpr bool OK = (LB == 128 || D == 128) && LB >= 32 && LB % 16 == 0 && D % 16 == 0 &&
                              COLS_USED <= 512;
 };
@@ -82,11 +90,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// B fragments of two n8 tiles (n0, n0 + 8), k16, from a [k][n] tile stored in the core-matrix
-// layout above (n contiguous within a chunk): the same rows and columns as frag_b_kn.
-__device__ __forceinline__ void frag_b_kn_core(uint32_t* r, const unsigned char* base, int cols, int n0,
-                                               int k0, int lane) {
-  ldsm4t(r, base + kmaj_off(k0 + ((lane >> 3) & 1) * 8 + (lane & 7), n0 + (lane >> 4) * 8, cols));
+// Byte offset of 16-byte chunk `c` (columns 8c .. 8c + 7) of row `r` in a 16-bit tile of `rows`
+// rows stored as 128-byte-swizzled atoms: atom column c / 8 (64 columns) at (c / 8) * rows * 128,
+// 8-row group r / 8 at (r / 8) * 1024, and within an atom chunk c % 8 of row r % 8 at
+// (r % 8) * 128 + ((c % 8) ^ (r % 8)) * 16 (the tile base is 1024-byte aligned).
+__device__ __forceinline__ uint32_t sw128_off(int r, int c, int rows) {
+  return (uint32_t)((c >> 3) * (rows * 128) + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Shared-memory descriptor of a 128-byte-swizzled operand (layout type 2).
+__device__ __forceinline__ uint64_t tc_desc_sw(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return tc_desc(saddr, lbo, sbo) | (2ull << 61);
+}
+
+// B fragments of two n8 tiles (n0, n0 + 8), k16, from a [k][n] tile of kTcRows rows in the
+// swizzled layout above: the same rows and columns as frag_b_kn.
+__device__ __forceinline__ void frag_b_kn_sw(uint32_t* r, const unsigned char* base, int n0, int k0, int lane) {
+  ldsm4t(r, base + sw128_off(k0 + ((lane >> 3) & 1) * 8 + (lane & 7), (n0 >> 3) + (lane >> 4), kTcRows));
 }
 
 // First sorted (query, path) pair of every leaf block of every head: out[bh][j] for j in
@@ -104,10 +124,12 @@ static __global__ void __launch_bounds__(256) blk_block_ranges_kernel(const uint
 }
 
 template <typename T, int LB, int D>
-__global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaParams p) {
+__global__ void __launch_bounds__(kTcBwdThreads, 1) blk_attn_bwd_tc_kernel(const BlkMmaParams p) {
   using G = BlkTcBwdGeom<LB, D>;
   static_assert(G::OK, "unsupported leaf block / head_dim for the tcgen05 backward");
-  extern __shared__ __align__(128) unsigned char sm[];
+  extern __shared__ __align__(1024) unsigned char sm_raw[];
+  // the swizzled operand tiles need 1024-byte-aligned bases
+  unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
   unsigned char* sK = sm + G::oK;
   unsigned char* sV = sm + G::oV;
   unsigned char* sWP = sm + G::oWP;
@@ -119,7 +141,7 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + G::oBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int quad = warp & 3, half = warp >> 2;
+  const int quad = warp & 3, part = warp >> 2;
   const int bh = blockIdx.x / p.nb;
   const int j = blockIdx.x - bh * p.nb;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
@@ -155,11 +177,12 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   for (int i = tid; i < LB * CPR; i += blockDim.x) {
     const int r = i / CPR, c = i - r * CPR;
     const int64_t key = key0 + r;
-    cp_async16(sK + kmaj_off(r, c * 8, D), p.k + (key * p.ks + (int64_t)b * p.kb + (int64_t)h * p.kh) * 2 + c * 16);
-    cp_async16(sV + kmaj_off(r, c * 8, D), p.v + (key * p.vs + (int64_t)b * p.vb + (int64_t)h * p.vh) * 2 + c * 16);
+    cp_async16(sK + sw128_off(r, c, LB), p.k + (key * p.ks + (int64_t)b * p.kb + (int64_t)h * p.kh) * 2 + c * 16);
+    cp_async16(sV + sw128_off(r, c, LB), p.v + (key * p.vs + (int64_t)b * p.vb + (int64_t)h * p.vh) * 2 + c * 16);
   }
   if (beg < end) fetch_paths(beg, 0);
   cp_async_commit();
+  for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) s_zraw[i] = 0.0f;
 
   // every global read of tile x (at t0, buffer `buf`), issued one tile ahead with cp.async:
   // threads 0-127 the query rows and the pair scalars, threads 128-255 the dO rows; all
@@ -167,19 +190,22 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   auto gather = [&](int64_t t0, int buf, int slot) {
     const int n = (int)min((int64_t)kTcRows, end - t0);
     const int r = tid & (kTcRows - 1);
-    const bool dout = tid >= kTcRows;
+    const int role = tid >> 7;                     // which tensor and which of its chunks
+    const bool dout = role >= kTcBwdParts / 2;
+    constexpr int CPP = CPR / (kTcBwdParts / 2);   // 16-byte chunks of a row per thread
+    const int cfirst = (role % (kTcBwdParts / 2)) * CPP;
     unsigned char* dst = sm + (dout ? G::oG : G::oQ) + buf * G::QT;
     const uint32_t path = s_path[slot * kTcRows + r];
     const int64_t l = (int64_t)(path / (uint32_t)p.S);
     const char* src = dout ? p.dout + (l * p.gs + (int64_t)b * p.gb + (int64_t)h * p.gh) * 2
                            : p.q + (l * p.qs + (int64_t)b * p.qb + (int64_t)h * p.qh) * 2;
 #pragma unroll
-    for (int c = 0; c < CPR; ++c) {
-      unsigned char* d_ = dst + kmaj_off(r, c * 8, D);
+    for (int c = cfirst; c < cfirst + CPP; ++c) {
+      unsigned char* d_ = dst + sw128_off(r, c, kTcRows);
       if (r < n) cp_async16(d_, src + c * 16);
       else *reinterpret_cast<uint4*>(d_) = make_uint4(0, 0, 0, 0);
     }
-    if (!dout) {
+    if (role == 0) {
       float* sc = reinterpret_cast<float*>(sm + G::oSC + buf * G::SCAL);
       if (r < n) {
         const int64_t s = (int64_t)path - l * p.S;
@@ -190,20 +216,33 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
         sc[r] = sc[kTcRows + r] = sc[2 * kTcRows + r] = 0.0f;
       }
     }
-    for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) {
-      const int rr = i >> zsh, c = i & ((1 << zsh) - 1);
-      if (rr < n && c < DF)
-        cp_async4(s_zraw + i, p.dz_rows + ((int64_t)bh * p.P + s_path[slot * kTcRows + rr]) * DF + c);
-      else
-        s_zraw[i] = 0.0f;
+    if ((DF & 3) == 0) {
+      // whole 16-byte pieces of the dz rows (the pad columns stay zero from the prologue)
+      const int cpr = DF >> 2;
+      for (int i = tid; i < kTcRows * cpr; i += blockDim.x) {
+        const int rr = i / cpr, c = i - rr * cpr;
+        float* d_ = s_zraw + (rr << zsh) + c * 4;
+        if (rr < n)
+          cp_async16(d_, p.dz_rows + ((int64_t)bh * p.P + s_path[slot * kTcRows + rr]) * DF + c * 4);
+        else
+          *reinterpret_cast<float4*>(d_) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    } else {
+      for (int i = tid; i < (kTcRows << zsh); i += blockDim.x) {
+        const int rr = i >> zsh, c = i & ((1 << zsh) - 1);
+        if (rr < n && c < DF)
+          cp_async4(s_zraw + i, p.dz_rows + ((int64_t)bh * p.P + s_path[slot * kTcRows + rr]) * DF + c);
+        else
+          s_zraw[i] = 0.0f;
+      }
     }
     if (t0 + kTcRows < end) fetch_paths(t0 + kTcRows, slot == 2 ? 0 : slot + 1);
     cp_async_commit();
   };
 
-  float acc_dc[2][2][4];
+  float acc_dc[kTcBwdDcItems][2][4];
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < kTcBwdDcItems; ++i)
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -227,22 +266,20 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
   int failed = 0;  // 1: a wait in the tile loop expired (the last commit was mS), 2: the final
                    // dq / dV / dK wait expired (the last commit was mD)
   int buf = 0, slot = 0;
-  // dq rows of the tile in ring slot `sl` with `n` pairs (this thread's pair, its half of the
+  // dq rows of the tile in ring slot `sl` with `n` pairs (this thread's pair, its part of the
   // columns), once its MMAs completed
   auto dq_out = [&](int sl, int n) {
     const uint32_t path = s_path[sl * kTcRows + r];
     float* dst = r < n ? p.dq_path + ((int64_t)bh * p.P + path) * D : nullptr;
 #pragma unroll
-    for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 32) {
-      float x[16], y[16];
-      tc_ld16x2(tQ + lane_addr + c0, tQ + lane_addr + c0 + 16, x, y);
+    for (int c0 = part * (D / kTcBwdParts); c0 < (part + 1) * (D / kTcBwdParts); c0 += 16) {
+      float x[16];
+      tc_ld16(tQ + lane_addr + c0, x);
       if (dst != nullptr) {
         float4* d4 = reinterpret_cast<float4*>(dst + c0);
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
+        for (int i = 0; i < 16; i += 4)
           d4[i >> 2] = make_float4(x[i] * p.scale, x[i + 1] * p.scale, x[i + 2] * p.scale, x[i + 3] * p.scale);
-          d4[(16 + i) >> 2] = make_float4(y[i] * p.scale, y[i + 1] * p.scale, y[i + 2] * p.scale, y[i + 3] * p.scale);
-        }
       }
     }
   };
@@ -259,10 +296,12 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        tc_mma(tS, tc_desc(smem_u32(sQ) + kk * 256, 128, D * 16), tc_desc(smem_u32(sK) + kk * 256, 128, D * 16),
-               idS, kk > 0 ? 1u : 0u);
-        tc_mma(tP, tc_desc(smem_u32(sG) + kk * 256, 128, D * 16), tc_desc(smem_u32(sV) + kk * 256, 128, D * 16),
-               idS, kk > 0 ? 1u : 0u);
+        // K-major over d: 16-column step kk is 32 bytes into atom column kk / 4
+        const uint32_t qo = (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, ko = (kk >> 2) * (LB * 128) + (kk & 3) * 32;
+        tc_mma(tS, tc_desc_sw(smem_u32(sQ) + qo, 16, 1024), tc_desc_sw(smem_u32(sK) + ko, 16, 1024), idS,
+               kk > 0 ? 1u : 0u);
+        tc_mma(tP, tc_desc_sw(smem_u32(sG) + qo, 16, 1024), tc_desc_sw(smem_u32(sV) + ko, 16, 1024), idS,
+               kk > 0 ? 1u : 0u);
       }
       tc_commit(mS);
     }
@@ -287,7 +326,7 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
     phS ^= 1u;
     tc_fence_after();
     {
-      // w P and dS of this thread's pair over its half of the keys
+      // w P and dS of this thread's pair over its part of the keys
       const float* sc = reinterpret_cast<const float*>(sm + G::oSC + buf * G::SCAL);
       const uint32_t path = s_path[slot * kTcRows + r];
       int vis = 0;
@@ -298,7 +337,7 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
       }
       const float w = sc[r], dl = sc[kTcRows + r], nlse2 = -sc[2 * kTcRows + r];
 #pragma unroll
-      for (int c0 = half * (LB / 2); c0 < (half + 1) * (LB / 2); c0 += 16) {
+      for (int c0 = part * (LB / kTcBwdParts); c0 < (part + 1) * (LB / kTcBwdParts); c0 += 16) {
         float sv[16], dv[16];
         tc_ld16x2(tS + lane_addr + c0, tP + lane_addr + c0, sv, dv);
         uint32_t pw[8], pd[8];
@@ -319,10 +358,11 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
             pd[i >> 1] = Mma<T>::pack(p0 * fmaf(w, dv[i], -dl), p1 * fmaf(w, dv[i + 1], -dl));
           }
         }
-        *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0, LB)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-        *reinterpret_cast<uint4*>(sWP + kmaj_off(r, c0 + 8, LB)) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
-        *reinterpret_cast<uint4*>(sDS + kmaj_off(r, c0, LB)) = make_uint4(pd[0], pd[1], pd[2], pd[3]);
-        *reinterpret_cast<uint4*>(sDS + kmaj_off(r, c0 + 8, LB)) = make_uint4(pd[4], pd[5], pd[6], pd[7]);
+        const uint32_t o0 = sw128_off(r, c0 >> 3, kTcRows), o1 = sw128_off(r, (c0 >> 3) + 1, kTcRows);
+        *reinterpret_cast<uint4*>(sWP + o0) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        *reinterpret_cast<uint4*>(sWP + o1) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+        *reinterpret_cast<uint4*>(sDS + o0) = make_uint4(pd[0], pd[1], pd[2], pd[3]);
+        *reinterpret_cast<uint4*>(sDS + o1) = make_uint4(pd[4], pd[5], pd[6], pd[7]);
       }
     }
     fence_async_smem();
@@ -333,17 +373,18 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
       // dq = dS K (K_blk as the MN-major B operand over its key rows)
 #pragma unroll
       for (int kk = 0; kk < LB / 16; ++kk)
-        tc_mma(tQ, tc_desc(smem_u32(sDS) + kk * 256, 128, LB * 16),
-               tc_desc(smem_u32(sK) + kk * 32 * D, D * 16, 128), idDQ, kk > 0 ? 1u : 0u);
+        tc_mma(tQ, tc_desc_sw(smem_u32(sDS) + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024),
+               tc_desc_sw(smem_u32(sK) + kk * 2048, LB * 128, 1024), idDQ, kk > 0 ? 1u : 0u);
       // dV += (w P)^T dO, dK += dS^T Q over the tile's pairs (the MMA's K), both operands
       // MN-major over their pair rows
       const int kend = (n + 15) >> 4;
       for (int kk = 0; kk < kend; ++kk) {
         const uint32_t acc = (t0 > beg || kk > 0) ? 1u : 0u;
-        const uint64_t dwp = tc_desc(smem_u32(sWP) + kk * 32 * LB, LB * 16, 128);
-        const uint64_t dds = tc_desc(smem_u32(sDS) + kk * 32 * LB, LB * 16, 128);
-        const uint64_t dgo = tc_desc(smem_u32(sG) + kk * 32 * D, D * 16, 128);
-        const uint64_t dq_ = tc_desc(smem_u32(sQ) + kk * 32 * D, D * 16, 128);
+        // MN-major over the pair rows: 16-row step kk is two 8-row groups (2048 bytes)
+        const uint64_t dwp = tc_desc_sw(smem_u32(sWP) + kk * 2048, kTcRows * 128, 1024);
+        const uint64_t dds = tc_desc_sw(smem_u32(sDS) + kk * 2048, kTcRows * 128, 1024);
+        const uint64_t dgo = tc_desc_sw(smem_u32(sG) + kk * 2048, kTcRows * 128, 1024);
+        const uint64_t dq_ = tc_desc_sw(smem_u32(sQ) + kk * 2048, kTcRows * 128, 1024);
         if constexpr (G::KEY_ROWS) {
           tc_mma(tV, dwp, dgo, idKV, acc);
           tc_mma(tK, dds, dq_, idKV, acc);
@@ -362,15 +403,15 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
     {
       const int kend = (n + 15) & ~15;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int item = warp + 8 * i;
+      for (int i = 0; i < kTcBwdDcItems; ++i) {
+        const int item = warp + kTcBwdWarps * i;
         if (item < zmt * NPAIR) {
           const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
           for (int kc = 0; kc < kend; kc += 16) {
             uint32_t ah[4], al[4], bb[4];
             frag_a_t(ah, s_zh, kZLd, zm, kc, lane);
             frag_a_t(al, s_zl, kZLd, zm, kc, lane);
-            frag_b_kn_core(bb, sQ, D, zn, kc, lane);
+            frag_b_kn_sw(bb, sQ, zn, kc, lane);
             Mma<T>::run(acc_dc[i][0], ah, bb);
             Mma<T>::run(acc_dc[i][0], al, bb);
             Mma<T>::run(acc_dc[i][1], ah, bb + 2);
@@ -408,8 +449,8 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
       const int g = lane >> 2, tq = lane & 3;
       float* dcp = p.dc_part + ((int64_t)bh * p.nb + j) * DF * D;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int item = warp + 8 * i;
+      for (int i = 0; i < kTcBwdDcItems; ++i) {
+        const int item = warp + kTcBwdWarps * i;
         if (item < zmt * NPAIR) {
           const int zm = (item / NPAIR) * 16, zn = (item % NPAIR) * 16;
 #pragma unroll
@@ -428,10 +469,10 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
     float* dkb = p.dk_attn + (int64_t)bh * p.N * D;
     const bool any = beg < end;
     if constexpr (G::KEY_ROWS) {
-      // lane = key row, columns = head_dim (this warp's half)
+      // lane = key row, columns = head_dim (this warp's part)
       const int64_t key = key0 + r;
 #pragma unroll
-      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 16) {
+      for (int c0 = part * (D / kTcBwdParts); c0 < (part + 1) * (D / kTcBwdParts); c0 += 16) {
         float x[16], y[16];
         tc_ld16x2(tV + lane_addr + c0, tK + lane_addr + c0, x, y);
         uint32_t pk[8];
@@ -447,10 +488,10 @@ __global__ void __launch_bounds__(256, 1) blk_attn_bwd_tc_kernel(const BlkMmaPar
                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
     } else {
-      // lane = head_dim column d, TMEM columns = keys (this warp's half)
+      // lane = head_dim column d, TMEM columns = keys (this warp's part)
       const int d = r;
 #pragma unroll
-      for (int c0 = half * (LB / 2); c0 < (half + 1) * (LB / 2); c0 += 16) {
+      for (int c0 = part * (LB / kTcBwdParts); c0 < (part + 1) * (LB / kTcBwdParts); c0 += 16) {
         float x[16], y[16];
         tc_ld16x2(tV + lane_addr + c0, tK + lane_addr + c0, x, y);
 #pragma unroll
