@@ -70,8 +70,14 @@ def _worker(rank, port, q):
             torch.manual_seed(99)
             out = sp_tree_attention(qq, kk, vv, causal, num_samples=S)
             out.backward(go[:, sl].contiguous())
-            if not torch.equal(out.detach(), ref[0][:, sl]):
+            # sampled rows bit for bit; the exact causal prefix (the first S positions, split
+            # over the ranks by heads) up to its split-K summation order
+            got, want = out.detach(), ref[0][:, sl]
+            e = max(0, min(S, N) - rank * n) if causal and N > S else 0
+            if not torch.equal(got[:, e:], want[:, e:]):
                 msgs.append(f"sp causal={causal} out")
+            if e and not torch.allclose(got[:, :e].float(), want[:, :e].float(), rtol=8e-3, atol=2e-3):
+                msgs.append(f"sp causal={causal} prefix out")
             for name, a, b in zip(("dq", "dk", "dv"), (qq.grad, kk.grad, vv.grad), ref[1:]):
                 if not torch.allclose(a.float(), b[:, sl].float(), rtol=2e-2, atol=2e-2):
                     msgs.append(f"sp causal={causal} {name}")
