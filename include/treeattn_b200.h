@@ -381,9 +381,10 @@ int ta_blocked_gumbel_fill(const ta_shape* shape, const ta_blocked* cfg, const t
 /*
  * Leaf-block attention on the tensor cores (16-bit inputs, head_dim 64 or 128, leaf block 16..128;
  * the backward also needs leaf_block >= 32 and leaf_block * head_dim <= 8192): the forward then
- * takes `path_out` (float32: [B*H][L*S][D] rows of w_s * o_s per path followed by [B*H][L*S]
- * base-2 log-sum-exps of each path's scaled leaf-block scores, B*H*L*S*(D+1) floats in all,
- * kept for the backward) and a workspace of ta_blocked_forward_workspace_size bytes; with
+ * takes `path_out` ([B*H][L*S][D] rows of w_s * o_s per path in the input dtype followed by
+ * [B*H][L*S] float32 base-2 log-sum-exps of each path's scaled leaf-block scores,
+ * B*H*L*S*(D/2+1) floats in all, kept for the backward) and a workspace of
+ * ta_blocked_forward_workspace_size bytes; with
  * path_out NULL (or for other shapes) everything runs on the CUDA cores.
  * ta_blocked_uses_tensor_cores tells which.
  */

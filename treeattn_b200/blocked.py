@@ -94,8 +94,9 @@ class BlockedTreeAttentionFunction(torch.autograd.Function):
         lib = L.load()
         path_out, ws = None, None
         if lib.ta_blocked_uses_tensor_cores(ctypes.byref(shape), ctypes.byref(cfg), 0):
-            # w_s o_s rows [B*H][L*S][D], then each pair's log-sum-exp [B*H][L*S]
-            path_out = torch.empty(B * H * Lq * num_samples * (D + 1), device=q.device,
+            # w_s o_s rows [B*H][L*S][D] in the input dtype, then each pair's float32
+            # log-sum-exp [B*H][L*S]
+            path_out = torch.empty(B * H * Lq * num_samples * (D // 2 + 1), device=q.device,
                                    dtype=torch.float32)
             ws_bytes = lib.ta_blocked_forward_workspace_size(ctypes.byref(shape), ctypes.byref(cfg))
             ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)

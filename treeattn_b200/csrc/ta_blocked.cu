@@ -291,9 +291,9 @@ extern "C" int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg,
   p.dk = (char*)dk; p.dks = dkl.seq; p.dkb = dkl.batch; p.dkh = dkl.head;
   p.dv = (char*)dv; p.dvs = dvl.seq; p.dvb = dvl.batch; p.dvh = dvl.head;
   if (mma) {
-    p.path_out = const_cast<float*>(path_out);
+    p.path_out = const_cast<float*>(path_out);  // 16-bit rows, then the lse (see the header)
     p.delta = (float*)(base + w.delta); p.dq_tree = (float*)(base + w.dq_tree);
-    p.dq_path = (float*)(base + w.dq_path);
+    p.dq_path = base + w.dq_path;
     p.ranges = (uint32_t*)(base + w.ranges);
     p.use_tcgen05_bwd = g_use_tcgen05_bwd && blk_tc_bwd_shape(p.Lb, p.D);
     if (p.use_tcgen05_bwd) {

@@ -80,10 +80,10 @@ struct BlkParams {
   // tensor-core leaf-block path
   int32_t sample_only;   // forward: tree walk only (weights = softmax, sort records)
   int32_t summary_only;  // backward block pass: summary gradients only
-  float* path_out;       // [B*H][P][D] w_s o_s
+  void* path_out;        // [B*H][P][D] w_s o_s in the input dtype, then [B*H][P] float lse
   float* delta;          // [B*H][P]
   float* dq_tree;        // [L][B][H][D] float32 tree part of dq
-  float* dq_path;        // [B*H][P][D]
+  void* dq_path;         // [B*H][P][D] input dtype
   volatile int32_t* status;  // tensor-core wait status word (mapped host memory)
   uint64_t wait_ns;          // bound of one tensor-core mbarrier wait
   int32_t use_tcgen05;   // leaf-block forward on tcgen05 (else mma.sync)
@@ -431,10 +431,10 @@ __global__ void __launch_bounds__(kBlkWarps * 32) blk_bwd_query_kernel(const Blk
   float wg = 0.0f;
   const bool mma = p.path_out != nullptr;
   for (int s = 0; mma && s < p.S; ++s) {
-    const float* orow = p.path_out + ((int64_t)bh * p.P + (int64_t)l * p.S + s) * p.D;
+    const T* orow = reinterpret_cast<const T*>(p.path_out) + ((int64_t)bh * p.P + (int64_t)l * p.S + s) * p.D;
     float part = 0.0f;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) part = fmaf(gf[e], orow[lane * EPL + e], part);
+    for (int e = 0; e < EPL; ++e) part = fmaf(gf[e], static_cast<float>(orow[lane * EPL + e]), part);
     const float dl = warp_sum(part);
     if (lane == 0) {
       s_gs[s] = dl;
@@ -975,16 +975,16 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
     const int64_t l = l0 + qi;
     if (l >= p.L) continue;
     const int64_t prow = (int64_t)bh * p.P + l * p.S + sp;
-    const float4* orow = reinterpret_cast<const float4*>(p.path_out + prow * D);
+    const uint2* orow = reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p.path_out) + prow * D);
     const uint16_t* grow = s_g + qi * LD;
     float dl = 0.0f;
 #pragma unroll 4
     for (int c = 0; c < D / 4; ++c) {
-      const float4 o = orow[c];
-      dl = fmaf(raw_to_float<T>(grow[4 * c]), o.x, dl);
-      dl = fmaf(raw_to_float<T>(grow[4 * c + 1]), o.y, dl);
-      dl = fmaf(raw_to_float<T>(grow[4 * c + 2]), o.z, dl);
-      dl = fmaf(raw_to_float<T>(grow[4 * c + 3]), o.w, dl);
+      const uint2 o = orow[c];
+      dl = fmaf(raw_to_float<T>(grow[4 * c]), raw_to_float<T>((uint16_t)(o.x & 0xFFFFu)), dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 1]), raw_to_float<T>((uint16_t)(o.x >> 16)), dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 2]), raw_to_float<T>((uint16_t)(o.y & 0xFFFFu)), dl);
+      dl = fmaf(raw_to_float<T>(grow[4 * c + 3]), raw_to_float<T>((uint16_t)(o.y >> 16)), dl);
     }
     s_dl[qi * p.S + sp] = dl;
     p.delta[prow] = dl;
@@ -1128,9 +1128,10 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
 // out[l,b,h] = sum_s path_out[b*H+h][l*S+s] in path order (tensor-core forward); with
 // `base` (dq), base[l,b,h] + sum_s. One row (l, b, h) per D/4 threads, four channels each.
 template <typename T>
-__device__ __forceinline__ void blk_combine_rows(const BlkParams& p, const float* paths,
+__device__ __forceinline__ void blk_combine_rows(const BlkParams& p, const void* paths_,
                                                  const float* base, char* dst, int64_t ss,
                                                  int64_t sb, int64_t sh) {
+  const T* paths = reinterpret_cast<const T*>(paths_);  // per-path rows in the input dtype
   const int tpr = p.D >> 2, rpb = 256 / tpr;
   const int rl = threadIdx.x / tpr, c = (threadIdx.x - rl * tpr) * 4;
   if (rl >= rpb) return;
@@ -1141,13 +1142,15 @@ __device__ __forceinline__ void blk_combine_rows(const BlkParams& p, const float
   const int b = (int)(lb % p.B);
   const int64_t l = lb / p.B;
   float4 acc = base ? *reinterpret_cast<const float4*>(base + row * p.D + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  const float* src = paths + (((int64_t)b * p.H + h) * p.P + l * p.S) * p.D + c;
-  for (int s = 0; s < p.S; ++s) {
-    const float4 v = *reinterpret_cast<const float4*>(src + (int64_t)s * p.D);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
+  const T* src = paths + (((int64_t)b * p.H + h) * p.P + l * p.S) * p.D + c;
+  if constexpr (sizeof(T) == 2) {  // (the tensor-core paths, the only users, are 16-bit)
+    for (int s = 0; s < p.S; ++s) {
+      const uint2 v = *reinterpret_cast<const uint2*>(src + (int64_t)s * p.D);
+      acc.x += raw_to_float<T>((uint16_t)(v.x & 0xFFFFu));
+      acc.y += raw_to_float<T>((uint16_t)(v.x >> 16));
+      acc.z += raw_to_float<T>((uint16_t)(v.y & 0xFFFFu));
+      acc.w += raw_to_float<T>((uint16_t)(v.y >> 16));
+    }
   }
   T* o = reinterpret_cast<T*>(dst) + l * ss + (int64_t)b * sb + (int64_t)h * sh + c;
   o[0] = static_cast<T>(acc.x);
@@ -1274,7 +1277,9 @@ static BlkMmaParams blk_mma_params(const BlkParams& p) {
   m.skeys = p.skeys; m.svals = p.svals; m.weights = p.weights; m.path_out = p.path_out;
   m.ranges = p.ranges;
   // the per-pair log-sum-exp follows the [B*H][P][D] rows in the same buffer
-  m.lse = p.path_out != nullptr ? p.path_out + (int64_t)p.B * p.H * p.P * p.D : nullptr;
+  m.lse = p.path_out != nullptr
+              ? reinterpret_cast<float*>(static_cast<char*>(p.path_out) + (int64_t)p.B * p.H * p.P * p.D * 2)
+              : nullptr;
   m.delta = p.delta; m.dq_path = p.dq_path; m.dk_attn = p.dk_attn;
   m.dz_rows = p.dz_rows; m.dc_part = p.dc_part; m.DF = p.Dp * p.f;
   m.dv = p.dv; m.dvs = p.dvs; m.dvb = p.dvb; m.dvh = p.dvh;
@@ -1533,7 +1538,7 @@ static BlkWs blk_ws(const BlkParams& p, bool mma) {
   } else {
     w.delta = take(HB * p.P * 4);
     w.dq_tree = take(HB * p.L * p.D * 4);
-    w.dq_path = take(HB * p.P * p.D * 4);
+    w.dq_path = take(HB * p.P * p.D * 2);  // 16-bit rows (the tensor-core paths are 16-bit)
     w.ranges = take(HB * (p.nb + 1) * 4);
   }
   w.dz = take(HB * p.P * (p.Dp * p.f > 0 ? p.Dp * p.f : 1) * 4);

@@ -99,10 +99,10 @@ struct BlkMmaParams {
   const uint32_t* skeys; const uint32_t* svals;  // [B*H][P] sorted by leaf block
   const uint32_t* ranges;  // [B*H][nb + 1] first sorted pair of each leaf block (or null)
   const float* weights;    // [L][B][H][S] path weights
-  float* path_out;         // [B*H][P][D]: w_s o_s (forward out, backward in)
+  void* path_out;          // [B*H][P][D] input dtype: w_s o_s (forward out, backward in)
   float* lse;              // [B*H][P]: base-2 log-sum-exp of each pair's scaled scores
   const float* delta;      // [B*H][P] dO_q . (w_s o_s) (backward)
-  float* dq_path;          // [B*H][P][D] (backward)
+  void* dq_path;           // [B*H][P][D] input dtype (backward)
   float* dk_attn;          // [B*H][N][D] (backward)
   const float* dz_rows;    // [B*H][P][DF] per-path summary coefficients (backward)
   float* dc_part;          // [B*H][nb][DF][D] per-block summary partials (backward)
@@ -265,21 +265,21 @@ __global__ void __launch_bounds__(128, LB * D > 8192 ? 2 : 4) blk_attn_fwd_mma_k
       const int64_t path = vals[t0 + r0];
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum0;
-      float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
+      T* dst = reinterpret_cast<T*>(p.path_out) + ((int64_t)bh * p.P + path) * D;
       if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx0 + __log2f(sum0);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
-        *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][0] * w, oc[t][1] * w);
+        *reinterpret_cast<uint32_t*>(dst + t * 8 + tq * 2) = Mma<T>::pack(oc[t][0] * w, oc[t][1] * w);
     }
     if (r1 < n) {
       const int64_t path = vals[t0 + r1];
       const int64_t l = path / p.S, s = path - l * p.S;
       const float w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum1;
-      float* dst = p.path_out + ((int64_t)bh * p.P + path) * D;
+      T* dst = reinterpret_cast<T*>(p.path_out) + ((int64_t)bh * p.P + path) * D;
       if (tq == 0 && p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = mx1 + __log2f(sum1);
 #pragma unroll
       for (int t = 0; t < G::NT_D; ++t)
-        *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(oc[t][2] * w, oc[t][3] * w);
+        *reinterpret_cast<uint32_t*>(dst + t * 8 + tq * 2) = Mma<T>::pack(oc[t][2] * w, oc[t][3] * w);
     }
   }  cp_async_wait_0();  // a block without pairs never waited for its K / V copies
 }
@@ -515,16 +515,16 @@ __global__ void __launch_bounds__(256) blk_attn_bwd_mma_kernel(const BlkMmaParam
         }
       }
       if (r0 < n) {
-        float* dst = p.dq_path + ((int64_t)bh * p.P + s_path[r0]) * D;
+        T* dst = reinterpret_cast<T*>(p.dq_path) + ((int64_t)bh * p.P + s_path[r0]) * D;
 #pragma unroll
         for (int t = 0; t < G::NT_D; ++t)
-          *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(dq[t][0] * p.scale, dq[t][1] * p.scale);
+          *reinterpret_cast<uint32_t*>(dst + t * 8 + tq * 2) = Mma<T>::pack(dq[t][0] * p.scale, dq[t][1] * p.scale);
       }
       if (r1 < n) {
-        float* dst = p.dq_path + ((int64_t)bh * p.P + s_path[r1]) * D;
+        T* dst = reinterpret_cast<T*>(p.dq_path) + ((int64_t)bh * p.P + s_path[r1]) * D;
 #pragma unroll
         for (int t = 0; t < G::NT_D; ++t)
-          *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(dq[t][2] * p.scale, dq[t][3] * p.scale);
+          *reinterpret_cast<uint32_t*>(dst + t * 8 + tq * 2) = Mma<T>::pack(dq[t][2] * p.scale, dq[t][3] * p.scale);
       }
     } else {
       // rows of an absent warp tile: zero so phase 3 may read the whole tile

@@ -11,7 +11,7 @@
 //   3. every thread loads its own S row from TMEM (tcgen05.ld 32x32b), applies the scale and
 //      its causal mask, and writes exp(s - max) as 16-bit P into shared memory (K-major);
 //   4. O = P V as Lb/16 tcgen05.mma (N = D) into a second TMEM range; every thread reads its O
-//      row, scales it by w_s / rowsum and stores w_s o_s to the float32 per-path buffer.
+//      row, scales it by w_s / rowsum and stores w_s o_s (input dtype) to the per-path buffer.
 // Descriptor and instruction-descriptor fields follow the sm100 UMMA layout (shared-memory
 // descriptor: start >> 4 in [0,14), leading-byte offset >> 4 in [16,30), stride-byte offset
 // >> 4 in [32,46), version 1 in [46,48), layout type in [61,64) = 0 for no swizzle; instruction
@@ -304,11 +304,11 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
     tc_fence_after();
     // O row: every lane executes the same tcgen05.ld; only valid rows store
     float w = 0.0f;
-    float4* dst = nullptr;
+    uint4* dst = nullptr;
     if (r < n) {
       const int64_t l = path / p.S, s = path - l * p.S;
       w = p.weights[(((int64_t)l * p.B + b) * p.H + h) * p.S + s] / sum;
-      dst = reinterpret_cast<float4*>(p.path_out + ((int64_t)bh * p.P + path) * D);
+      dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.path_out) + ((int64_t)bh * p.P + path) * D);
       if (p.lse != nullptr) p.lse[(int64_t)bh * p.P + path] = (row_max + logf(sum)) * kLog2e;
     }
     __syncwarp();
@@ -317,9 +317,11 @@ __global__ void __launch_bounds__(kTcRows) blk_attn_fwd_tc_kernel(const BlkMmaPa
       float v[16];
       tc_ld16(tO + lane_base + c0, v);
       if (dst != nullptr) {
+        uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          dst[(c0 + i) >> 2] = make_float4(v[i] * w, v[i + 1] * w, v[i + 2] * w, v[i + 3] * w);
+        for (int i = 0; i < 16; i += 2) pk[i >> 1] = Mma<T>::pack(v[i] * w, v[i + 1] * w);
+        dst[c0 >> 3] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[(c0 >> 3) + 1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
     }
     tc_fence_before();

@@ -19,7 +19,7 @@
 //      after it) as cp.async into the other buffers, so no thread waits on a global load, and
 //      add this tile's summary gradients dc += dz^T Q on mma.sync (dz split into 16-bit high
 //      and low parts; M = levels * fanout is too small for tcgen05);
-//   5. each warp reads its dq rows back and stores them to the float32 per-path buffer, while
+//   5. each warp reads its dq rows back and stores them (input dtype) to the per-path buffer, while
 //      the next tile's S and dP MMAs run.
 // A block's pair range comes from a table built once per call (blk_block_ranges_kernel).
 // Every operand tile is stored as 128-byte-swizzled atoms (8 rows x 64 16-bit columns, the
@@ -270,16 +270,18 @@ __global__ void __launch_bounds__(kTcBwdThreads, 1) blk_attn_bwd_tc_kernel(const
   // columns), once its MMAs completed
   auto dq_out = [&](int sl, int n) {
     const uint32_t path = s_path[sl * kTcRows + r];
-    float* dst = r < n ? p.dq_path + ((int64_t)bh * p.P + path) * D : nullptr;
+    T* dst = r < n ? reinterpret_cast<T*>(p.dq_path) + ((int64_t)bh * p.P + path) * D : nullptr;
 #pragma unroll
     for (int c0 = part * (D / kTcBwdParts); c0 < (part + 1) * (D / kTcBwdParts); c0 += 16) {
       float x[16];
       tc_ld16(tQ + lane_addr + c0, x);
       if (dst != nullptr) {
-        float4* d4 = reinterpret_cast<float4*>(dst + c0);
+        uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          d4[i >> 2] = make_float4(x[i] * p.scale, x[i + 1] * p.scale, x[i + 2] * p.scale, x[i + 3] * p.scale);
+        for (int i = 0; i < 16; i += 2) pk[i >> 1] = Mma<T>::pack(x[i] * p.scale, x[i + 1] * p.scale);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+        d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
     }
   };
