@@ -22,6 +22,18 @@ NUM_SAMPLES_ENV_VAR = "TREEATTN_NUM_SAMPLES"
 _DEFAULT_BLOCK_SIZE = 256
 
 
+_NOISE_STREAMS: dict = {}
+
+
+def _noise_stream(device):
+    """One side stream per device for the forward's noise draw."""
+    key = torch.device(device).index
+    st = _NOISE_STREAMS.get(key)
+    if st is None:
+        st = _NOISE_STREAMS[key] = torch.cuda.Stream(device)
+    return st
+
+
 class TreeAttentionFunction(torch.autograd.Function):
     """Stochastic non-causal tree attention on (seq, B, H, D) views.
 
@@ -59,7 +71,25 @@ class TreeAttentionBshdFunction(torch.autograd.Function):
     def forward(ctx, q, k, v, num_samples, max_logit, gumbels=None, causal=False, shard=None,
                 node_layout="reference"):
         qv, kv, vv = (t.transpose(0, 1) for t in (q, k, v))  # logical (S, B, H, D) views
+        side = None
+        if (q.is_cuda and not causal and gumbels is None and kv.shape[0] > 1
+                and ops.is_power_of_two(kv.shape[0])):
+            # the noise draw does not depend on the tree: it runs on a side stream beside the
+            # tree build (the generator offsets are reserved on the host in the same order)
+            # (the buffer is allocated on the current stream, which waits for the draw before
+            # its first use, so the caching allocator reuses it step after step)
+            Lq, B, H = qv.shape[:3]
+            buf = torch.empty((ops.log_n_of(kv.shape[0]), Lq * B * H * num_samples * 2),
+                              device=q.device, dtype=torch.float32)
+            cur = torch.cuda.current_stream(q.device)
+            side = _noise_stream(q.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                gumbels = ops.draw_gumbels(Lq, B, H, kv.shape[0], num_samples, q.device,
+                                           shard=shard, out=buf)
         k_int = ops.tree_build(kv, node_layout=node_layout)
+        if side is not None:
+            cur.wait_stream(side)
         ctx.node_layout = node_layout
         out = torch.empty_like(q)
         ctx.num_samples = num_samples

@@ -242,6 +242,37 @@ class ForwardResult:
     branch_prob: torch.Tensor | None  # (B*H, L*S, stride) float32, for the backward
 
 
+def draw_gumbels(Lq: int, B: int, H: int, N: int, num_samples: int, device, *, shard=None,
+                 query_rows: tuple[int, int] | None = None, rng: L.Rng | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """The Gumbel noise ``forward`` would draw for q of shape (Lq, B, H, D) over N keys, as a
+    float32 (log2 N, Lq * B * H * num_samples * 2) tensor on the current stream: reserved from
+    torch's CUDA generator exactly as the reference's per-depth draws are (the matching slice of
+    the full problem's draw for a ``shard`` or ``query_rows`` block). Passing it to ``forward``
+    as ``gumbels`` gives the same result as letting ``forward`` draw it. ``out`` is an optional
+    float32 (log2 N, numel) buffer to fill."""
+    numel = Lq * B * H * num_samples * 2
+    ln = log_n_of(N)
+    if out is None:
+        out = torch.empty((ln, numel), device=device, dtype=torch.float32)
+    sharded = (shard is not None and not shard.is_full) or query_rows is not None
+    if not sharded:
+        if rng is None:
+            rng = reserve_gumbel_stream(device, numel, ln)
+        return gumbel_fill(out, rng)
+    from .sharding import ShardSpec
+    spec = shard if shard is not None else ShardSpec(B, 0, B, H, 0, H)
+    if (spec.batch_count, spec.head_count) != (B, H):
+        raise ValueError(f"shard {spec} does not match q's (batch, heads) = ({B}, {H})")
+    row0, row_total = query_rows if query_rows is not None else (0, Lq)
+    if row0 < 0 or row0 + Lq > row_total:
+        raise ValueError(f"query rows {row0}..{row0 + Lq} outside {row_total}")
+    if rng is None:
+        rng = reserve_gumbel_stream(
+            device, row_total * spec.batch_total * spec.head_total * num_samples * 2, ln)
+    return gumbel_fill_shard(out, rng, Lq, spec, num_samples * 2, row_total=row_total, row0=row0)
+
+
 def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: int, *,
             max_logit: float = MAX_LOGIT, out: torch.Tensor | None = None,
             gumbels: torch.Tensor | None = None, want_packed: bool = False,
@@ -280,21 +311,10 @@ def forward(q: torch.Tensor, k_int: torch.Tensor, v: torch.Tensor, num_samples: 
     rng_p = None
     sharded = (shard is not None and not shard.is_full) or query_rows is not None
     if sharded and gumbels is None:
-        from .sharding import ShardSpec
-        spec = shard if shard is not None else ShardSpec(B, 0, B, H, 0, H)
-        if (spec.batch_count, spec.head_count) != (B, H):
-            raise ValueError(f"shard {spec} does not match q's (batch, heads) = ({B}, {H})")
-        row0, row_total = query_rows if query_rows is not None else (0, Lq)
-        if row0 < 0 or row0 + Lq > row_total:
-            raise ValueError(f"query rows {row0}..{row0 + Lq} outside {row_total}")
         if fused_rng:
             raise ValueError("fused_rng does not support shards")
-        if rng is None:
-            rng = reserve_gumbel_stream(
-                dev, row_total * spec.batch_total * spec.head_total * num_samples * 2, log_n_of(N))
-        gumbels = gumbel_fill_shard(
-            torch.empty((log_n_of(N), numel), device=dev, dtype=torch.float32), rng, Lq, spec,
-            num_samples * 2, row_total=row_total, row0=row0)
+        gumbels = draw_gumbels(Lq, B, H, N, num_samples, dev, shard=shard, query_rows=query_rows,
+                               rng=rng)
     if gumbels is not None:
         gumbels = gumbels.to(device=dev, dtype=torch.float32).contiguous()
     else:
