@@ -1081,7 +1081,8 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
   for (int t = 0; t < NTW; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
   for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
     __syncthreads();  // DZ complete / previous chunk consumed
-    walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
+    // (a single chunk is still in shared memory from the score pass)
+    if (RP > kWalkChunk) walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
     __syncthreads();
 #pragma unroll 2
     for (int k0 = 0; k0 < kWalkChunk; k0 += 16) {
