@@ -245,6 +245,7 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
     }
     p.keys0 = (uint32_t*)((char*)ws + w.keys[0]);
     p.vals0 = (uint32_t*)((char*)ws + w.vals[0]);
+    if (p.R > 0) p.summ_split = (uint16_t*)((char*)ws + w.split);
     sp = blk_sort_params(p, (char*)ws, w.keys, w.vals, w.hist);
   }
   cudaStream_t st = (cudaStream_t)stream;
@@ -295,6 +296,7 @@ extern "C" int ta_blocked_backward(const ta_shape* shape, const ta_blocked* cfg,
     p.delta = (float*)(base + w.delta); p.dq_tree = (float*)(base + w.dq_tree);
     p.dq_path = base + w.dq_path;
     p.ranges = (uint32_t*)(base + w.ranges);
+    if (p.R > 0) p.summ_split = (uint16_t*)(base + w.split);
     p.use_tcgen05_bwd = g_use_tcgen05_bwd && blk_tc_bwd_shape(p.Lb, p.D);
     if (p.use_tcgen05_bwd) {
       int32_t* word = tc_status_word();

@@ -89,6 +89,7 @@ struct BlkParams {
   int32_t use_tcgen05;   // leaf-block forward on tcgen05 (else mma.sync)
   int32_t use_tcgen05_bwd;  // leaf-block backward on tcgen05 where its shape allows
   uint32_t* ranges;          // [B*H][nb + 1] first sorted pair of each leaf block
+  uint16_t* summ_split;      // [2][B*H][RP][D] summaries as 16-bit high / low parts (or null)
 };
 
 template <typename T, int EPL>
@@ -776,6 +777,21 @@ template <typename T, int D>
 __device__ __forceinline__ void walk_load_chunk(const BlkParams& p, int bh, int r0, uint16_t* s_chi,
                                                 uint16_t* s_clo) {
   constexpr int LD = D + 8;
+  if (p.summ_split != nullptr) {
+    // the rows were split once per call (blk_split_summaries_kernel): 16-byte cp.async copies,
+    // completed by the caller's cp_async_wait_0
+    constexpr int CPR = D * 2 / 16;
+    const int RP = walk_rows_pad(p.R);
+    const int64_t half = (int64_t)p.B * p.H * RP * D;
+    const uint16_t* hsrc = p.summ_split + ((int64_t)bh * RP + r0) * D;
+    for (int i = threadIdx.x; i < kWalkChunk * CPR; i += blockDim.x) {
+      const int r = i / CPR, c = i - r * CPR;
+      cp_async16(s_chi + r * LD + c * 8, hsrc + (int64_t)r * D + c * 8);
+      cp_async16(s_clo + r * LD + c * 8, hsrc + half + (int64_t)r * D + c * 8);
+    }
+    cp_async_commit();
+    return;
+  }
   const float* csrc = p.summ + (int64_t)bh * p.R * D;
   for (int i = threadIdx.x; i < kWalkChunk * D / 2; i += blockDim.x) {
     const int r = i / (D / 2), c = (i - r * (D / 2)) * 2;
@@ -791,6 +807,28 @@ __device__ __forceinline__ void walk_load_chunk(const BlkParams& p, int bh, int 
     *reinterpret_cast<uint32_t*>(s_chi + r * LD + c) = hi;
     *reinterpret_cast<uint32_t*>(s_clo + r * LD + c) = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
   }
+}
+
+// summaries [B*H][R][D] float32 -> 16-bit high and low parts [2][B*H][RP][D] (rows >= R zero)
+template <typename T>
+__global__ void __launch_bounds__(256) blk_split_summaries_kernel(const BlkParams p) {
+  const int RP = walk_rows_pad(p.R);
+  const int64_t n = (int64_t)p.B * p.H * RP * p.D;
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (i >= n) return;
+  const int64_t bh = i / ((int64_t)RP * p.D), rem = i - bh * RP * p.D;
+  const int64_t r = rem / p.D, c = rem - r * p.D;
+  float2 v = make_float2(0.f, 0.f);
+  if (r < p.R) v = *reinterpret_cast<const float2*>(p.summ + (bh * p.R + r) * p.D + c);
+  const uint32_t hi = Mma<T>::pack(v.x, v.y);
+  float2 hf;
+  if constexpr (std::is_same<T, __half>::value) {
+    hf = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  } else {
+    hf = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+  }
+  *reinterpret_cast<uint32_t*>(p.summ_split + i) = hi;
+  *reinterpret_cast<uint32_t*>(p.summ_split + n + i) = Mma<T>::pack(v.x - hf.x, v.y - hf.y);
 }
 
 // Z[q][r] = q . c_r for the CTA's kWalkQ query rows (s_q, 16-bit) and every summary row, on
@@ -1082,7 +1120,10 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
   for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
     __syncthreads();  // DZ complete / previous chunk consumed
     // (a single chunk is still in shared memory from the score pass)
-    if (RP > kWalkChunk) walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
+    if (RP > kWalkChunk) {
+      walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
+      cp_async_wait_0();
+    }
     __syncthreads();
 #pragma unroll 2
     for (int k0 = 0; k0 < kWalkChunk; k0 += 16) {
@@ -1431,6 +1472,10 @@ int blk_fwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
           constexpr int D = 32 * EPL;
           const size_t wsm = walk_smem(p.R, D, p.S);
           cudaFuncSetAttribute(blk_walk_mma_kernel<T, D, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm);
+          if (p.summ_split != nullptr) {
+            const int64_t ns = (int64_t)p.B * p.H * walk_rows_pad(p.R) * D / 2;
+            blk_split_summaries_kernel<T><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(p);
+          }
           const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
           blk_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
         } else {
@@ -1469,6 +1514,10 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
       const size_t wsm = bwd_walk_smem(p.R, D, p.S, p.Dp * F);
       if (mma && wsm <= 220 * 1024 && p.S * kWalkQ <= 4 * 256 && p.Dp * F <= kDFMax) {
         cudaFuncSetAttribute(blk_bwd_walk_mma_kernel<T, D, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm);
+        if (p.summ_split != nullptr) {
+          const int64_t ns = (int64_t)p.B * p.H * walk_rows_pad(p.R) * D / 2;
+          blk_split_summaries_kernel<T><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(p);
+        }
         const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
         blk_bwd_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
         done = true;
@@ -1519,7 +1568,7 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
 }
 
 struct BlkWs {
-  size_t keys[2], vals[2], hist, ds, wp, dz, dk_attn, dc_part, dc, delta, dq_tree, dq_path, ranges, total;
+  size_t keys[2], vals[2], hist, ds, wp, dz, dk_attn, dc_part, dc, delta, dq_tree, dq_path, ranges, split, total;
 };
 
 // Backward workspace; `mma` = tensor-core leaf-block path (no per-path dS / wP rows, but
@@ -1541,6 +1590,7 @@ static BlkWs blk_ws(const BlkParams& p, bool mma) {
     w.dq_tree = take(HB * p.L * p.D * 4);
     w.dq_path = take(HB * p.P * p.D * 2);  // 16-bit rows (the tensor-core paths are 16-bit)
     w.ranges = take(HB * (p.nb + 1) * 4);
+    w.split = take((size_t)2 * HB * walk_rows_pad(p.R > 0 ? p.R : 1) * p.D * 2);
   }
   w.dz = take(HB * p.P * (p.Dp * p.f > 0 ? p.Dp * p.f : 1) * 4);
   w.dk_attn = take(HB * p.N * p.D * 4);
@@ -1560,6 +1610,7 @@ static BlkWs blk_fwd_ws(const BlkParams& p) {
   w.keys[0] = take(HB * p.P * 4); w.keys[1] = take(HB * p.P * 4);
   w.vals[0] = take(HB * p.P * 4); w.vals[1] = take(HB * p.P * 4);
   w.hist = take(HB * kRadix * tiles * 4);
+  w.split = take((size_t)2 * HB * walk_rows_pad(p.R > 0 ? p.R : 1) * p.D * 2);
   w.total = off;
   return w;
 }
