@@ -392,8 +392,8 @@ int32_t ta_blocked_uses_tensor_cores(const ta_shape* shape, const ta_blocked* cf
                                      int32_t backward);
 /*
  * Process-wide choice of the tensor-core forward: 1 = tcgen05 with TMEM accumulators, 0 =
- * mma.sync (default; it measured faster at the benchmark configurations). Returns the previous
- * setting.
+ * mma.sync, -1 = by shape (the default: tcgen05 at leaf_block 128, mma.sync below, as measured
+ * at the benchmark configurations). Returns the previous setting.
  */
 int32_t ta_blocked_set_tcgen05(int32_t enable);
 /*

@@ -134,7 +134,7 @@ namespace {
 // leaf-block forward on tcgen05 (1) or mma.sync (0). mma.sync is the default: it measured
 // faster (config 2: 1.32 vs 1.54 ms per forward, config 3: 7.0 vs 9.6 ms), the tcgen05 kernel
 // serialising gather, MMA and epilogue per 128-pair tile at two CTAs per SM.
-int g_use_tcgen05 = 0;
+int g_use_tcgen05 = -1;  // -1: by shape (tcgen05 at leaf block 128), 0: mma.sync, 1: tcgen05
 int g_use_tcgen05_bwd = 1;
 std::atomic<uint64_t> g_tc_wait_ns{kTcWaitNs};
 std::mutex g_tc_status_mu;
@@ -173,7 +173,7 @@ int check_tc_status() {
 
 extern "C" int32_t ta_blocked_set_tcgen05(int32_t enable) {
   const int32_t old = g_use_tcgen05;
-  g_use_tcgen05 = enable ? 1 : 0;
+  g_use_tcgen05 = enable < 0 ? -1 : (enable ? 1 : 0);
   return old;
 }
 
@@ -232,7 +232,9 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
     const BlkWs w = blk_fwd_ws(p);
     if (!ws || ws_bytes < w.total) return fail(TA_ERR_WORKSPACE, "blocked forward workspace too small");
     p.path_out = path_out;
-    p.use_tcgen05 = g_use_tcgen05;
+    // measured per forward: tcgen05 2.71 vs mma.sync 3.61 ms at leaf block 128 (config 3),
+    // 0.65 vs 0.55 ms at leaf block 64 (config 2)
+    p.use_tcgen05 = g_use_tcgen05 < 0 ? (p.Lb == 128 ? 1 : 0) : g_use_tcgen05;
     if (p.use_tcgen05) {
       int32_t* word = tc_status_word();
       void* dword = nullptr;
@@ -246,6 +248,7 @@ extern "C" int ta_blocked_forward(const ta_shape* shape, const ta_blocked* cfg, 
     p.keys0 = (uint32_t*)((char*)ws + w.keys[0]);
     p.vals0 = (uint32_t*)((char*)ws + w.vals[0]);
     if (p.R > 0) p.summ_split = (uint16_t*)((char*)ws + w.split);
+    p.ranges = (uint32_t*)((char*)ws + w.ranges);
     sp = blk_sort_params(p, (char*)ws, w.keys, w.vals, w.hist);
   }
   cudaStream_t st = (cudaStream_t)stream;

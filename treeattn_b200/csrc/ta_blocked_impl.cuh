@@ -1377,17 +1377,29 @@ inline bool blk_tc_bwd_shape(int Lb, int D) {
 
 template <typename T, int LB, int D>
 static void launch_attn_fwd_tc(const BlkMmaParams& m, unsigned grid, cudaStream_t st) {
-  constexpr size_t smem = blk_tc_fwd_smem<LB, D>();
-  cudaFuncSetAttribute(blk_attn_fwd_tc_kernel<T, LB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  blk_attn_fwd_tc_kernel<T, LB, D><<<grid, kTcRows, smem, st>>>(m);
+  if constexpr (BlkTcFwdGeom<LB, D>::OK) {
+    constexpr size_t smem = BlkTcFwdGeom<LB, D>::SMEM;
+    static std::atomic<uint32_t> set_on{0};  // devices whose function attribute is set
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint32_t bit = 1u << (dev & 31);
+    if (!(set_on.load() & bit)) {
+      cudaFuncSetAttribute(blk_attn_fwd_tc_kernel<T, LB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      set_on.fetch_or(bit);
+    }
+    blk_attn_fwd_tc_kernel<T, LB, D><<<grid, 256, smem, st>>>(m);
+  }
 }
 
 template <typename T>
 void attn_fwd_mma(const BlkParams& p, cudaStream_t st) {
   const BlkMmaParams m = blk_mma_params(p);
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.nb);
-  if (p.use_tcgen05 && p.status != nullptr) {
+  if (p.use_tcgen05 && p.status != nullptr && p.ranges != nullptr) {
     TA_PROFILE("blocked_attn_tc", st);
+    const int64_t HB = (int64_t)p.B * p.H;
+    const int64_t nr = HB * (p.P + 1);
+    blk_block_ranges_kernel<<<(unsigned)((nr + 255) / 256), 256, 0, st>>>(p.skeys, p.P, p.nb, HB, p.ranges);
     if (p.D == 64) {
       switch (p.Lb) {
         case 16: launch_attn_fwd_tc<T, 16, 64>(m, grid, st); break;
@@ -1611,6 +1623,7 @@ static BlkWs blk_fwd_ws(const BlkParams& p) {
   w.vals[0] = take(HB * p.P * 4); w.vals[1] = take(HB * p.P * 4);
   w.hist = take(HB * kRadix * tiles * 4);
   w.split = take((size_t)2 * HB * walk_rows_pad(p.R > 0 ? p.R : 1) * p.D * 2);
+  w.ranges = take(HB * (p.nb + 1) * 4);
   w.total = off;
   return w;
 }

@@ -62,67 +62,6 @@ struct BlkTcBwdGeom {
                              COLS_USED <= 512;
 };
 
-// Two 16-column TMEM reads of this thread's lane and their completion wait in one asm
-// statement, so no use of the registers can be scheduled before the wait.
-__device__ __forceinline__ void tc_ld16x2(uint32_t a0, uint32_t a1, float* x, float* y) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(a0), "r"(a1)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    x[i] = __uint_as_float(r[i]);
-    y[i] = __uint_as_float(r[16 + i]);
-  }
-}
-
-// 2^x with the hardware approximation (inputs are <= 0 up to rounding; -inf gives 0)
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Byte offset of 16-byte chunk `c` (columns 8c .. 8c + 7) of row `r` in a 16-bit tile of `rows`
-// rows stored as 128-byte-swizzled atoms: atom column c / 8 (64 columns) at (c / 8) * rows * 128,
-// 8-row group r / 8 at (r / 8) * 1024, and within an atom chunk c % 8 of row r % 8 at
-// (r % 8) * 128 + ((c % 8) ^ (r % 8)) * 16 (the tile base is 1024-byte aligned).
-__device__ __forceinline__ uint32_t sw128_off(int r, int c, int rows) {
-  return (uint32_t)((c >> 3) * (rows * 128) + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
-// Shared-memory descriptor of a 128-byte-swizzled operand (layout type 2).
-__device__ __forceinline__ uint64_t tc_desc_sw(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return tc_desc(saddr, lbo, sbo) | (2ull << 61);
-}
-
-// B fragments of two n8 tiles (n0, n0 + 8), k16, from a [k][n] tile of kTcRows rows in the
-// swizzled layout above: the same rows and columns as frag_b_kn.
-__device__ __forceinline__ void frag_b_kn_sw(uint32_t* r, const unsigned char* base, int n0, int k0, int lane) {
-  ldsm4t(r, base + sw128_off(k0 + ((lane >> 3) & 1) * 8 + (lane & 7), (n0 >> 3) + (lane >> 4), kTcRows));
-}
-
-// First sorted (query, path) pair of every leaf block of every head: out[bh][j] for j in
-// [0, nb], out[bh][nb] = P (one thread per sorted position; each boundary writes the blocks it
-// opens, so empty blocks get their successor's start).
-static __global__ void __launch_bounds__(256) blk_block_ranges_kernel(const uint32_t* skeys, int64_t P, int nb,
-                                                               int64_t HB, uint32_t* out) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= HB * (P + 1)) return;
-  const int64_t bh = i / (P + 1), x = i - bh * (P + 1);
-  const uint32_t* keys = skeys + bh * P;
-  const int64_t prev = x > 0 ? (int64_t)keys[x - 1] : -1;
-  const int64_t cur = x < P ? (int64_t)keys[x] : (int64_t)nb;
-  for (int64_t kk = prev + 1; kk <= cur && kk <= nb; ++kk) out[bh * (nb + 1) + kk] = (uint32_t)x;
-}
-
 template <typename T, int LB, int D>
 __global__ void __launch_bounds__(kTcBwdThreads, 1) blk_attn_bwd_tc_kernel(const BlkMmaParams p) {
   using G = BlkTcBwdGeom<LB, D>;
