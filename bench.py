@@ -71,6 +71,18 @@ def parse_args():
     return p.parse_args()
 
 
+def tensor_peak():
+    """Dense 16-bit tensor peak in TFLOP/s: the measured burst cuBLAS figure (a kernel timed
+    inside a step of a few ms), else the fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured MEASURED_PEAKS.json bf16_tflops (burst)"
+    return 1590.0, "fallback 1.59 PFLOP/s"
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -289,12 +301,26 @@ def record_c3(args, world, rank, dev):
     ms, prof = _timed(step, args.steps, args.warmup, world, dev, profile=True)
     fa2 = None if args.no_fa2 else _fa2_ms((B, S, hl, D), torch.float16, True, args.steps,
                                             args.warmup, world, dev, 0.5)
+    # tensor roofline of the dominant kernel: the five leaf-block products of the backward
+    # (S, dP, dq, dV, dK), 2 * Lb * D flops each per (query, path) pair, as issued (masked keys
+    # included), over its average launch time, against the measured dense 16-bit peak
+    roof = None
+    bk = "blocked_attn_bwd_tc" if "blocked_attn_bwd_tc" in prof else "blocked_attn_bwd_mma"
+    if bk in prof:
+        cnt, tms = prof[bk]
+        flops = 5 * 2 * Lb * D * B * S * hl * P
+        peak, kind = tensor_peak()
+        ach = flops / (tms / cnt / 1e3) / 1e12
+        roof = {"kernel": bk, "bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                "frac": ach / peak, "peak_source": kind, "algorithmic_flops_per_launch": flops,
+                "launch_ms": tms / cnt, "traffic": None}
     rec = {"config": {"workload": "generalised tree (fanout 4, leaf block 128), causal", "batch": B,
                       "seq_len": S, "heads": H, "head_dim": D, "num_samples": P, "fanout": f,
                       "leaf_block": Lb, "dtype": "f16", "data": "N(0, 0.5)",
                       "parallelism": f"head-sharded x{world} ({hl} heads per GPU), no collective"},
            "scaling": "strong", "value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-           "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps)}
+           "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps),
+           "roofline": roof}
     if fa2 is not None:
         rec["fa2"] = {"value": B * S / (fa2 / 1e3), "unit": "tokens/s", "ms_per_step": fa2,
                       "what": "flash_attn_func dense causal fwd+bwd on each rank's head slice"}
