@@ -237,11 +237,18 @@ def _timed(step, steps, warmup, world, dev, profile=False):
     if profile:
         prof = ops.profile_collect()
         ops.profile_enable(False)
+    global _LAST_RANK_MS
+    _LAST_RANK_MS = [ms / steps]
     if world > 1:
-        tm = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        ms = float(tm.item())
+        allm = torch.zeros(world, device=dev, dtype=torch.float64)
+        allm[dist.get_rank()] = ms
+        dist.all_reduce(allm)  # every rank's time (the others contribute zeros)
+        _LAST_RANK_MS = [float(x) / steps for x in allm.tolist()]
+        ms = float(allm.max().item())
     return (ms / steps, prof) if profile else ms / steps
+
+
+_LAST_RANK_MS = None  # per-rank ms per step of the last _timed call
 
 
 def _fa2_ms(shape, dtype, causal, steps, warmup, world, dev, sd=1.0):
@@ -299,6 +306,7 @@ def record_c3(args, world, rank, dev):
                                shard=shard).backward(go)
 
     ms, prof = _timed(step, args.steps, args.warmup, world, dev, profile=True)
+    rank_ms = _LAST_RANK_MS
     fa2 = None if args.no_fa2 else _fa2_ms((B, S, hl, D), torch.float16, True, args.steps,
                                             args.warmup, world, dev, 0.5)
     # tensor roofline of the dominant kernel: the five leaf-block products of the backward
@@ -320,7 +328,7 @@ def record_c3(args, world, rank, dev):
                       "parallelism": f"head-sharded x{world} ({hl} heads per GPU), no collective"},
            "scaling": "strong", "value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
            "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps),
-           "roofline": roof}
+           "roofline": roof, "ms_per_step_by_rank": rank_ms}
     if fa2 is not None:
         rec["fa2"] = {"value": B * S / (fa2 / 1e3), "unit": "tokens/s", "ms_per_step": fa2,
                       "what": "flash_attn_func dense causal fwd+bwd on each rank's head slice"}
@@ -357,12 +365,14 @@ def record_c4(args, world, rank, dev):
         out.backward(go)
 
     ms, prof = _timed(step, args.steps, args.warmup, world, dev, profile=True)
+    rank_ms = _LAST_RANK_MS
     rec = {"config": {"workload": "stochastic tree attention, causal (exact prefix + corrected "
                                   "sampler)", "batch": B, "seq_len": S, "heads": H, "head_dim": D,
                       "num_samples": P, "dtype": "bf16",
                       "parallelism": f"sequence-parallel x{world}: NCCL all-gather of K/V, "
                                      "reduce-scatter of dK/dV" if world > 1 else "one GPU"},
            "scaling": "strong", "value": B * S / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "ms_per_step_by_rank": rank_ms,
            "gpu_launches": int(sum(c for c, _ in prof.values())), "kernels": _kernels(prof, args.steps)}
     if world == 1 and not args.no_fa2:
         fa2 = _fa2_ms((B, S, H, D), torch.bfloat16, True, 2, 1, world, dev)
