@@ -965,12 +965,18 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
 // (written per path for the summary gradients); per (query, level) thread: the query's
 // coefficient row DZ (paths summed in order); then dq_tree = DZ C on the tensor cores with
 // both operands split into high and low parts.
+// The Q and dO tiles are dead once delta is formed, so they share one region with the per-path
+// delta and dz: delta overlaps the Q tile only (Q is last read by the score product, while the
+// delta pass still reads dO), dz follows it.
+__host__ __device__ inline size_t bwd_walk_union(int D, int S, int DF) {
+  const size_t tiles = (size_t)2 * kWalkQ * (D + 8) * 2;
+  const size_t paths = (size_t)kWalkQ * S * 4 + (size_t)kWalkQ * S * DF * 4;
+  return tiles > paths ? tiles : paths;
+}
 __host__ __device__ inline size_t bwd_walk_smem(int64_t R, int D, int S, int DF) {
   return (size_t)kWalkQ * (walk_rows_pad(R) + 4) * 4    // Z table, then DZ
          + (size_t)2 * kWalkChunk * (D + 8) * 2          // C chunk high / low
-         + (size_t)2 * kWalkQ * (D + 8) * 2              // Q and dO tiles
-         + (size_t)kWalkQ * S * 4                        // delta, then dlp
-         + (size_t)kWalkQ * S * DF * 4;                  // dz per path
+         + bwd_walk_union(D, S, DF);                     // Q, dO tiles | delta, dz per path
 }
 
 template <typename T, int D, int F>
@@ -985,7 +991,7 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
   uint16_t* s_clo = s_chi + kWalkChunk * LD;
   uint16_t* s_q = s_clo + kWalkChunk * LD;                            // [kWalkQ][LD]
   uint16_t* s_g = s_q + kWalkQ * LD;                                  // [kWalkQ][LD]
-  float* s_dl = reinterpret_cast<float*>(s_g + kWalkQ * LD);          // [kWalkQ][S]
+  float* s_dl = reinterpret_cast<float*>(s_q);                        // [kWalkQ][S] (over Q)
   float* s_dzp = s_dl + kWalkQ * p.S;                                 // [kWalkQ][S][DF]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lt = (p.L + kWalkQ - 1) / kWalkQ;
