@@ -732,6 +732,9 @@ __global__ void __launch_bounds__(256) blk_bwd_key_kernel(const BlkParams p) {
 constexpr int kWalkQ = 32;         // queries per CTA
 constexpr int kWalkChunk = 128;    // summary rows per product chunk
 constexpr int kWalkMaxRows = 1024; // summary rows the table holds (levels 1..Dp)
+constexpr int kWalkRep = 4;         // consecutive query tiles of one head per sampler CTA
+constexpr int kBwdWalkRep = 1;      // ... per backward-walk CTA (more tiles per CTA measured slower
+                                    // at config 3: 3.39 -> 3.53 ms)
 
 __host__ __device__ inline int walk_rows_pad(int64_t R) { return (int)((R + kWalkChunk - 1) / kWalkChunk) * kWalkChunk; }
 __host__ __device__ inline size_t walk_smem(int64_t R, int D, int S) {
@@ -836,13 +839,15 @@ __global__ void __launch_bounds__(256) blk_split_summaries_kernel(const BlkParam
 // Waits for the caller's pending cp.async copies (the query rows).
 template <typename T, int D>
 __device__ __forceinline__ void walk_scores(const BlkParams& p, int bh, const uint16_t* s_q,
-                                            uint16_t* s_chi, uint16_t* s_clo, float* s_z, int RP, int ZS) {
+                                            uint16_t* s_chi, uint16_t* s_clo, float* s_z, int RP, int ZS,
+                                            bool staged = false) {
   constexpr int LD = D + 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int m0 = (warp & 1) * 16, nb0 = (warp >> 1) * 32;  // warp: 16 queries x 32 rows of a chunk
   for (int r0 = 0; r0 < RP; r0 += kWalkChunk) {
     __syncthreads();  // the previous chunk's readers are done
-    walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
+    // (a single chunk staged for an earlier query tile of the same head is still in place)
+    if (!(staged && RP == kWalkChunk)) walk_load_chunk<T, D>(p, bh, r0, s_chi, s_clo);
     cp_async_wait_0();
     __syncthreads();
     float acc[4][4];
@@ -886,10 +891,15 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
   float* s_lp = reinterpret_cast<float*>(s_q + kWalkQ * LD);          // [kWalkQ][S]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lt = (p.L + kWalkQ - 1) / kWalkQ;
-  const int bh = blockIdx.x / lt;
-  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
+  const int ltr = (lt + kWalkRep - 1) / kWalkRep;  // CTAs per head
+  const int bh = blockIdx.x / ltr;
+  const int tile0 = (blockIdx.x - bh * ltr) * kWalkRep;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
   constexpr int CPR = D * 2 / 16;
+  // consecutive query tiles of the head, the summary table staged once
+  for (int rep = 0; rep < kWalkRep && tile0 + rep < lt; ++rep) {
+  const int l0 = (tile0 + rep) * kWalkQ;
+  if (rep > 0) __syncthreads();  // the previous tile's readers are done
   for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
     const int r = i / CPR, c = i - r * CPR;
     if (l0 + r < p.L)
@@ -898,7 +908,7 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
       *reinterpret_cast<uint4*>(s_q + r * LD + c * 8) = make_uint4(0, 0, 0, 0);
   }
   cp_async_commit();
-  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS);
+  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS, rep > 0);
   __syncthreads();
   // one thread per (query, path): the walk reads its children's logits from the table
   for (int i = tid; i < kWalkQ * p.S; i += blockDim.x) {
@@ -957,6 +967,7 @@ __global__ void __launch_bounds__(256) blk_walk_mma_kernel(const BlkParams p) {
     const int64_t o = (((int64_t)l * p.B + b) * p.H + h) * p.S;
     for (int s = 0; s < p.S; ++s) p.weights[o + s] = expf(s_lp[qi * p.S + s] - m) * inv;
   }
+  }  // query tiles
 }
 
 // Backward of the tree levels as table lookups (tensor-core path), per 32 queries of a head:
@@ -995,10 +1006,15 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
   float* s_dzp = s_dl + kWalkQ * p.S;                                 // [kWalkQ][S][DF]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lt = (p.L + kWalkQ - 1) / kWalkQ;
-  const int bh = blockIdx.x / lt;
-  const int l0 = (blockIdx.x - bh * lt) * kWalkQ;
+  const int ltr = (lt + kBwdWalkRep - 1) / kBwdWalkRep;  // CTAs per head
+  const int bh = blockIdx.x / ltr;
+  const int tile0 = (blockIdx.x - bh * ltr) * kBwdWalkRep;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
   constexpr int CPR = D * 2 / 16;
+  // consecutive query tiles of the head, the summary table staged once
+  for (int rep = 0; rep < kBwdWalkRep && tile0 + rep < lt; ++rep) {
+  const int l0 = (tile0 + rep) * kWalkQ;
+  if (rep > 0) __syncthreads();  // the previous tile's readers are done
   for (int i = tid; i < kWalkQ * CPR; i += blockDim.x) {
     const int r = i / CPR, c = i - r * CPR;
     if (l0 + r < p.L) {
@@ -1011,7 +1027,7 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
     }
   }
   cp_async_commit();
-  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS);
+  walk_scores<T, D>(p, bh, s_q, s_chi, s_clo, s_z, RP, ZS, rep > 0);
   __syncthreads();
   // delta_s = dO_q . (w_s o_s)
   for (int i = tid; i < kWalkQ * p.S; i += blockDim.x) {
@@ -1171,6 +1187,7 @@ __global__ void __launch_bounds__(256) blk_bwd_walk_mma_kernel(const BlkParams p
     for (int t = 0; t < NTW; ++t)
       *reinterpret_cast<float2*>(dst + t * 8 + tq * 2) = make_float2(acc[t][2 * u], acc[t][2 * u + 1]);
   }
+  }  // query tiles
 }
 
 // out[l,b,h] = sum_s path_out[b*H+h][l*S+s] in path order (tensor-core forward); with
@@ -1494,7 +1511,7 @@ int blk_fwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
             const int64_t ns = (int64_t)p.B * p.H * walk_rows_pad(p.R) * D / 2;
             blk_split_summaries_kernel<T><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(p);
           }
-          const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
+          const unsigned wg = (unsigned)(((p.L + kWalkQ * kWalkRep - 1) / (kWalkQ * kWalkRep)) * (int64_t)p.B * p.H);
           blk_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
         } else {
           launch();
@@ -1536,7 +1553,7 @@ int blk_bwd_typed(BlkParams& p, BwdParams& sp, cudaStream_t st) {
           const int64_t ns = (int64_t)p.B * p.H * walk_rows_pad(p.R) * D / 2;
           blk_split_summaries_kernel<T><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(p);
         }
-        const unsigned wg = (unsigned)(((p.L + kWalkQ - 1) / kWalkQ) * (int64_t)p.B * p.H);
+        const unsigned wg = (unsigned)(((p.L + kWalkQ * kBwdWalkRep - 1) / (kWalkQ * kBwdWalkRep)) * (int64_t)p.B * p.H);
         blk_bwd_walk_mma_kernel<T, D, F><<<wg, 256, wsm, st>>>(p);
         done = true;
       }
