@@ -170,6 +170,34 @@ static BwdLayout bwd_layout(const ta_shape* s) {
 }
 
 
+bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join) {
+  struct Handles {
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+  };
+  constexpr int kMaxDevices = 64;
+  thread_local Handles h[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return false;
+  }
+  Handles& x = h[dev];
+  if (x.side == nullptr) {
+    if (cudaStreamCreateWithFlags(&x.side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      x = Handles{};
+      return false;
+    }
+  }
+  side = x.side;
+  fork = x.fork;
+  join = x.join;
+  return true;
+}
+
 int run_sort(BwdParams& p, cudaStream_t st) {
   const int passes = (p.log_n + kRadixBits - 1) / kRadixBits;
   const unsigned tiles = (unsigned)(p.B * p.H * p.tiles_per_seg);

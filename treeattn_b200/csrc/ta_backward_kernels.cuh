@@ -64,6 +64,7 @@ struct BwdParams {
   int32_t top_levels;  // tree levels staged in shared memory by the query pass
   int32_t chunk;       // sorted paths per node-pass chunk
   int32_t coef_mode;   // sig holds final per-level coefficients, dlp holds value weights
+  int32_t records_apart;  // the sort records were written by sort_records_kernel (not the query pass)
   int32_t dv_f32;      // dv written as float32 (else input dtype)
   int32_t node_range_chunks;  // tensor-core node pass: chunks per CTA range (0 = from the shape)
   int32_t qtable_levels;      // query pass: top levels reduced on the tensor cores (0 = none)
@@ -226,8 +227,10 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_query_kernel(const BwdPara
       s_dlp[s] = d;
       p.dlp[path0 + s] = d;
       // sort record of path s: (path bits, path id within its head)
-      p.keys[0][path0 + s] = (uint32_t)p.leaf[j0 + s] + K - base_node;
-      p.vals[0][path0 + s] = (uint32_t)(l * p.S + s);
+      if (!p.records_apart) {
+        p.keys[0][path0 + s] = (uint32_t)p.leaf[j0 + s] + K - base_node;
+        p.vals[0][path0 + s] = (uint32_t)(l * p.S + s);
+      }
     }
   }
   __syncwarp(gmask);
@@ -963,8 +966,8 @@ void launch_node_el(const BwdParams& p, cudaStream_t st, unsigned grid) {
 }
 
 template <typename T>
-int run_rest(BwdParams& p, cudaStream_t st) {
-  int rc = run_sort(p, st);
+int run_rest(BwdParams& p, cudaStream_t st, bool sorted = false) {
+  int rc = sorted ? TA_OK : run_sort(p, st);
   if (rc) return rc;
   if constexpr (sizeof(T) == 2) {
     if (p.chunk == kChunkMma) {
@@ -1019,10 +1022,48 @@ int run_rest(BwdParams& p, cudaStream_t st) {
 }
 
 // the typed half of ta_backward: query pass, then sort + node pass + fix-up
+// The sort records of every path from the forward's leaves alone: (path bits, path id within
+// its head), the same values the query pass writes. One thread per path.
+static __global__ void __launch_bounds__(256) sort_records_kernel(const BwdParams p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // head-major path index
+  const int64_t total = (int64_t)p.B * p.H * p.P;
+  if (i >= total) return;
+  const int64_t hb = i / p.P, pl = i - hb * p.P;
+  const int64_t l = pl / p.S, s = pl - l * p.S;
+  const int b = (int)(hb / p.H), h = (int)(hb - (hb / p.H) * p.H);
+  const uint32_t K = (uint32_t)p.N - 1u, base_node = (1u << p.log_n) - 1u;
+  p.keys[0][i] = (uint32_t)p.leaf[((l * p.B + b) * p.H + h) * p.S + s] + K - base_node;
+  p.vals[0][i] = (uint32_t)pl;
+}
+
+// A side stream and two events for the calling host thread on the current device (created on
+// first use; thread-local, so concurrent callers never share an event).
+bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join);
+
 template <typename T>
 int run_backward_typed(BwdParams& p, cudaStream_t st) {
-  int rc = run_query<T>(p, st);
-  if (rc) return rc;
+  // The sort of the paths by leaf needs only the forward's leaves, not the query pass: it runs
+  // on a side stream beside the query pass, and the node pass waits for both.
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  const bool apart = !p.coef_mode && backward_fork_handles(side, fork, join);
+  int rc;
+  if (apart) {
+    p.records_apart = 1;
+    cudaEventRecord(fork, st);
+    cudaStreamWaitEvent(side, fork, 0);
+    {
+      TA_PROFILE("sort_records", side);
+      const int64_t total = (int64_t)p.B * p.H * p.P;
+      sort_records_kernel<<<(unsigned)((total + 255) / 256), 256, 0, side>>>(p);
+    }
+    if ((rc = run_sort(p, side))) return rc;
+    cudaEventRecord(join, side);
+    if ((rc = run_query<T>(p, st))) return rc;
+    cudaStreamWaitEvent(st, join, 0);
+    return run_rest<T>(p, st, /*sorted=*/true);
+  }
+  if ((rc = run_query<T>(p, st))) return rc;
   return run_rest<T>(p, st);
 }
 
