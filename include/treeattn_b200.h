@@ -230,6 +230,10 @@ int32_t ta_branch_prob_stride(int64_t num_leaves);
  * shape->dtype; dk in `dk_dtype` and dv in `dv_dtype` (each TA_F32 for a float32 buffer, e.g.
  * partial gradients that are reduced across ranks afterwards, or shape->dtype). No float atomics: dK/dV are reduced by sorting paths by leaf and summing
  * each node's contributions in a fixed order, so results are bitwise repeatable.
+ * The sort of the paths by leaf needs only `leaf`, so it runs on an internal side stream of the
+ * calling thread (created on its first call on a device) beside the query pass; `stream` waits
+ * for it through an event before the node pass, so all the call's work is ordered before
+ * anything enqueued on `stream` afterwards, and the call never blocks the host.
  * Replaces _StochasticNonCausalTreeAttention.backward (_autograd.py:707-860):
  * prepare_non_causal_backward, scatter_weighted_grad_v_forward and
  * accumulate_qk_non_causal_all_depths_prepared_inplace (treeattn_cuda.cpp:479-488).
