@@ -64,6 +64,7 @@ def run_ranks(R, fn):
     (512, 2, 8, 2, 64, True, torch.float32),
     (1024, 4, 16, 2, 64, True, torch.bfloat16),
     (1024, 4, 16, 4, 64, True, torch.bfloat16),  # H % R == 0: exact prefix split by heads
+    (512, 8, 16, 8, 64, True, torch.bfloat16),   # eight ranks, prefix split by heads
     (64, 8, 16, 2, 32, True, torch.float32),    # chunk 8 < S: exact prefix spans two ranks
 ])
 def test_sp_equals_unsharded(N, R, S, H, D, causal, dtype):
