@@ -170,7 +170,8 @@ static BwdLayout bwd_layout(const ta_shape* s) {
 }
 
 
-bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join) {
+bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join,
+                           cudaStream_t st) {
   struct Handles {
     cudaStream_t side = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
@@ -179,6 +180,11 @@ bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& j
   thread_local Handles h[kMaxDevices];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return false;
+  }
+  int sdev = dev;  // fork only when the caller's stream is on the current device
+  if (cudaStreamGetDevice(st, &sdev) != cudaSuccess || sdev != dev) {
     cudaGetLastError();
     return false;
   }

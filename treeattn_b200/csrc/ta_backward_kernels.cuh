@@ -1037,8 +1037,10 @@ static __global__ void __launch_bounds__(256) sort_records_kernel(const BwdParam
 }
 
 // A side stream and two events for the calling host thread on the current device (created on
-// first use; thread-local, so concurrent callers never share an event).
-bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join);
+// first use; thread-local, so concurrent callers never share an event); false when `st` is on
+// another device or a handle cannot be created (the caller then stays on one stream).
+bool backward_fork_handles(cudaStream_t& side, cudaEvent_t& fork, cudaEvent_t& join,
+                           cudaStream_t st);
 
 template <typename T>
 int run_backward_typed(BwdParams& p, cudaStream_t st) {
@@ -1046,7 +1048,7 @@ int run_backward_typed(BwdParams& p, cudaStream_t st) {
   // on a side stream beside the query pass, and the node pass waits for both.
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
-  const bool apart = !p.coef_mode && backward_fork_handles(side, fork, join);
+  const bool apart = !p.coef_mode && backward_fork_handles(side, fork, join, st);
   int rc;
   if (apart) {
     p.records_apart = 1;
